@@ -1,0 +1,194 @@
+/*
+ * pdx_moe.h -- C ABI of the B200 (sm_100a) MoE expert-execution library.
+ *
+ * One shared library, libpdx_moe.so, implements the per-layer MoE expert path
+ * of PDScope (nezha-Anonymous/PDScope): top-k gate softmax with
+ * renormalisation, ragged token->expert packing, the grouped SwiGLU expert FFN
+ * and the fused weighted combine.  Each entry point below names the reference
+ * interface it replaces (paths inside the reference project).
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor arguments are caller-owned DEVICE pointers (BF16 passed as
+ *     void*, raw IEEE bfloat16 bits), dense row-major, on the current device.
+ *   - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default
+ *     stream) and never synchronises the host, except pdx_device_error.
+ *   - Nothing allocates device memory.  Scratch comes from a caller-provided
+ *     workspace whose minimum size the matching *_workspace_bytes query
+ *     returns; it must be 256-byte aligned.
+ *   - The return value is a pdx_status; on failure pdx_last_error() returns a
+ *     thread-local message.  PDX_ERR_INVALID corresponds to the reference's
+ *     ValueError (contract violations), the others to RuntimeError.
+ */
+#ifndef PDX_MOE_H
+#define PDX_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *pdx_stream_t; /* identical to cudaStream_t */
+
+typedef enum pdx_status {
+    PDX_OK = 0,
+    PDX_ERR_INVALID = 1,     /* bad shape/argument: reference raises ValueError */
+    PDX_ERR_UNSUPPORTED = 2, /* valid, but outside the shapes these kernels cover */
+    PDX_ERR_WORKSPACE = 3,   /* workspace NULL, misaligned or too small */
+    PDX_ERR_CUDA = 4,        /* a CUDA runtime call failed */
+    PDX_ERR_DEVICE = 5       /* a kernel raised the device error word */
+} pdx_status;
+
+/* Device error codes (read back by pdx_device_error). */
+#define PDX_DEVERR_NONE 0u
+#define PDX_DEVERR_WAIT_TIMEOUT 1u  /* a bounded mbarrier wait expired */
+#define PDX_DEVERR_BAD_EXPERT 2u    /* routed expert id outside [0, E) */
+#define PDX_DEVERR_BAD_SLOT 3u      /* slot_of_expert[e] outside [0, num_slots) */
+
+/* Thread-local description of the last failure ("" after success). */
+const char *pdx_last_error(void);
+
+/* ABI version of this header (bumped on any signature change). */
+#define PDX_ABI_VERSION 1
+int pdx_abi_version(void);
+
+/*
+ * Expert weight placement.  Expert e lives in slot s = slot_of_expert[e]
+ * (identity when slot_of_expert is NULL); its three projections are
+ *   gate = (bf16*)gate + s*gate_stride  [I, H]   (gate_proj.weight)
+ *   up   = (bf16*)up   + s*up_stride    [I, H]   (up_proj.weight)
+ *   down = (bf16*)down + s*down_stride  [H, I]   (down_proj.weight)
+ * Strides are in elements.  The reference's ExpertExecutor cache slab
+ * (expertbench/executor.py:219-227, 323-331: equal slots holding gate|up|down
+ * back to back) is described without copying by gate = slab,
+ * up = slab + I*H, down = slab + 2*I*H and all strides = 3*I*H.
+ * gate_stride must be a multiple of H and down_stride a multiple of I.
+ */
+typedef struct pdx_expert_weights {
+    const void *gate;
+    const void *up;
+    const void *down;
+    int64_t gate_stride;
+    int64_t up_stride;
+    int64_t down_stride;
+    int64_t num_slots;
+    const int32_t *slot_of_expert; /* device int32[E] or NULL */
+} pdx_expert_weights;
+
+/* ---------------------------------------------------------------------------
+ * a1. Routing.  Replaces route() -- expertbench/adapters/qwen.py:140-152:
+ *   logits = F.linear(x, gate)                       (BF16, [T,E])
+ *   p = softmax(logits.float()); w, ids = topk(p, k) (desc, ties: lower id)
+ *   if normalize: w /= w.sum(-1);  weights = w.to(bf16)
+ * Logits are the exact dot products rounded once to BF16 (FP64 accumulation).
+ * logits_out may be NULL (then the workspace holds them).
+ */
+size_t pdx_route_workspace_bytes(int64_t T, int64_t E);
+int pdx_route_topk(const void *x, const void *gate, int64_t T, int64_t H, int64_t E,
+                   int32_t top_k, int32_t normalize, void *logits_out,
+                   int64_t *selected_out, void *weights_out, void *workspace,
+                   size_t workspace_bytes, pdx_stream_t stream);
+
+/* Softmax + top-k + renormalisation of given BF16 logits [T,E]
+ * (qwen.py:148-152 alone). */
+int pdx_topk_from_logits(const void *logits, int64_t T, int64_t E, int32_t top_k,
+                         int32_t normalize, int64_t *selected_out, void *weights_out,
+                         pdx_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * a2/a3. Packing.  Replaces compact_expert_groups() --
+ * expertbench/pdscope_runtime.py:16-39 (and expert_groups(), qwen.py:155-174,
+ * which yields the same order).  Stable counting sort of the T*k assignments
+ * taken in slot-major order (flat index f = s*T + t):
+ *   counts[E]       assignments per expert            (bincount, :26)
+ *   offsets[E+1]    exclusive prefix of counts
+ *   tokens[T*k]     packed row p -> token t           (order % T, :29)
+ *   positions[T*k]  packed row p -> t*k + s           (:29)
+ *   packed_w[T*k]   BF16 weights in packed order      (:31)
+ *   inverse[T*k]    t*k + s -> packed row p
+ *   active[E+1]     active[0] = #experts with count>0, active[1..] = their ids
+ *                   ascending
+ * Ids outside [0,E) set PDX_DEVERR_BAD_EXPERT (reference: ValueError, :27).
+ */
+size_t pdx_pack_workspace_bytes(int64_t T, int32_t top_k, int64_t E);
+int pdx_pack(const int64_t *selected, const void *weights, int64_t T, int32_t top_k,
+             int64_t E, int32_t *counts, int32_t *offsets, int32_t *tokens,
+             int32_t *positions, void *packed_w, int32_t *inverse, int32_t *active,
+             void *workspace, size_t workspace_bytes, pdx_stream_t stream);
+
+/* a4. Row gather x[tokens[p]] -> out[p]  (inputs[flat_tokens],
+ * pdscope_runtime.py:333-336). */
+int pdx_gather_rows(const void *x, const int32_t *tokens, int64_t rows, int64_t H,
+                    void *out, pdx_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * a5. Grouped expert FFN.  Replaces the per-expert ExpertExecutor.gpu ->
+ * expert_forward loop (expertbench/executor.py:454-488, qwen.py:87-90):
+ *   y[p] = F.linear(silu(F.linear(x[tok], Wg)) * F.linear(x[tok], Wu), Wd)
+ * for every packed row p of every active expert, UNWEIGHTED, in packed order,
+ * with the reference's BF16 roundings (after each linear, after silu, after
+ * the product).  `x` is the [T,H] token matrix; rows are gathered through
+ * `tokens`.  mode: 0 = auto, 1 = streaming GEMV (decode), 2 = tcgen05
+ * grouped GEMM (prefill).
+ */
+#define PDX_FFN_AUTO 0
+#define PDX_FFN_GEMV 1
+#define PDX_FFN_GEMM 2
+size_t pdx_ffn_workspace_bytes(int64_t rows, int64_t H, int64_t I, int32_t mode);
+int pdx_moe_ffn_grouped(const void *x, int64_t T, const int32_t *tokens,
+                        const int32_t *offsets, const int32_t *active, int64_t E,
+                        int64_t rows, const pdx_expert_weights *weights, int64_t H,
+                        int64_t I, void *y_out, int32_t mode, void *workspace,
+                        size_t workspace_bytes, pdx_stream_t stream);
+
+/* Single expert, the ExpertExecutor.gpu_backend plug-in
+ * (expertbench/executor.py:178, 476-477): y[n,H] = expert_forward(x[n,H]). */
+size_t pdx_expert_ffn_workspace_bytes(int64_t n, int64_t H, int64_t I);
+int pdx_expert_ffn(const void *x, int64_t n, const void *gate, const void *up,
+                   const void *down, int64_t H, int64_t I, void *y_out, void *workspace,
+                   size_t workspace_bytes, pdx_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * a7. Combine.  Replaces the fused merge
+ *   output.index_add_(0, index, rows.to(bf16) * weight)
+ * (expertbench/pdscope_runtime.py:454-464; native finish_and_merge,
+ * native/native_layer_dispatch.cpp:73-90).  Deterministic gather form:
+ *   out[t] = bf16( residual[t] + sum_s bf16(y[inverse[t*k+s]] * w[t*k+s]) )
+ * accumulated in FP32 over s = 0..k-1.  residual may be NULL (zeros, as the
+ * reference's torch.zeros_like output); `weights` is the [T,k] routing weight
+ * matrix.
+ */
+int pdx_combine(const void *y, const void *weights, const int32_t *inverse, int64_t T,
+                int32_t top_k, int64_t H, const void *residual, void *out,
+                pdx_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Whole layer: route -> pack -> grouped FFN -> combine, all on `stream`, no
+ * host synchronisation (PDScopeCudaRuntime.forward's GPU work,
+ * expertbench/pdscope_runtime.py:208-512, with every expert resident).
+ * Optional outputs (NULL = kept in the workspace): logits [T,E] BF16,
+ * selected [T,k] int64, weights [T,k] BF16, counts [E] int32.
+ */
+size_t pdx_layer_workspace_bytes(int64_t T, int64_t H, int64_t E, int32_t top_k,
+                                 int64_t I, int32_t mode);
+int pdx_moe_layer(const void *x, const void *gate, int64_t T, int64_t H, int64_t E,
+                  int32_t top_k, int32_t normalize, const pdx_expert_weights *weights,
+                  int64_t I, const void *residual, void *out, void *logits_out,
+                  int64_t *selected_out, void *weights_out, int32_t *counts_out,
+                  int32_t mode, void *workspace, size_t workspace_bytes,
+                  pdx_stream_t stream);
+
+/* Synchronise `stream`, then read and clear this device's error word.
+ * *code_out receives a PDX_DEVERR_* value; returns PDX_ERR_DEVICE if nonzero. */
+int pdx_device_error(pdx_stream_t stream, uint32_t *code_out);
+
+/* Number of kernels this library has launched in this process (all devices);
+ * used by benchmarks to report their own launch count. */
+uint64_t pdx_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PDX_MOE_H */

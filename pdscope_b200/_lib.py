@@ -1,0 +1,118 @@
+"""ctypes binding of libpdx_moe.so (the C ABI in include/pdx_moe.h).
+
+The shared library is the only compute path: if it is missing or cannot be
+loaded this module raises at import time; there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = Path(os.environ.get("PDX_MOE_LIB", _PKG / "libpdx_moe.so"))
+
+PDX_OK = 0
+PDX_ERR_INVALID = 1
+PDX_ERR_UNSUPPORTED = 2
+PDX_ERR_WORKSPACE = 3
+PDX_ERR_CUDA = 4
+PDX_ERR_DEVICE = 5
+
+PDX_DEVERR_NONE = 0
+PDX_DEVERR_WAIT_TIMEOUT = 1
+PDX_DEVERR_BAD_EXPERT = 2
+PDX_DEVERR_BAD_SLOT = 3
+
+FFN_AUTO, FFN_GEMV, FFN_GEMM = 0, 1, 2
+
+ABI_VERSION = 1
+
+c_i64 = ctypes.c_int64
+c_i32 = ctypes.c_int32
+c_vp = ctypes.c_void_p
+c_sz = ctypes.c_size_t
+
+
+class ExpertWeights(ctypes.Structure):
+    """struct pdx_expert_weights."""
+    _fields_ = [("gate", c_vp), ("up", c_vp), ("down", c_vp),
+                ("gate_stride", c_i64), ("up_stride", c_i64), ("down_stride", c_i64),
+                ("num_slots", c_i64), ("slot_of_expert", c_vp)]
+
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "pdx_last_error": (ctypes.c_char_p, []),
+    "pdx_abi_version": (ctypes.c_int, []),
+    "pdx_launch_count": (ctypes.c_uint64, []),
+    "pdx_route_workspace_bytes": (c_sz, [c_i64, c_i64]),
+    "pdx_route_topk": (ctypes.c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp,
+                                      c_vp, c_sz, c_vp]),
+    "pdx_topk_from_logits": (ctypes.c_int, [c_vp, c_i64, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp]),
+    "pdx_pack_workspace_bytes": (c_sz, [c_i64, c_i32, c_i64]),
+    "pdx_pack": (ctypes.c_int, [c_vp, c_vp, c_i64, c_i32, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                c_vp, c_sz, c_vp]),
+    "pdx_gather_rows": (ctypes.c_int, [c_vp, c_vp, c_i64, c_i64, c_vp, c_vp]),
+    "pdx_ffn_workspace_bytes": (c_sz, [c_i64, c_i64, c_i64, c_i32]),
+    "pdx_moe_ffn_grouped": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64,
+                                           ctypes.POINTER(ExpertWeights), c_i64, c_i64, c_vp, c_i32, c_vp,
+                                           c_sz, c_vp]),
+    "pdx_expert_ffn_workspace_bytes": (c_sz, [c_i64, c_i64, c_i64]),
+    "pdx_expert_ffn": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_sz, c_vp]),
+    "pdx_combine": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, c_i32, c_i64, c_vp, c_vp, c_vp]),
+    "pdx_layer_workspace_bytes": (c_sz, [c_i64, c_i64, c_i64, c_i32, c_i64, c_i32]),
+    "pdx_moe_layer": (ctypes.c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_i32,
+                                     ctypes.POINTER(ExpertWeights), c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                     c_i32, c_vp, c_sz, c_vp]),
+    "pdx_device_error": (ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_uint32)]),
+}
+
+
+class PdxError(RuntimeError):
+    """A CUDA or device-side failure reported by libpdx_moe."""
+
+
+def _load():
+    if not LIB_PATH.exists():
+        raise ImportError(f"libpdx_moe.so not found at {LIB_PATH}; build it with "
+                          "`python -m pdscope_b200.build` (the CUDA path has no fallback)")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if lib.pdx_abi_version() != ABI_VERSION:
+        raise ImportError("libpdx_moe.so ABI version mismatch; rebuild it")
+    return lib
+
+
+lib = _load()
+
+
+def last_error() -> str:
+    msg = lib.pdx_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(status: int) -> None:
+    """Map a pdx_status to the reference's exception types."""
+    if status == PDX_OK:
+        return
+    msg = last_error()
+    if status == PDX_ERR_INVALID:
+        raise ValueError(msg)
+    if status == PDX_ERR_UNSUPPORTED:
+        raise ValueError("unsupported by the sm_100a kernels: " + msg)
+    if status == PDX_ERR_WORKSPACE:
+        raise RuntimeError("workspace: " + msg)
+    raise PdxError(msg)
+
+
+def device_error(stream_handle) -> int:
+    """Synchronise the stream, then read and clear the device error word."""
+    code = ctypes.c_uint32(0)
+    status = lib.pdx_device_error(stream_handle, ctypes.byref(code))
+    if status not in (PDX_OK, PDX_ERR_DEVICE):
+        check(status)
+    return int(code.value)

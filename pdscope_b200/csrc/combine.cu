@@ -1,0 +1,86 @@
+// Combine and row-gather kernels.
+//
+// Combine replaces the fused merge of expertbench/pdscope_runtime.py:454-464
+//   output.index_add_(0, index, rows.to(bf16) * weight)
+// (and the native finish_and_merge scatter, native/native_layer_dispatch.cpp:88)
+// with a deterministic gather: every output row is owned by one CTA, which
+// reads its k expert rows through the inverse permutation, forms the BF16
+// product y*w exactly as the reference does, accumulates in FP32 in slot
+// order and rounds once.  No atomics, so results do not depend on scheduling.
+#include "pdx_common.cuh"
+
+namespace pdx {
+
+constexpr int kCombineThreads = 256;
+
+__device__ __forceinline__ void unpack8(const uint4& v, float* f) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        f[2 * i] = __uint_as_float(w[i] << 16);
+        f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+}
+
+__device__ __forceinline__ uint4 pack8(const float* f) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        w[i] = static_cast<uint32_t>(f2bits(f[2 * i])) | (static_cast<uint32_t>(f2bits(f[2 * i + 1])) << 16);
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// out[t] = bf16( residual[t] + sum_{s<k} bf16(y[inverse[t*k+s]] * w[t*k+s]) )
+__global__ void __launch_bounds__(kCombineThreads) k_combine(const uint16_t* __restrict__ y,
+                                                             const uint16_t* __restrict__ weights,
+                                                             const int32_t* __restrict__ inverse, int T, int k,
+                                                             int H, const uint16_t* __restrict__ residual,
+                                                             uint16_t* __restrict__ out) {
+    const int t = static_cast<int>(blockIdx.x);
+    if (t >= T) return;
+    __shared__ int s_row[32];
+    __shared__ float s_w[32];
+    if (threadIdx.x < static_cast<unsigned>(k)) {
+        int row = inverse[static_cast<size_t>(t) * k + threadIdx.x];
+        float w = bits2f(weights[static_cast<size_t>(t) * k + threadIdx.x]);
+        if (row < 0 || row >= T * k) {  // not a permutation of [0, T*k): flag, contribute nothing
+            raise_error(PDX_DEVERR_BAD_EXPERT);
+            row = 0;
+            w = 0.f;
+        }
+        s_row[threadIdx.x] = row;
+        s_w[threadIdx.x] = w;
+    }
+    __syncthreads();
+    for (int c = static_cast<int>(threadIdx.x) * 8; c < H; c += blockDim.x * 8) {
+        float acc[8];
+        if (residual) {
+            unpack8(*reinterpret_cast<const uint4*>(residual + static_cast<size_t>(t) * H + c), acc);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        }
+        for (int s = 0; s < k; ++s) {
+            float v[8];
+            unpack8(__ldg(reinterpret_cast<const uint4*>(y + static_cast<size_t>(s_row[s]) * H + c)), v);
+            const float w = s_w[s];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] += round_bf16(v[i] * w);
+        }
+        *reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H + c) = pack8(acc);
+    }
+}
+
+// out[p] = x[tokens[p]]  (inputs[flat_tokens], pdscope_runtime.py:333-336)
+__global__ void __launch_bounds__(kCombineThreads) k_gather_rows(const uint16_t* __restrict__ x,
+                                                                 const int32_t* __restrict__ tokens, int rows,
+                                                                 int H, uint16_t* __restrict__ out) {
+    const int p = static_cast<int>(blockIdx.x);
+    if (p >= rows) return;
+    const size_t src = static_cast<size_t>(tokens[p]) * H;
+    for (int c = static_cast<int>(threadIdx.x) * 8; c < H; c += blockDim.x * 8)
+        *reinterpret_cast<uint4*>(out + static_cast<size_t>(p) * H + c) =
+            __ldg(reinterpret_cast<const uint4*>(x + src + c));
+}
+
+}  // namespace pdx

@@ -1,0 +1,354 @@
+// Prefill-path grouped expert FFN: tcgen05 / TMEM grouped GEMM fed by TMA.
+//
+// Reference: expert_forward() -- expertbench/adapters/qwen.py:87-90, applied
+// per expert to the rows routed to it (ExpertExecutor.gpu,
+// expertbench/executor.py:454-488, on the compact grouping of
+// expertbench/pdscope_runtime.py:16-39).
+//
+// One persistent CTA per SM walks a static schedule of output tiles over the
+// ragged expert segments (tile = 128 packed rows x N columns of one expert).
+//   warp 0      TMA producer: A tile [128 x 64] + B tile [256 x 64] per stage
+//   warp 1      MMA issuer: tcgen05.mma.cta_group::1.kind::f16, M=128 N=256
+//               K=16, FP32 accumulators in TMEM (two 256-column buffers)
+//   warps 2..5  epilogue: tcgen05.ld 32x32b, BF16 rounding, global stores
+// GEMM1 (SwiGLU): B = [128 gate rows ; 128 up rows] of the expert, epilogue
+//   h = bf16(bf16(silu(bf16(g))) * bf16(u)) -> h[rows, I].
+// GEMM2 (down):   B = 256 rows of Wd, epilogue y = bf16(acc) -> y[rows, H].
+// Rows of an A tile past the expert's segment belong to the next expert (or
+// are TMA zero fill past the end); they are computed but never stored.
+// Every mbarrier wait is bounded (2 s); a timeout raises the device error
+// word, releases the other roles through a shared abort flag, drains the
+// tensor core and frees TMEM before the CTA exits.
+#include <cuda.h>
+
+#include "pdx_common.cuh"
+
+namespace pdx {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;   // 64 BF16 = one 128-byte swizzle row
+constexpr int kGemmBN = 256;  // MMA N (B rows per stage)
+constexpr int kGemmStages = 4;
+constexpr int kGemmThreads = 192;
+constexpr uint32_t kTileABytes = kGemmBM * kGemmBK * 2;  // 16 KiB
+constexpr uint32_t kTileBBytes = kGemmBN * kGemmBK * 2;  // 32 KiB
+constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
+constexpr uint32_t kTmemCols = 512;  // two 256-column FP32 accumulators
+constexpr int kMaxActive = 1024;
+constexpr size_t kGemmSmemBytes = 1024 /*alignment slack*/ + kGemmStages * kStageBytes + 256 /*barriers*/ +
+                                  (kMaxActive + 1) * 4 /*tile prefix*/;
+
+struct GemmArgs {
+    const int32_t* offsets;
+    const int32_t* active;
+    const int32_t* slot_of_expert;
+    int64_t num_slots;
+    int64_t b0_rows_per_slot;  // B-map rows between consecutive slots
+    int64_t b1_rows_per_slot;
+    int K;                     // reduction length
+    int n_cols;                // output columns per expert
+    int swiglu;                // 1: GEMM1 with SiLU*up epilogue, 0: down projection
+    uint16_t* out;
+    int64_t out_ld;
+};
+
+// ---- tcgen05 wrappers -------------------------------------------------------
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
+    return static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
+           (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+           (static_cast<uint64_t>(2) << 61);
+}
+
+__host__ __device__ constexpr uint32_t bf16_idesc(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+           (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---- tile schedule ------------------------------------------------------------
+struct TileInfo {
+    int e;
+    int m;
+    int n;
+};
+
+__device__ __forceinline__ TileInfo decode_tile(int tile, const int* prefix, int n_active, int n_tiles,
+                                                const int32_t* active) {
+    int lo = 0, hi = n_active - 1;  // largest a with prefix[a] <= tile
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (prefix[mid] <= tile) lo = mid; else hi = mid - 1;
+    }
+    const int local = tile - prefix[lo];
+    TileInfo ti;
+    ti.e = active[1 + lo];
+    ti.m = local / n_tiles;
+    ti.n = local % n_tiles;
+    return ti;
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    k_grouped_gemm(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b0,
+                   const __grid_constant__ CUtensorMap tm_b1, GemmArgs args) {
+    extern __shared__ __align__(1024) unsigned char smem_gemm[];
+    // 1024-byte aligned stage buffers (SWIZZLE_128B atoms)
+    const uint32_t raw_addr = smem_u32(smem_gemm);
+    unsigned char* smem = smem_gemm + ((1024u - (raw_addr & 1023u)) & 1023u);
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + kGemmStages * kStageBytes);
+    uint64_t* empty_bar = full_bar + kGemmStages;
+    uint64_t* tmem_full = empty_bar + kGemmStages;
+    uint64_t* tmem_empty = tmem_full + 2;
+    uint64_t* drain_bar = tmem_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int* s_misc = reinterpret_cast<int*>(tmem_slot + 2);  // [0] = total tiles, [1] = n_active
+    int* prefix = reinterpret_cast<int*>(smem + kGemmStages * kStageBytes + 256);
+
+    const int warp = static_cast<int>(threadIdx.x >> 5);
+    const uint32_t lane = lane_id();
+    const int n_active = min(args.active[0], kMaxActive);
+    const int out_cols_per_tile = args.swiglu ? kGemmBN / 2 : kGemmBN;
+    const int n_tiles = args.n_cols / out_cols_per_tile;
+    const int num_kb = args.K / kGemmBK;
+
+    // -- setup: barriers, TMEM, tile prefix ------------------------------------
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kGemmStages; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tmem_full[b], 1);
+            mbar_init(&tmem_empty[b], 128);
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tm_a);
+        tma_prefetch_desc(&tm_b0);
+        if (args.swiglu) tma_prefetch_desc(&tm_b1);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    // per-expert m-tile counts -> exclusive prefix (warp 2)
+    if (warp == 2) {
+        const int per = (n_active + 31) / 32;
+        const int b = static_cast<int>(lane) * per;
+        int local = 0;
+        for (int i = 0; i < per; ++i)
+            if (b + i < n_active) {
+                const int e = args.active[1 + b + i];
+                const int rows = args.offsets[e + 1] - args.offsets[e];
+                const int tiles = ((rows + kGemmBM - 1) / kGemmBM) * n_tiles;
+                prefix[b + i] = tiles;
+                local += tiles;
+            }
+        int inc = local;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, inc, off);
+            if (static_cast<int>(lane) >= off) inc += y;
+        }
+        int run = inc - local;
+        for (int i = 0; i < per; ++i)
+            if (b + i < n_active) {
+                const int t = prefix[b + i];
+                prefix[b + i] = run;
+                run += t;
+            }
+        if (lane == 31) { s_misc[0] = inc; s_misc[1] = n_active; }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total_tiles = s_misc[0];
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (elect_one()) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+                const TileInfo ti = decode_tile(tile, prefix, n_active, n_tiles, args.active);
+                int64_t slot = args.slot_of_expert ? args.slot_of_expert[ti.e] : ti.e;
+                if (slot < 0 || slot >= args.num_slots) {
+                    raise_error(PDX_DEVERR_BAD_SLOT);
+                    slot = 0;  // keep the pipeline consistent; the result is flagged invalid
+                }
+                const int row_a = args.offsets[ti.e] + ti.m * kGemmBM;
+                const int row_b0 = static_cast<int>(slot * args.b0_rows_per_slot) + ti.n * out_cols_per_tile;
+                const int row_b1 = static_cast<int>(slot * args.b1_rows_per_slot) + ti.n * out_cols_per_tile;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
+                    unsigned char* sa = smem + stage * kStageBytes;
+                    unsigned char* sb = sa + kTileABytes;
+                    mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
+                    tma_load_2d(sa, &tm_a, &full_bar[stage], kb * kGemmBK, row_a);
+                    if (args.swiglu) {
+                        tma_load_2d(sb, &tm_b0, &full_bar[stage], kb * kGemmBK, row_b0);
+                        tma_load_2d(sb + kTileBBytes / 2, &tm_b1, &full_bar[stage], kb * kGemmBK, row_b1);
+                    } else {
+                        tma_load_2d(sb, &tm_b0, &full_bar[stage], kb * kGemmBK, row_b0);
+                    }
+                    if (++stage == kGemmStages) { stage = 0; phase ^= 1u; }
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        constexpr uint32_t idesc = bf16_idesc(kGemmBM, kGemmBN);
+        int stage = 0;
+        uint32_t phase = 0;
+        int lt = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++lt) {
+            const int b = lt & 1;
+            const uint32_t acc_phase = static_cast<uint32_t>(lt >> 1) & 1u;
+            if (!mbar_wait(&tmem_empty[b], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * kGemmBN);
+            for (int kb = 0; kb < num_kb; ++kb) {
+                if (!mbar_wait(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                if (elect_one()) {
+                    const uint32_t sa = smem_u32(smem + stage * kStageBytes);
+                    const uint32_t sb = sa + kTileABytes;
+                    const uint64_t a0 = sw128_desc(sa), b0 = sw128_desc(sb);
+#pragma unroll
+                    for (int kk = 0; kk < kGemmBK / 16; ++kk)
+                        umma_bf16(d_tmem, a0 + 2u * kk, b0 + 2u * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+                    umma_commit(&empty_bar[stage]);
+                }
+                __syncwarp();
+                if (++stage == kGemmStages) { stage = 0; phase ^= 1u; }
+            }
+            if (!ok) break;
+            if (elect_one()) umma_commit(&tmem_full[b]);
+            __syncwarp();
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        const int row_in_tile = q * 32 + static_cast<int>(lane);
+        int lt = 0;
+        for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++lt) {
+            const int b = lt & 1;
+            const uint32_t acc_phase = static_cast<uint32_t>(lt >> 1) & 1u;
+            if (!mbar_wait(&tmem_full[b], acc_phase, abort_flag)) break;
+            tc_fence_after();
+            const TileInfo ti = decode_tile(tile, prefix, n_active, n_tiles, args.active);
+            const int seg0 = args.offsets[ti.e];
+            const int n_e = args.offsets[ti.e + 1] - seg0;
+            const int r = ti.m * kGemmBM + row_in_tile;
+            const bool valid = r < n_e;
+            uint16_t* orow = args.out + static_cast<int64_t>(seg0 + r) * args.out_ld + ti.n * out_cols_per_tile;
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * kGemmBN);
+            if (args.swiglu) {
+#pragma unroll 1
+                for (int c = 0; c < kGemmBN / 2; c += 16) {
+                    uint32_t g[16], u[16];
+                    tmem_ld16(taddr + c, g);
+                    tmem_ld16(taddr + kGemmBN / 2 + c, u);
+                    tmem_wait_ld();
+                    uint32_t packed[8];
+#pragma unroll
+                    for (int i = 0; i < 16; i += 2) {
+                        float hv[2];
+#pragma unroll
+                        for (int j = 0; j < 2; ++j) {
+                            const float gb = round_bf16(__uint_as_float(g[i + j]));
+                            const float ub = round_bf16(__uint_as_float(u[i + j]));
+                            const float s = round_bf16(__fdiv_rn(gb, 1.0f + expf(-gb)));
+                            hv[j] = s * ub;
+                        }
+                        packed[i / 2] = static_cast<uint32_t>(f2bits(hv[0])) | (static_cast<uint32_t>(f2bits(hv[1])) << 16);
+                    }
+                    if (valid) {
+                        uint4* dst = reinterpret_cast<uint4*>(orow + c);
+                        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < kGemmBN; c += 16) {
+                    uint32_t v[16];
+                    tmem_ld16(taddr + c, v);
+                    tmem_wait_ld();
+                    uint32_t packed[8];
+#pragma unroll
+                    for (int i = 0; i < 16; i += 2)
+                        packed[i / 2] = static_cast<uint32_t>(f2bits(__uint_as_float(v[i]))) |
+                                        (static_cast<uint32_t>(f2bits(__uint_as_float(v[i + 1]))) << 16);
+                    if (valid) {
+                        uint4* dst = reinterpret_cast<uint4*>(orow + c);
+                        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tmem_empty[b]);
+        }
+    }
+
+    // -- teardown -------------------------------------------------------------------
+    __syncthreads();
+    if (*abort_flag) {
+        // Let in-flight TMA copies land and the tensor core finish before the
+        // shared memory and TMEM of this CTA are released.
+        if (warp == 1) {
+            if (elect_one()) umma_commit(drain_bar);
+            __syncwarp();
+            volatile int never = 0;
+            mbar_wait(drain_bar, 0, &never);
+        }
+        const unsigned long long t0 = global_timer_ns();
+        while (global_timer_ns() - t0 < 2000000ull) __nanosleep(1000);
+        __syncthreads();
+    }
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
+}  // namespace pdx

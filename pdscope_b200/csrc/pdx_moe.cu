@@ -1,0 +1,579 @@
+// libpdx_moe.so: the C ABI declared in include/pdx_moe.h.
+//
+// Unity build: the kernel files are included here so the whole library is
+// one translation unit (one copy of the device error word, no -rdc).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "combine.cu"
+#include "ffn_gemm.cu"
+#include "ffn_gemv.cu"
+#include "pack.cu"
+#include "route.cu"
+
+namespace pdx {
+namespace {
+
+thread_local std::string t_last_error;
+std::atomic<uint64_t> g_launches{0};
+
+int fail(int status, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return status;
+}
+
+int ok() {
+    t_last_error.clear();
+    return PDX_OK;
+}
+
+#define PDX_CUDA_TRY(expr)                                                                   \
+    do {                                                                                     \
+        cudaError_t _e = (expr);                                                             \
+        if (_e != cudaSuccess) return fail(PDX_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(_e)); \
+    } while (0)
+
+#define PDX_LAUNCHED()                                                                              \
+    do {                                                                                            \
+        g_launches.fetch_add(1, std::memory_order_relaxed);                                         \
+        cudaError_t _e = cudaGetLastError();                                                        \
+        if (_e != cudaSuccess) return fail(PDX_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(_e)); \
+    } while (0)
+
+constexpr size_t kAlign = 256;
+inline size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+// Bump allocator over the caller's workspace.
+struct Carver {
+    char* base;
+    size_t cap;
+    size_t used = 0;
+    bool overflow = false;
+    void* take(size_t bytes) {
+        const size_t off = used;
+        used = align_up(used + bytes);
+        if (used > cap) overflow = true;
+        return base ? base + off : nullptr;
+    }
+};
+
+constexpr int kMaxDevices = 64;
+int g_num_sms[kMaxDevices] = {0};
+bool g_attrs_set[kMaxDevices] = {false};
+std::mutex g_dev_mutex;
+
+int device_setup(int* sms_out) {
+    int dev = 0;
+    PDX_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return fail(PDX_ERR_UNSUPPORTED, "device ordinal %d", dev);
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    if (!g_attrs_set[dev]) {
+        int sms = 0;
+        PDX_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        int major = 0;
+        PDX_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+        if (major != 10) return fail(PDX_ERR_UNSUPPORTED, "pdx_moe is built for sm_100a; device %d is sm_%d", dev, major);
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_grouped_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(kGemmSmemBytes)));
+        const int gemv_smem = 128 * 1024;
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_gateup_gemv<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemv_smem));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_gateup_gemv<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemv_smem));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_down_gemv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemv_smem));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_down_gemv<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemv_smem));
+        g_num_sms[dev] = sms;
+        g_attrs_set[dev] = true;
+    }
+    *sms_out = g_num_sms[dev];
+    return PDX_OK;
+}
+
+// ---- TMA descriptors -------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int encode_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (!g_encode) return fail(PDX_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return fail(PDX_ERR_INVALID, "TMA base not 16-byte aligned");
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kGemmBK), box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(PDX_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return PDX_OK;
+}
+
+// ---- shape checks -----------------------------------------------------------------
+constexpr int kMaxTopK = 32;
+constexpr int kMaxExperts = 1024;
+constexpr int64_t kTailMaxTokens = 64;     // fused route tail up to this many tokens
+constexpr int64_t kPackSingleMax = 8192;   // single-CTA pack up to this many assignments
+constexpr int64_t kGemvMaxTokens = 64;     // auto mode: GEMV for T <= this
+
+int check_route_shape(int64_t T, int64_t H, int64_t E, int32_t k) {
+    if (T < 1) return fail(PDX_ERR_INVALID, "empty expert routing (T=%lld)", static_cast<long long>(T));
+    if (E < 1 || k < 1 || k > E) return fail(PDX_ERR_INVALID, "invalid routing parameters (E=%lld, top_k=%d)",
+                                             static_cast<long long>(E), k);
+    if (E > kMaxExperts) return fail(PDX_ERR_UNSUPPORTED, "E=%lld > %d experts", static_cast<long long>(E), kMaxExperts);
+    if (k > kMaxTopK) return fail(PDX_ERR_UNSUPPORTED, "top_k=%d > %d", k, kMaxTopK);
+    if (H < 8 || H % 8) return fail(PDX_ERR_UNSUPPORTED, "hidden size %lld must be a positive multiple of 8",
+                                    static_cast<long long>(H));
+    if (T * k >= (int64_t(1) << 31) || T * E >= (int64_t(1) << 40))
+        return fail(PDX_ERR_UNSUPPORTED, "T=%lld too large", static_cast<long long>(T));
+    return PDX_OK;
+}
+
+int resolve_mode(int32_t mode, int64_t T, int64_t H, int64_t I) {
+    const bool gemm_ok = (H % 256 == 0) && (I % 128 == 0) && (H >= 256) && (I >= 128);
+    if (mode == PDX_FFN_AUTO) return (T > kGemvMaxTokens && gemm_ok) ? PDX_FFN_GEMM : PDX_FFN_GEMV;
+    return mode;
+}
+
+int check_ffn_shape(int64_t H, int64_t I, int32_t mode) {
+    if (H < 8 || I < 8 || H % 8 || I % 8)
+        return fail(PDX_ERR_UNSUPPORTED, "H=%lld, I=%lld must be positive multiples of 8", static_cast<long long>(H),
+                    static_cast<long long>(I));
+    if (mode == PDX_FFN_GEMV) {
+        if (I % 16 || H % 32)
+            return fail(PDX_ERR_UNSUPPORTED, "GEMV path needs I %% 16 == 0 and H %% 32 == 0");
+        if (H > 4096 || I > 4096)
+            return fail(PDX_ERR_UNSUPPORTED, "GEMV path supports H, I <= 4096");
+    } else if (mode == PDX_FFN_GEMM) {
+        if (H % 256 || I % 128)
+            return fail(PDX_ERR_UNSUPPORTED, "tcgen05 path needs H %% 256 == 0 and I %% 128 == 0");
+    } else {
+        return fail(PDX_ERR_INVALID, "unknown FFN mode %d", mode);
+    }
+    return PDX_OK;
+}
+
+int check_weights(const pdx_expert_weights* w, int64_t H, int64_t I) {
+    if (!w || !w->gate || !w->up || !w->down) return fail(PDX_ERR_INVALID, "expert weights missing");
+    if (w->num_slots < 1) return fail(PDX_ERR_INVALID, "num_slots must be >= 1");
+    if (w->num_slots > 1 && (w->gate_stride % H || w->up_stride % H || w->down_stride % I ||
+                             w->gate_stride < I * H || w->up_stride < I * H || w->down_stride < H * I))
+        return fail(PDX_ERR_INVALID, "slot strides must be multiples of the row length and cover one expert");
+    if ((reinterpret_cast<uintptr_t>(w->gate) | reinterpret_cast<uintptr_t>(w->up) |
+         reinterpret_cast<uintptr_t>(w->down)) & 15u)
+        return fail(PDX_ERR_INVALID, "expert weights must be 16-byte aligned");
+    return PDX_OK;
+}
+
+ExpertSlab to_slab(const pdx_expert_weights* w) {
+    ExpertSlab s;
+    s.gate = static_cast<const uint16_t*>(w->gate);
+    s.up = static_cast<const uint16_t*>(w->up);
+    s.down = static_cast<const uint16_t*>(w->down);
+    s.gate_stride = w->gate_stride;
+    s.up_stride = w->up_stride;
+    s.down_stride = w->down_stride;
+    s.num_slots = w->num_slots;
+    s.slot_of_expert = w->slot_of_expert;
+    return s;
+}
+
+// ---- internal launchers ---------------------------------------------------------------
+struct RouteBufs {
+    uint16_t* logits;
+    int64_t* selected;
+    uint16_t* weights;
+    unsigned int* ticket;
+};
+
+int launch_route(const void* x, const void* gate, int64_t T, int64_t H, int64_t E, int32_t k, int32_t normalize,
+                 const RouteBufs& b, const PackOut* fused_pack, cudaStream_t stream) {
+    const int n_tb = static_cast<int>((T + kRouteTB - 1) / kRouteTB);
+    const int n_eb = static_cast<int>((E + kRouteEB - 1) / kRouteEB);
+    RouteTail tail{};
+    const bool use_tail = T <= kTailMaxTokens;
+    size_t smem = 0;
+    if (use_tail) {
+        PDX_CUDA_TRY(cudaMemsetAsync(b.ticket, 0, sizeof(unsigned int), stream));
+        tail.enabled = 1;
+        tail.k = k;
+        tail.normalize = normalize;
+        tail.ticket = b.ticket;
+        tail.selected = b.selected;
+        tail.weights = b.weights;
+        if (fused_pack) {
+            tail.do_pack = 1;
+            tail.pack = *fused_pack;
+            smem = static_cast<size_t>(E + E + 1 + (kRouteWarps * E)) * sizeof(int);
+        }
+    }
+    k_router_logits<<<n_tb * n_eb, kRouteWarps * 32, smem, stream>>>(
+        static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gate), static_cast<int>(T), static_cast<int>(H),
+        static_cast<int>(E), b.logits, tail);
+    PDX_LAUNCHED();
+    if (!use_tail) {
+        const int warps_per_cta = 8;
+        const int grid = static_cast<int>((T + warps_per_cta - 1) / warps_per_cta);
+        k_topk<<<grid, warps_per_cta * 32, 0, stream>>>(b.logits, static_cast<int>(T), static_cast<int>(E), k,
+                                                        normalize, b.selected, b.weights);
+        PDX_LAUNCHED();
+    }
+    return PDX_OK;
+}
+
+size_t pack_chunks(int64_t N) { return static_cast<size_t>((N + kPackChunk - 1) / kPackChunk); }
+
+int launch_pack(const int64_t* selected, const uint16_t* weights, int64_t T, int32_t k, int64_t E, const PackOut& o,
+                int* chunk_hist, cudaStream_t stream) {
+    const int64_t N = T * k;
+    if (N <= kPackSingleMax) {
+        const size_t smem = static_cast<size_t>(E + E + 1 + 8 * E) * sizeof(int);
+        k_pack_single<<<1, kPackThreads, smem, stream>>>(selected, weights, static_cast<int>(T), k,
+                                                          static_cast<int>(E), o);
+        PDX_LAUNCHED();
+        return PDX_OK;
+    }
+    const int chunks = static_cast<int>(pack_chunks(N));
+    k_pack_hist<<<chunks, kPackThreads, E * sizeof(int), stream>>>(selected, static_cast<int>(T), k,
+                                                                     static_cast<int>(E), chunk_hist);
+    PDX_LAUNCHED();
+    k_pack_scan<<<1, kPackThreads, (2 * E + 1) * sizeof(int), stream>>>(chunk_hist, chunks, static_cast<int>(E), o);
+    PDX_LAUNCHED();
+    k_pack_scatter<<<chunks, kPackThreads, (E + 8 * E) * sizeof(int), stream>>>(
+        selected, weights, static_cast<int>(T), k, static_cast<int>(E), chunk_hist, o);
+    PDX_LAUNCHED();
+    return PDX_OK;
+}
+
+size_t ffn_ws_bytes(int64_t rows, int64_t H, int64_t I, int mode) {
+    size_t b = align_up(static_cast<size_t>(rows) * I * 2);  // h
+    if (mode == PDX_FFN_GEMM) b += align_up(static_cast<size_t>(rows) * H * 2);  // gathered rows
+    return b;
+}
+
+int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* offsets, const int32_t* active,
+               int64_t E, int64_t rows, const pdx_expert_weights* w, int64_t H, int64_t I, void* y, int mode,
+               Carver& ws, cudaStream_t stream) {
+    int sms = 0;
+    int st = device_setup(&sms);
+    if (st) return st;
+    uint16_t* h = static_cast<uint16_t*>(ws.take(static_cast<size_t>(rows) * I * 2));
+    uint16_t* xp = mode == PDX_FFN_GEMM ? static_cast<uint16_t*>(ws.take(static_cast<size_t>(rows) * H * 2)) : nullptr;
+    if (ws.overflow) return fail(PDX_ERR_WORKSPACE, "FFN workspace too small (%zu > %zu bytes)", ws.used, ws.cap);
+    const ExpertSlab slab = to_slab(w);
+    const int64_t max_active = std::min<int64_t>(E, rows);
+    if (mode == PDX_FFN_GEMV) {
+        const bool small = rows <= 64;
+        const int rb = small ? 4 : 16;
+        const int rpw_down = small ? 1 : 4;
+        if (I % rb || H % (8 * rpw_down))
+            return fail(PDX_ERR_UNSUPPORTED, "GEMV tiling needs I %% %d == 0 and H %% %d == 0", rb, 8 * rpw_down);
+        const int64_t items1 = max_active * (I / rb);
+        const int64_t items2 = max_active * (H / (8 * rpw_down));
+        const int grid1 = static_cast<int>(std::min<int64_t>(items1, static_cast<int64_t>(sms) * 4));
+        const int grid2 = static_cast<int>(std::min<int64_t>(items2, static_cast<int64_t>(sms) * 4));
+        const size_t smem1 = static_cast<size_t>(kTokChunk) * H * 2 + 2 * rb * kTokChunk * 4;
+        const size_t smem2 = static_cast<size_t>(kTokChunk) * I * 2 + 8 * rpw_down * kTokChunk * 4;
+        const uint16_t* xb = static_cast<const uint16_t*>(x);
+        if (small)
+            k_gateup_gemv<4><<<grid1, kGemvThreads, smem1, stream>>>(xb, tokens, offsets, active, slab,
+                                                                      static_cast<int>(H), static_cast<int>(I), h);
+        else
+            k_gateup_gemv<16><<<grid1, kGemvThreads, smem1, stream>>>(xb, tokens, offsets, active, slab,
+                                                                       static_cast<int>(H), static_cast<int>(I), h);
+        PDX_LAUNCHED();
+        if (small)
+            k_down_gemv<1><<<grid2, kGemvThreads, smem2, stream>>>(h, offsets, active, slab, static_cast<int>(H),
+                                                                    static_cast<int>(I), static_cast<uint16_t*>(y));
+        else
+            k_down_gemv<4><<<grid2, kGemvThreads, smem2, stream>>>(h, offsets, active, slab, static_cast<int>(H),
+                                                                    static_cast<int>(I), static_cast<uint16_t*>(y));
+        PDX_LAUNCHED();
+        return PDX_OK;
+    }
+    // tcgen05 path: gather -> GEMM1 (gate|up, SwiGLU) -> GEMM2 (down)
+    k_gather_rows<<<static_cast<unsigned>(rows), kCombineThreads, 0, stream>>>(
+        static_cast<const uint16_t*>(x), tokens, static_cast<int>(rows), static_cast<int>(H), xp);
+    PDX_LAUNCHED();
+    const int64_t gs = w->num_slots > 1 ? w->gate_stride / H : 0;
+    const int64_t us = w->num_slots > 1 ? w->up_stride / H : 0;
+    const int64_t ds = w->num_slots > 1 ? w->down_stride / I : 0;
+    CUtensorMap tm_x, tm_g, tm_u, tm_h, tm_d;
+    if ((st = encode_2d(&tm_x, xp, rows, H, kGemmBM))) return st;
+    if ((st = encode_2d(&tm_g, w->gate, (w->num_slots - 1) * gs + I, H, kGemmBN / 2))) return st;
+    if ((st = encode_2d(&tm_u, w->up, (w->num_slots - 1) * us + I, H, kGemmBN / 2))) return st;
+    if ((st = encode_2d(&tm_h, h, rows, I, kGemmBM))) return st;
+    if ((st = encode_2d(&tm_d, w->down, (w->num_slots - 1) * ds + H, I, kGemmBN))) return st;
+    if ((w->num_slots - 1) * std::max(gs, std::max(us, ds)) + H >= (int64_t(1) << 31))
+        return fail(PDX_ERR_UNSUPPORTED, "expert slab too large for 32-bit TMA row coordinates");
+    const int64_t m_tiles_bound = rows / kGemmBM + max_active;
+    GemmArgs a1{offsets, active, w->slot_of_expert, w->num_slots, gs, us, static_cast<int>(H),
+                static_cast<int>(I), 1, h, I};
+    const int grid1 = static_cast<int>(std::min<int64_t>(sms, m_tiles_bound * (I / (kGemmBN / 2))));
+    k_grouped_gemm<<<grid1, kGemmThreads, kGemmSmemBytes, stream>>>(tm_x, tm_g, tm_u, a1);
+    PDX_LAUNCHED();
+    GemmArgs a2{offsets, active, w->slot_of_expert, w->num_slots, ds, ds, static_cast<int>(I),
+                static_cast<int>(H), 0, static_cast<uint16_t*>(y), H};
+    const int grid2 = static_cast<int>(std::min<int64_t>(sms, m_tiles_bound * (H / kGemmBN)));
+    k_grouped_gemm<<<grid2, kGemmThreads, kGemmSmemBytes, stream>>>(tm_h, tm_d, tm_d, a2);
+    PDX_LAUNCHED();
+    return PDX_OK;
+}
+
+// one expert owning rows [0, n): offsets = {0, n}, active = {1, 0}, tokens = 0..n-1
+__global__ void k_single_expert_setup(int n, int32_t* offsets, int32_t* active, int32_t* tokens) {
+    const int i = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x);
+    if (i == 0) {
+        offsets[0] = 0;
+        offsets[1] = n;
+        active[0] = 1;
+        active[1] = 0;
+    }
+    if (i < n) tokens[i] = i;
+}
+
+struct PackBufs {
+    PackOut o;
+    int* chunk_hist;
+};
+
+PackBufs carve_pack(Carver& c, int64_t T, int32_t k, int64_t E, int32_t* counts_out) {
+    const int64_t N = T * k;
+    PackBufs p;
+    p.o.counts = counts_out ? counts_out : static_cast<int32_t*>(c.take(E * 4));
+    p.o.offsets = static_cast<int32_t*>(c.take((E + 1) * 4));
+    p.o.tokens = static_cast<int32_t*>(c.take(N * 4));
+    p.o.positions = static_cast<int32_t*>(c.take(N * 4));
+    p.o.packed_w = static_cast<uint16_t*>(c.take(N * 2));
+    p.o.inverse = static_cast<int32_t*>(c.take(N * 4));
+    p.o.active = static_cast<int32_t*>(c.take((E + 1) * 4));
+    p.chunk_hist = static_cast<int*>(c.take(pack_chunks(N) * E * 4));
+    return p;
+}
+
+}  // namespace
+}  // namespace pdx
+
+using namespace pdx;
+
+extern "C" {
+
+const char* pdx_last_error(void) { return t_last_error.c_str(); }
+
+int pdx_abi_version(void) { return PDX_ABI_VERSION; }
+
+uint64_t pdx_launch_count(void) { return g_launches.load(); }
+
+size_t pdx_route_workspace_bytes(int64_t T, int64_t E) {
+    return align_up(256) + align_up(static_cast<size_t>(std::max<int64_t>(T, 0)) * std::max<int64_t>(E, 0) * 2);
+}
+
+int pdx_route_topk(const void* x, const void* gate, int64_t T, int64_t H, int64_t E, int32_t top_k, int32_t normalize,
+                   void* logits_out, int64_t* selected_out, void* weights_out, void* workspace,
+                   size_t workspace_bytes, pdx_stream_t stream) {
+    int st = check_route_shape(T, H, E, top_k);
+    if (st) return st;
+    if (!x || !gate || !selected_out || !weights_out) return fail(PDX_ERR_INVALID, "null routing argument");
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1)))
+        return fail(PDX_ERR_WORKSPACE, "workspace must be non-null and 256-byte aligned");
+    Carver c{static_cast<char*>(workspace), workspace_bytes};
+    RouteBufs b;
+    b.ticket = static_cast<unsigned int*>(c.take(256));
+    b.logits = logits_out ? static_cast<uint16_t*>(logits_out) : static_cast<uint16_t*>(c.take(T * E * 2));
+    b.selected = selected_out;
+    b.weights = static_cast<uint16_t*>(weights_out);
+    if (c.overflow) return fail(PDX_ERR_WORKSPACE, "route workspace too small");
+    st = launch_route(x, gate, T, H, E, top_k, normalize, b, nullptr, stream);
+    return st ? st : ok();
+}
+
+int pdx_topk_from_logits(const void* logits, int64_t T, int64_t E, int32_t top_k, int32_t normalize,
+                         int64_t* selected_out, void* weights_out, pdx_stream_t stream) {
+    int st = check_route_shape(T, 8, E, top_k);
+    if (st) return st;
+    if (!logits || !selected_out || !weights_out) return fail(PDX_ERR_INVALID, "null routing argument");
+    const int warps_per_cta = 8;
+    const int grid = static_cast<int>((T + warps_per_cta - 1) / warps_per_cta);
+    k_topk<<<grid, warps_per_cta * 32, 0, stream>>>(static_cast<const uint16_t*>(logits), static_cast<int>(T),
+                                                    static_cast<int>(E), top_k, normalize, selected_out,
+                                                    static_cast<uint16_t*>(weights_out));
+    PDX_LAUNCHED();
+    return ok();
+}
+
+size_t pdx_pack_workspace_bytes(int64_t T, int32_t top_k, int64_t E) {
+    const int64_t N = std::max<int64_t>(T, 0) * std::max<int32_t>(top_k, 0);
+    return align_up(pack_chunks(N) * std::max<int64_t>(E, 0) * 4) + kAlign;
+}
+
+int pdx_pack(const int64_t* selected, const void* weights, int64_t T, int32_t top_k, int64_t E, int32_t* counts,
+             int32_t* offsets, int32_t* tokens, int32_t* positions, void* packed_w, int32_t* inverse,
+             int32_t* active, void* workspace, size_t workspace_bytes, pdx_stream_t stream) {
+    int st = check_route_shape(T, 8, E, top_k);
+    if (st) return st;
+    if (!selected || !weights || !counts || !offsets || !tokens || !positions || !packed_w || !inverse || !active)
+        return fail(PDX_ERR_INVALID, "null packing argument");
+    if (workspace_bytes < pdx_pack_workspace_bytes(T, top_k, E) || !workspace)
+        return fail(PDX_ERR_WORKSPACE, "pack workspace too small");
+    PackOut o{counts, offsets, tokens, positions, static_cast<uint16_t*>(packed_w), inverse, active};
+    st = launch_pack(selected, static_cast<const uint16_t*>(weights), T, top_k, E, o, static_cast<int*>(workspace),
+                     stream);
+    return st ? st : ok();
+}
+
+int pdx_gather_rows(const void* x, const int32_t* tokens, int64_t rows, int64_t H, void* out, pdx_stream_t stream) {
+    if (!x || !tokens || !out || rows < 0) return fail(PDX_ERR_INVALID, "null gather argument");
+    if (H < 8 || H % 8) return fail(PDX_ERR_UNSUPPORTED, "H must be a positive multiple of 8");
+    if (rows == 0) return ok();
+    k_gather_rows<<<static_cast<unsigned>(rows), kCombineThreads, 0, stream>>>(
+        static_cast<const uint16_t*>(x), tokens, static_cast<int>(rows), static_cast<int>(H),
+        static_cast<uint16_t*>(out));
+    PDX_LAUNCHED();
+    return ok();
+}
+
+size_t pdx_ffn_workspace_bytes(int64_t rows, int64_t H, int64_t I, int32_t mode) {
+    const int m = resolve_mode(mode, rows, H, I);
+    return ffn_ws_bytes(rows, H, I, m) + kAlign;
+}
+
+int pdx_moe_ffn_grouped(const void* x, int64_t T, const int32_t* tokens, const int32_t* offsets,
+                        const int32_t* active, int64_t E, int64_t rows, const pdx_expert_weights* weights, int64_t H,
+                        int64_t I, void* y_out, int32_t mode, void* workspace, size_t workspace_bytes,
+                        pdx_stream_t stream) {
+    if (!x || !tokens || !offsets || !active || !y_out) return fail(PDX_ERR_INVALID, "null FFN argument");
+    if (T < 1 || rows < 1 || E < 1) return fail(PDX_ERR_INVALID, "empty FFN batch");
+    const int m = resolve_mode(mode, T, H, I);
+    int st = check_ffn_shape(H, I, m);
+    if (st) return st;
+    if ((st = check_weights(weights, H, I))) return st;
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1)))
+        return fail(PDX_ERR_WORKSPACE, "workspace must be non-null and 256-byte aligned");
+    Carver c{static_cast<char*>(workspace), workspace_bytes};
+    st = launch_ffn(x, T, tokens, offsets, active, E, rows, weights, H, I, y_out, m, c, stream);
+    return st ? st : ok();
+}
+
+size_t pdx_expert_ffn_workspace_bytes(int64_t n, int64_t H, int64_t I) {
+    const int64_t nn = std::max<int64_t>(n, 1);
+    const int m = resolve_mode(PDX_FFN_AUTO, nn, H, I);
+    return align_up(8) * 2 + align_up(nn * 4) + ffn_ws_bytes(nn, H, I, m) + kAlign;
+}
+
+int pdx_expert_ffn(const void* x, int64_t n, const void* gate, const void* up, const void* down, int64_t H, int64_t I,
+                   void* y_out, void* workspace, size_t workspace_bytes, pdx_stream_t stream) {
+    if (!x || !gate || !up || !down || !y_out) return fail(PDX_ERR_INVALID, "null expert argument");
+    if (n < 1) return fail(PDX_ERR_INVALID, "expert input must have at least one row");
+    const int m = resolve_mode(PDX_FFN_AUTO, n, H, I);
+    int st = check_ffn_shape(H, I, m);
+    if (st) return st;
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1)) ||
+        workspace_bytes < pdx_expert_ffn_workspace_bytes(n, H, I))
+        return fail(PDX_ERR_WORKSPACE, "expert FFN workspace too small");
+    pdx_expert_weights w{gate, up, down, 0, 0, 0, 1, nullptr};
+    if ((st = check_weights(&w, H, I))) return st;
+    Carver c{static_cast<char*>(workspace), workspace_bytes};
+    int32_t* offsets = static_cast<int32_t*>(c.take(8));
+    int32_t* active = static_cast<int32_t*>(c.take(8));
+    int32_t* tokens = static_cast<int32_t*>(c.take(n * 4));
+    k_single_expert_setup<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(static_cast<int>(n), offsets,
+                                                                                      active, tokens);
+    PDX_LAUNCHED();
+    st = launch_ffn(x, n, tokens, offsets, active, 1, n, &w, H, I, y_out, m, c, stream);
+    return st ? st : ok();
+}
+
+int pdx_combine(const void* y, const void* weights, const int32_t* inverse, int64_t T, int32_t top_k, int64_t H,
+                const void* residual, void* out, pdx_stream_t stream) {
+    if (!y || !weights || !inverse || !out) return fail(PDX_ERR_INVALID, "null combine argument");
+    if (T < 1 || top_k < 1) return fail(PDX_ERR_INVALID, "empty combine");
+    if (top_k > kMaxTopK) return fail(PDX_ERR_UNSUPPORTED, "top_k > %d", kMaxTopK);
+    if (H < 8 || H % 8) return fail(PDX_ERR_UNSUPPORTED, "H must be a positive multiple of 8");
+    k_combine<<<static_cast<unsigned>(T), kCombineThreads, 0, stream>>>(
+        static_cast<const uint16_t*>(y), static_cast<const uint16_t*>(weights), inverse, static_cast<int>(T), top_k,
+        static_cast<int>(H), static_cast<const uint16_t*>(residual), static_cast<uint16_t*>(out));
+    PDX_LAUNCHED();
+    return ok();
+}
+
+size_t pdx_layer_workspace_bytes(int64_t T, int64_t H, int64_t E, int32_t top_k, int64_t I, int32_t mode) {
+    T = std::max<int64_t>(T, 1);
+    E = std::max<int64_t>(E, 1);
+    top_k = std::max<int32_t>(top_k, 1);
+    const int64_t N = T * top_k;
+    Carver c{nullptr, SIZE_MAX};
+    c.take(256);                 // ticket
+    c.take(T * E * 2);           // logits
+    c.take(N * 8);               // selected
+    c.take(N * 2);               // weights
+    carve_pack(c, T, top_k, E, nullptr);
+    c.take(N * H * 2);           // y
+    const int m = resolve_mode(mode, T, H, I);
+    return c.used + ffn_ws_bytes(N, H, I, m) + kAlign;
+}
+
+int pdx_moe_layer(const void* x, const void* gate, int64_t T, int64_t H, int64_t E, int32_t top_k, int32_t normalize,
+                  const pdx_expert_weights* weights, int64_t I, const void* residual, void* out, void* logits_out,
+                  int64_t* selected_out, void* weights_out, int32_t* counts_out, int32_t mode, void* workspace,
+                  size_t workspace_bytes, pdx_stream_t stream) {
+    int st = check_route_shape(T, H, E, top_k);
+    if (st) return st;
+    if (!x || !gate || !out) return fail(PDX_ERR_INVALID, "null layer argument");
+    const int m = resolve_mode(mode, T, H, I);
+    if ((st = check_ffn_shape(H, I, m))) return st;
+    if ((st = check_weights(weights, H, I))) return st;
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1)))
+        return fail(PDX_ERR_WORKSPACE, "workspace must be non-null and 256-byte aligned");
+    const int64_t N = T * top_k;
+    Carver c{static_cast<char*>(workspace), workspace_bytes};
+    RouteBufs rb;
+    rb.ticket = static_cast<unsigned int*>(c.take(256));
+    rb.logits = logits_out ? static_cast<uint16_t*>(logits_out) : static_cast<uint16_t*>(c.take(T * E * 2));
+    rb.selected = selected_out ? selected_out : static_cast<int64_t*>(c.take(N * 8));
+    rb.weights = weights_out ? static_cast<uint16_t*>(weights_out) : static_cast<uint16_t*>(c.take(N * 2));
+    PackBufs pb = carve_pack(c, T, top_k, E, counts_out);
+    uint16_t* y = static_cast<uint16_t*>(c.take(N * H * 2));
+    if (c.overflow) return fail(PDX_ERR_WORKSPACE, "layer workspace too small (%zu > %zu bytes)", c.used, c.cap);
+    const bool fused = T <= kTailMaxTokens;
+    if ((st = launch_route(x, gate, T, H, E, top_k, normalize, rb, fused ? &pb.o : nullptr, stream))) return st;
+    if (!fused && (st = launch_pack(rb.selected, rb.weights, T, top_k, E, pb.o, pb.chunk_hist, stream))) return st;
+    if ((st = launch_ffn(x, T, pb.o.tokens, pb.o.offsets, pb.o.active, E, N, weights, H, I, y, m, c, stream)))
+        return st;
+    k_combine<<<static_cast<unsigned>(T), kCombineThreads, 0, stream>>>(
+        y, rb.weights, pb.o.inverse, static_cast<int>(T), top_k, static_cast<int>(H),
+        static_cast<const uint16_t*>(residual), static_cast<uint16_t*>(out));
+    PDX_LAUNCHED();
+    return ok();
+}
+
+int pdx_device_error(pdx_stream_t stream, uint32_t* code_out) {
+    PDX_CUDA_TRY(cudaStreamSynchronize(stream));
+    unsigned int code = 0;
+    PDX_CUDA_TRY(cudaMemcpyFromSymbol(&code, g_device_error, sizeof(code)));
+    if (code) {
+        const unsigned int zero = 0;
+        PDX_CUDA_TRY(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)));
+    }
+    if (code_out) *code_out = code;
+    if (code) return fail(PDX_ERR_DEVICE, "device error code %u", code);
+    return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,133 @@
+// Router kernels: exact BF16 logits, softmax/top-k, and the fused decode tail.
+//
+// Reference: route() -- expertbench/adapters/qwen.py:140-152 (logits via
+// F.linear, FP32 softmax, torch.topk, renormalise, cast to BF16).
+#include "routing.cuh"
+
+namespace pdx {
+
+constexpr int kRouteTB = 8;       // tokens per CTA block
+constexpr int kRouteEB = 8;       // experts per CTA block
+constexpr int kRouteWarps = 8;    // warps per CTA, each owning a share of K
+
+struct RouteTail {
+    int enabled;           // 1: last CTA runs top-k (+ pack) for every token
+    int k;
+    int normalize;
+    int do_pack;
+    unsigned int* ticket;  // zeroed by the host before the launch
+    int64_t* selected;
+    uint16_t* weights;
+    PackOut pack;
+};
+
+__device__ __forceinline__ double bits_to_f64(uint32_t b16) {
+    return static_cast<double>(__uint_as_float(b16 << 16));
+}
+
+// logits[t, e] = RNE_bf16( sum_h x[t,h] * gate[e,h] ) with FP64 accumulation.
+// A CTA owns an 8-token x 8-expert block.  Warp w accumulates the 256-wide K
+// chunks j = w, w+8, ...; inside a chunk lane l takes elements 8l..8l+7.  A
+// transpose-reduction leaves block outputs (2l, 2l+1) (row-major t*8+e) in
+// lane l; the 8 warps' partials are then added in warp order.  Products of
+// two BF16 values are exact in FP64 and the FP64 sum of 2048 of them is
+// within a few units of 2^-53 relative, so the BF16 rounding equals that of
+// the exact sum except in cases of probability ~1e-12 per logit.
+__global__ void __launch_bounds__(kRouteWarps * 32) k_router_logits(const uint16_t* __restrict__ x,
+                                                                     const uint16_t* __restrict__ gate, int T,
+                                                                     int H, int E, uint16_t* __restrict__ logits,
+                                                                     RouteTail tail) {
+    __shared__ double s_part[kRouteWarps][kRouteTB * kRouteEB];
+    const int warp = static_cast<int>(threadIdx.x >> 5);
+    const int lane = static_cast<int>(lane_id());
+    const int n_eb = (E + kRouteEB - 1) / kRouteEB;
+    const int t0 = (static_cast<int>(blockIdx.x) / n_eb) * kRouteTB;
+    const int e0 = (static_cast<int>(blockIdx.x) % n_eb) * kRouteEB;
+    double acc[kRouteTB * kRouteEB];
+#pragma unroll
+    for (int i = 0; i < kRouteTB * kRouteEB; ++i) acc[i] = 0.0;
+    for (int k0 = warp * 256 + lane * 8; k0 < H; k0 += kRouteWarps * 256) {
+        uint4 xv[kRouteTB], gv[kRouteEB];
+#pragma unroll
+        for (int t = 0; t < kRouteTB; ++t)
+            xv[t] = (t0 + t < T) ? __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(t0 + t) * H + k0))
+                                 : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int e = 0; e < kRouteEB; ++e)
+            gv[e] = (e0 + e < E) ? __ldg(reinterpret_cast<const uint4*>(gate + static_cast<size_t>(e0 + e) * H + k0))
+                                 : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            double xd[kRouteTB], gd[kRouteEB];
+#pragma unroll
+            for (int t = 0; t < kRouteTB; ++t) {
+                const uint32_t w = (&xv[t].x)[q >> 1];
+                xd[t] = bits_to_f64((q & 1) ? (w >> 16) : (w & 0xFFFFu));
+            }
+#pragma unroll
+            for (int e = 0; e < kRouteEB; ++e) {
+                const uint32_t w = (&gv[e].x)[q >> 1];
+                gd[e] = bits_to_f64((q & 1) ? (w >> 16) : (w & 0xFFFFu));
+            }
+#pragma unroll
+            for (int t = 0; t < kRouteTB; ++t)
+#pragma unroll
+                for (int e = 0; e < kRouteEB; ++e) acc[t * kRouteEB + e] = fma(xd[t], gd[e], acc[t * kRouteEB + e]);
+        }
+    }
+    // transpose-reduce 64 partial sums over 32 lanes: lane l keeps outputs 2l, 2l+1
+#pragma unroll
+    for (int step = 0; step < 5; ++step) {
+        const int mask = 16 >> step;
+        const int half = 32 >> step;
+        const bool upper = (lane & mask) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const double send = upper ? acc[i] : acc[i + half];
+            const double keep = upper ? acc[i + half] : acc[i];
+            acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
+        }
+    }
+    s_part[warp][2 * lane] = acc[0];
+    s_part[warp][2 * lane + 1] = acc[1];
+    __syncthreads();
+    if (threadIdx.x < kRouteTB * kRouteEB) {
+        const int o = static_cast<int>(threadIdx.x);
+        double sum = s_part[0][o];
+#pragma unroll
+        for (int w = 1; w < kRouteWarps; ++w) sum += s_part[w][o];
+        const int t = t0 + o / kRouteEB;
+        const int e = e0 + o % kRouteEB;
+        if (t < T && e < E) logits[static_cast<size_t>(t) * E + e] = f64_to_bf16_bits(sum);
+    }
+    if (!tail.enabled) return;
+    // ---- fused tail: the last CTA to finish routes and packs every token ----
+    __shared__ unsigned int s_ticket;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_ticket = atomicAdd(tail.ticket, 1u);
+    __syncthreads();
+    if (s_ticket != gridDim.x - 1) return;
+    __threadfence();
+    const int nwarps = static_cast<int>(blockDim.x >> 5);
+    topk_rows_dispatch(logits, T, E, tail.k, tail.normalize != 0, tail.selected, tail.weights, warp, nwarps);
+    if (!tail.do_pack) return;
+    __threadfence_block();
+    __syncthreads();
+    extern __shared__ int smem_i[];
+    int* hist = smem_i;
+    int* excl = hist + E;
+    int* warp_hist = excl + E + 1;
+    block_pack_all(tail.selected, tail.weights, T, tail.k, E, hist, excl, warp_hist, tail.pack);
+}
+
+// Softmax + top-k + renormalisation, one warp per token.
+__global__ void __launch_bounds__(256) k_topk(const uint16_t* __restrict__ logits, int T, int E, int k,
+                                              int normalize, int64_t* __restrict__ selected,
+                                              uint16_t* __restrict__ weights) {
+    const int warps = static_cast<int>(blockDim.x >> 5);
+    const int first = static_cast<int>(blockIdx.x) * warps + static_cast<int>(threadIdx.x >> 5);
+    topk_rows_dispatch(logits, T, E, k, normalize != 0, selected, weights, first, gridDim.x * warps);
+}
+
+}  // namespace pdx

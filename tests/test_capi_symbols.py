@@ -1,0 +1,80 @@
+"""CPU checks of the C-ABI library: it loads, exports every declared symbol,
+and rejects invalid arguments before touching a device."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_functions():
+    text = (ROOT / "include" / "pdx_moe.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(pdx_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_path():
+    names = declared_functions()
+    for required in ("pdx_route_topk", "pdx_topk_from_logits", "pdx_pack", "pdx_gather_rows",
+                     "pdx_moe_ffn_grouped", "pdx_expert_ffn", "pdx_combine", "pdx_moe_layer",
+                     "pdx_device_error", "pdx_last_error"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    from pdscope_b200 import _lib
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+    # the binding table covers the header exactly
+    assert set(_lib.SIGNATURES) == set(declared_functions())
+    assert _lib.lib.pdx_abi_version() == _lib.ABI_VERSION
+
+
+def test_workspace_queries_are_monotone():
+    from pdscope_b200._lib import lib
+    a = lib.pdx_layer_workspace_bytes(1, 2048, 128, 8, 768, 0)
+    b = lib.pdx_layer_workspace_bytes(512, 2048, 128, 8, 768, 0)
+    c = lib.pdx_layer_workspace_bytes(512, 2048, 128, 8, 768, 2)
+    assert 0 < a < b <= c
+    assert lib.pdx_pack_workspace_bytes(4096, 8, 128) >= 8 * 128 * 4
+    assert lib.pdx_route_workspace_bytes(64, 128) >= 64 * 128 * 2
+
+
+def test_validation_errors_without_device():
+    """Contract violations return PDX_ERR_INVALID (the reference's ValueError)."""
+    from pdscope_b200 import _lib
+    lib = _lib.lib
+    null = ctypes.c_void_p(0)
+    # T = 0: 'empty expert routing'
+    st = lib.pdx_route_topk(null, null, 0, 2048, 128, 8, 1, null, null, null, null, 0, null)
+    assert st == _lib.PDX_ERR_INVALID and "empty" in _lib.last_error()
+    # top_k > E: 'invalid routing parameters'
+    st = lib.pdx_route_topk(null, null, 4, 2048, 8, 9, 1, null, null, null, null, 0, null)
+    assert st == _lib.PDX_ERR_INVALID and "routing parameters" in _lib.last_error()
+    # top_k beyond the kernels' range is UNSUPPORTED, not silently wrong
+    st = lib.pdx_route_topk(null, null, 4, 2048, 128, 33, 1, null, null, null, null, 0, null)
+    assert st == _lib.PDX_ERR_UNSUPPORTED
+    with pytest.raises(ValueError):
+        _lib.check(_lib.PDX_ERR_INVALID)
+    # pack with null outputs
+    st = lib.pdx_pack(null, null, 4, 8, 128, null, null, null, null, null, null, null, null, 0, null)
+    assert st == _lib.PDX_ERR_INVALID
+    # combine with top_k = 0
+    st = lib.pdx_combine(null, null, null, 4, 0, 2048, null, null, null)
+    assert st == _lib.PDX_ERR_INVALID
+    # layer: unsupported hidden size for the tcgen05 path
+    w = _lib.ExpertWeights()
+    st = lib.pdx_moe_layer(null, null, 4, 2040, 128, 8, 1, ctypes.byref(w), 768, null, null, null, null, null,
+                           null, 2, null, 0, null)
+    assert st in (_lib.PDX_ERR_UNSUPPORTED, _lib.PDX_ERR_INVALID)
+
+
+def test_expert_ffn_rejects_empty_input():
+    from pdscope_b200 import _lib
+    null = ctypes.c_void_p(0)
+    st = _lib.lib.pdx_expert_ffn(ctypes.c_void_p(16), 0, ctypes.c_void_p(16), ctypes.c_void_p(16),
+                                 ctypes.c_void_p(16), 2048, 768, ctypes.c_void_p(16), null, 0, null)
+    assert st == _lib.PDX_ERR_INVALID

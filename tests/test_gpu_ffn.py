@@ -1,0 +1,134 @@
+"""GPU parity of the expert FFN (expert_forward, qwen.py:87-90): streaming GEMV
+(decode) and tcgen05 grouped GEMM (prefill) against the oracle.
+
+Tolerance: BF16 outputs within rtol 2e-2 / atol 2e-2 of the oracle's BF16
+restatement, and FP32-accumulate relative L2 <= 0.02 against reference_fp32
+(the reference's own bound, pdscope_compare.py:692-695)."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as mo
+
+pytestmark = pytest.mark.gpu
+
+RTOL = ATOL = 2e-2
+
+
+@pytest.fixture(scope="module")
+def pdx():
+    import pdscope_b200
+    return pdscope_b200
+
+
+def _expert(seed, hidden, inter):
+    rng = np.random.default_rng(seed)
+    g = mo.f32_to_bf16(rng.standard_normal((inter, hidden), dtype=np.float32) * 0.02)
+    u = mo.f32_to_bf16(rng.standard_normal((inter, hidden), dtype=np.float32) * 0.02)
+    d = mo.f32_to_bf16(rng.standard_normal((hidden, inter), dtype=np.float32) * 0.02)
+    return g, u, d
+
+
+def _check_rows(actual_bits, x, g, u, d):
+    exp = mo.expert_forward(x, g, u, d)
+    a = mo.bf16_to_f32(actual_bits)
+    np.testing.assert_allclose(a, mo.bf16_to_f32(exp), rtol=RTOL, atol=ATOL)
+    ref32 = mo.reference_fp32(x, g, u, d)
+    assert mo.error_metrics(a, ref32)["relative_l2"] <= 0.02
+    # nearly all elements bit-identical to the BF16 restatement
+    return (actual_bits == exp).mean()
+
+
+@pytest.mark.parametrize("n", (1, 3, 8, 9, 64, 65, 200, 1000))
+@pytest.mark.parametrize("shape", ((256, 128), (2048, 768)))
+def test_expert_forward(pdx, n, shape):
+    from tests.gpu_util import to_bits, to_dev
+    hidden, inter = shape
+    g, u, d = _expert(n + hidden, hidden, inter)
+    x = mo.f32_to_bf16(np.random.default_rng(n).standard_normal((n, hidden), dtype=np.float32))
+    y = pdx.expert_forward(to_dev(x), dict(gate_proj=to_dev(g), up_proj=to_dev(u), down_proj=to_dev(d)))
+    frac = _check_rows(to_bits(y), x, g, u, d)
+    assert frac > 0.9
+
+
+def test_expert_forward_vs_torch_on_device(pdx):
+    """Against the reference's own GPU expert_forward (cuBLAS) on the B200."""
+    from tests.gpu_util import f32, to_dev, torch_expert_forward
+    g, u, d = _expert(5, 2048, 768)
+    for n in (1, 7, 300):
+        x = to_dev(mo.f32_to_bf16(np.random.default_rng(n).standard_normal((n, 2048), dtype=np.float32)))
+        gd, ud, dd = to_dev(g), to_dev(u), to_dev(d)
+        ours = pdx.expert_forward(x, dict(gate_proj=gd, up_proj=ud, down_proj=dd))
+        ref = torch_expert_forward(x, gd, ud, dd)
+        np.testing.assert_allclose(f32(ours), f32(ref), rtol=RTOL, atol=ATOL)
+
+
+def _grouped_case(pdx, tokens, experts, k, hidden, inter, mode, seed, slot_perm=False):
+    from tests.gpu_util import to_bits, to_dev
+    from pdscope_b200 import _lib
+    from pdscope_b200.runtime import ExpertSlab
+    x, gate, wg, wu, wd = mo.synthetic_layer(seed, tokens, hidden, experts, inter)
+    _, sel, w = mo.route(x, gate, k, True)
+    packed = mo.compact_expert_groups(sel, w, experts)
+    slab = ExpertSlab.from_tensors([dict(gate_proj=to_dev(wg[e]), up_proj=to_dev(wu[e]), down_proj=to_dev(wd[e]))
+                                    for e in range(experts)])
+    slot_of = None
+    if slot_perm:  # experts stored in a shuffled slot order, as a cache ledger would
+        perm = np.random.default_rng(seed).permutation(experts)
+        order = np.argsort(perm)  # slot s holds expert perm[s]
+        storage = slab.storage.view(experts, -1)[torch.from_numpy(perm).cuda()].contiguous()
+        slot_of = torch.from_numpy(order.astype(np.int32)).cuda()
+        slab = ExpertSlab(storage.view(-1), hidden, inter, slot_of_expert=slot_of)
+    rows = tokens * k
+    y = torch.empty((rows, hidden), dtype=torch.bfloat16, device="cuda")
+    dev = {key: torch.from_numpy(packed[key]).cuda() for key in ("tokens", "offsets")}
+    nz = np.nonzero(packed["counts"])[0]
+    active = torch.from_numpy(np.concatenate([[len(nz)], nz, np.zeros(experts - len(nz), int)]).astype(np.int32)).cuda()
+    ws_bytes = _lib.lib.pdx_ffn_workspace_bytes(rows, hidden, inter, mode)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    xd = to_dev(x)
+    _lib.check(_lib.lib.pdx_moe_ffn_grouped(
+        ctypes.c_void_p(xd.data_ptr()), tokens, ctypes.c_void_p(dev["tokens"].data_ptr()),
+        ctypes.c_void_p(dev["offsets"].data_ptr()), ctypes.c_void_p(active.data_ptr()), experts, rows,
+        ctypes.byref(slab.struct), hidden, inter, ctypes.c_void_p(y.data_ptr()), mode,
+        ctypes.c_void_p(ws.data_ptr()), ws.numel(), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    assert _lib.device_error(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+    got = to_bits(y)
+    exp = np.zeros_like(got)
+    off = packed["offsets"]
+    for e in nz:
+        a, b = off[e], off[e + 1]
+        exp[a:b] = mo.expert_forward(x[packed["tokens"][a:b]], wg[e], wu[e], wd[e])
+    np.testing.assert_allclose(mo.bf16_to_f32(got), mo.bf16_to_f32(exp), rtol=RTOL, atol=ATOL)
+    assert (got == exp).mean() > 0.9
+    return got
+
+
+@pytest.mark.parametrize("mode", (1, 2))
+@pytest.mark.parametrize("tokens", (1, 5, 64, 300))
+def test_grouped_ffn_small_shape(pdx, mode, tokens):
+    _grouped_case(pdx, tokens, 16, 4, 256, 128, mode, 100 + tokens)
+
+
+@pytest.mark.parametrize("mode", (1, 2))
+def test_grouped_ffn_slot_mapping(pdx, mode):
+    """Experts located through slot_of_expert (the executor's cache-slot ledger)."""
+    a = _grouped_case(pdx, 40, 16, 4, 256, 128, mode, 7, slot_perm=False)
+    b = _grouped_case(pdx, 40, 16, 4, 256, 128, mode, 7, slot_perm=True)
+    assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("mode,tokens", ((1, 1), (1, 64), (2, 130), (2, 512)))
+def test_grouped_ffn_qwen3_shape(pdx, mode, tokens):
+    _grouped_case(pdx, tokens, 128, 8, 2048, 768, mode, 200 + tokens)
+
+
+def test_gemv_and_gemm_agree(pdx):
+    """The two FFN paths are independent implementations of the same rows."""
+    a = _grouped_case(pdx, 96, 32, 8, 512, 256, 1, 31)
+    b = _grouped_case(pdx, 96, 32, 8, 512, 256, 2, 31)
+    diff = np.abs(mo.bf16_to_f32(a) - mo.bf16_to_f32(b))
+    assert diff.max() <= 2e-2
