@@ -1,0 +1,400 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 MoE expert path (PDScope per-layer expert execution).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl pdx|reference]
+
+Workload (synthetic seeded data, random-init weights):
+  * headline ``value``: config 2 -- a 48-layer Qwen3-30B-A3B-shaped MoE stack
+    (H=2048, E=128, I=768, top-8; all 6144 experts resident in HBM) decoding a
+    batch of 64 tokens; one step = all 48 layers (route, pack, grouped FFN,
+    combine) replayed from one CUDA graph.  Expert weights streamed per step
+    (~3.6 GB) far exceed the 126 MB L2, so no L2 flush is needed.
+  * also reported: decode at batch 1 and 8, and config 3 -- a ragged prefill of
+    8 sequences (lengths ~U[256, 4096], seeded) through the same 48 layers with a
+    Zipf(1.1) router skew.
+  * ``e2e``: the same decode step through the public stack API with the input
+    copied host->device from pinned memory and the output copied back every step.
+  * ``roofline``: the grouped expert FFN (k_gateup_gemv + k_down_gemv) timed on
+    its own stream with CUDA events; algorithmic bytes = active experts x
+    9,437,184 B + activation rows.
+  * ``cpu_baseline``: the reference's CPU layer path (oracle/cpu_path.py, torch
+    CPU ops) on this host's cores, a bounded sample of layers.
+Multi-GPU (N>1): one process per GPU, each a full replica of the stack serving
+its own batch (weak scaling); value = tokens of all ranks / max-over-ranks time.
+
+``--impl reference`` times the reference's own CPU implementation of the path
+(the torch-CPU restatement in oracle/cpu_path.py) on all host cores and prints
+the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode & prefill tok/s, Qwen3-30B-A3B-shape MoE, 1–8 B200; % HBM/tensor roofline"
+CFG = dict(hidden=2048, experts=128, inter=768, top_k=8, layers=48)
+EXPERT_BYTES = 3 * CFG["hidden"] * CFG["inter"] * 2          # 9,437,184
+FLOPS_PER_ROW = 6 * CFG["hidden"] * CFG["inter"]              # 9,437,184 (x2 flops, 3 matmuls)
+FALLBACK_PEAKS = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0)
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("pdx", "reference"), default="pdx")
+    ap.add_argument("--layers", type=int, default=CFG["layers"])
+    ap.add_argument("--decode-batch", type=int, default=64)
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--prefill-steps", type=int, default=3)
+    ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU baseline sample")
+    ap.add_argument("--cpu-threads", type=int, default=0, help="0 = all usable cores")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return dict(hbm_gbs=float(d["hbm_gbs"]), bf16_tflops=float(d["bf16_tflops"]),
+                    bf16_tflops_sustained=float(d["bf16_tflops_sustained"]), source="measured")
+    return dict(FALLBACK_PEAKS, source="fallback")
+
+
+def usable_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ----------------------------------------------------------------------------
+# clocks during the timed region
+# ----------------------------------------------------------------------------
+REASON_FIELDS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+
+class ClockSampler:
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = Path(f"/tmp/pdx_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None or not self.path.exists():
+            return dict(sm_mhz=None, sm_max_mhz=None, reasons=["nvidia-smi unavailable"], samples=0)
+        sm, smax, power, reasons = [], None, [], set()
+        for line in self.path.read_text().splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for name, val in zip(REASON_FIELDS, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        self.path.unlink(missing_ok=True)
+        return dict(sm_mhz=statistics.median(sm) if sm else None, sm_max_mhz=smax,
+                    power_w_max=max(power) if power else None, reasons=sorted(reasons), samples=len(sm))
+
+
+# ----------------------------------------------------------------------------
+# CPU baseline (reference CPU path, oracle/cpu_path.py)
+# ----------------------------------------------------------------------------
+
+
+def cpu_baseline(tokens, layers, threads, steps=1):
+    from oracle import cpu_path
+    import torch
+    cores = threads or usable_cores()
+    sample = [cpu_path.make_layer(CFG["hidden"], CFG["experts"], CFG["inter"], seed=100 + i) for i in range(layers)]
+    cpu_path.time_layers(sample[:1], tokens, CFG["hidden"], cores, repeats=1)  # warm
+    per_layer, active = cpu_path.time_layers(sample, tokens, CFG["hidden"], cores, repeats=steps)
+    tok_s = tokens / (per_layer * CFG["layers"])
+    try:
+        model = next((l.split(":", 1)[1].strip() for l in open("/proc/cpuinfo") if l.startswith("model name")), "")
+    except OSError:
+        model = ""
+    return dict(value=tok_s, unit="tok/s", cores=cores, kind="port",
+                sample=(f"{layers} random-init Qwen3-30B-A3B layers x {steps} pass(es) at decode batch {tokens}, "
+                        f"torch CPU route/compact_expert_groups/expert_forward/index_add_ "
+                        f"(oracle/cpu_path.py); {per_layer * 1e3:.1f} ms/layer, scaled to 48 layers; "
+                        f"mean active experts {statistics.mean(active):.1f}; cpu '{model}'"),
+                ms_per_layer=per_layer * 1e3, torch_threads=torch.get_num_threads())
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return 0
+    steps = max(1, args.steps)
+    warm = max(0, args.warmup)
+    from oracle import cpu_path
+    cores = args.cpu_threads or usable_cores()
+    sample = [cpu_path.make_layer(CFG["hidden"], CFG["experts"], CFG["inter"], seed=100 + i)
+              for i in range(max(1, args.cpu_layers))]
+    t_count = args.decode_batch
+    for _ in range(min(warm, 1)):
+        cpu_path.time_layers(sample[:1], t_count, CFG["hidden"], cores, repeats=1)
+    t0 = time.perf_counter()
+    per_layer_all = []
+    for s in range(steps):
+        per_layer, _ = cpu_path.time_layers(sample[:1], t_count, CFG["hidden"], cores, repeats=1, seed=s)
+        per_layer_all.append(per_layer)
+    elapsed = time.perf_counter() - t0
+    per_layer = statistics.mean(per_layer_all)
+    value = t_count / (per_layer * CFG["layers"])
+    line = dict(metric=METRIC, value=value, unit="tok/s", impl="reference", n_gpus=args.gpus, steps=steps,
+                warmup=warm, ms_per_step=per_layer * CFG["layers"] * 1e3, higher_is_better=True, scaling="weak",
+                vs_baseline=None, dtype="bf16", data="synthetic",
+                config=dict(workload=f"config2 decode batch {t_count}: 48-layer Qwen3-30B-A3B-shape MoE stack",
+                            hidden=CFG["hidden"], experts=CFG["experts"], inter=CFG["inter"], top_k=CFG["top_k"],
+                            layers=CFG["layers"], decode_batch=t_count, parallelism="cpu"),
+                cpu_baseline=dict(value=value, unit="tok/s", cores=cores, kind="port",
+                                  sample=(f"each step = 1 random-init layer at batch {t_count} on the reference's "
+                                          f"CPU path (torch CPU, oracle/cpu_path.py), scaled to 48 layers; "
+                                          f"wall {elapsed:.1f}s")),
+                e2e=dict(value=value, unit="tok/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------
+# GPU benchmark
+# ----------------------------------------------------------------------------
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from pdscope_b200 import _lib
+    from pdscope_b200.stack import (ResidentMoEStack, activations, build_stack, prefill_lengths, ZIPF_ALPHA,
+                                    ZIPF_S)
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    K, W = max(1, args.steps), max(3, args.warmup)
+    pk = peaks()
+    L = args.layers
+    stack = build_stack(L, CFG["hidden"], CFG["experts"], CFG["inter"], CFG["top_k"], device=dev, seed=rank)
+    torch.cuda.synchronize(dev)
+
+    def timed(fn, steps, warm, sampler=None):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize(dev)
+        barrier()
+        torch.cuda.synchronize(dev)
+        s = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(steps):
+            fn()
+        e1.record(s)
+        torch.cuda.synchronize(dev)
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1))
+
+    def active_per_layer(t_count):
+        b = stack.buffers(t_count)
+        return [int((st.counts > 0).sum().item()) for st in b["stages"]]
+
+    # ---- decode: batches 1, 8 and the headline batch --------------------------------
+    decode = {}
+    headline_t = args.decode_batch
+    for t_count in sorted({1, 8, headline_t}):
+        stack.input(t_count).copy_(activations(t_count, CFG["hidden"], device=dev, seed=10 + t_count + 1000 * rank))
+        launches0 = _lib.lib.pdx_launch_count()
+        stack.step(t_count)  # capture (counts the kernels of one step)
+        torch.cuda.synchronize(dev)
+        launches_per_step = (_lib.lib.pdx_launch_count() - launches0) // 2  # warm call + captured call
+        sampler = ClockSampler(local_rank) if t_count == headline_t else None
+        if sampler:
+            with sampler:
+                ms = timed(lambda: stack.step(t_count), K, W)
+            clocks = sampler.summary()
+        else:
+            ms = timed(lambda: stack.step(t_count), K, W)
+            clocks = None
+        act = active_per_layer(t_count)
+        decode[t_count] = dict(ms_per_step=ms / K, tok_s=sum_over_ranks(t_count) * K / (ms / 1e3),
+                               active_experts_per_layer=statistics.mean(act),
+                               weight_gb_per_step=sum(act) * EXPERT_BYTES / 1e9,
+                               launches_per_step=launches_per_step, clocks=clocks)
+        decode[t_count]["hbm_gbs_step"] = decode[t_count]["weight_gb_per_step"] / (decode[t_count]["ms_per_step"] / 1e3)
+
+    # ---- roofline of the dominant kernel: grouped FFN GEMV at the headline batch ----
+    t_count = headline_t
+    stack.stage_once(t_count)
+    g = stack.ffn_graph(t_count)
+    ffn_ms = timed(g.replay, K, W)
+    act = active_per_layer(t_count)
+    n_rows = t_count * CFG["top_k"]
+    act_bytes = t_count * CFG["hidden"] * 2 + n_rows * CFG["inter"] * 2 * 2 + n_rows * CFG["hidden"] * 2
+    bytes_per_launch = statistics.mean(act) * EXPERT_BYTES + act_bytes
+    per_launch_s = ffn_ms / 1e3 / (K * L)
+    achieved = bytes_per_launch / per_launch_s / 1e9
+    traffic = None
+    tj = ROOT / "profiles" / "traffic.json"
+    if tj.exists():
+        d = json.loads(tj.read_text()).get("decode_ffn")
+        if d:
+            traffic = d["dram_bytes_per_active_expert"] * statistics.mean(act)
+    roofline = dict(bound="hbm", kernel="pdx_moe_ffn_grouped GEMV (k_gateup_gemv + k_down_gemv)",
+                    achieved=achieved, peak=pk["hbm_gbs"], unit="GB/s", frac=achieved / pk["hbm_gbs"],
+                    peak_source=pk["source"], frac_of_8000_nominal=achieved / 8000.0, traffic=traffic,
+                    bytes_per_launch=bytes_per_launch, us_per_launch=per_launch_s * 1e6)
+
+    # ---- prefill (config 3): ragged 8-sequence batch, Zipf router skew -----------------
+    prefill = None
+    if not args.no_prefill:
+        lengths = prefill_lengths(8, seed=rank)
+        tp = sum(lengths)
+        zgates = []
+        gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+        for l in range(L):
+            gte = stack.gates[l].clone()
+            perm = torch.randperm(CFG["experts"], device=dev, generator=gen)
+            ranks = torch.empty(CFG["experts"], device=dev)
+            ranks[perm] = torch.arange(1, CFG["experts"] + 1, device=dev, dtype=torch.float32)
+            gte[:, 0] = (-ZIPF_ALPHA * ZIPF_S * torch.log(ranks)).to(torch.bfloat16)
+            zgates.append(gte)
+        pstack = ResidentMoEStack(zgates, stack.slabs, top_k=CFG["top_k"])
+        pstack.input(tp).copy_(activations(tp, CFG["hidden"], device=dev, seed=77 + rank, zipf=True))
+        stack.release_graphs()
+        pstack.step(tp)
+        pk_steps = max(1, args.prefill_steps)
+        ms = timed(lambda: pstack.step(tp), pk_steps, 1)
+        b = pstack.buffers(tp)
+        c0 = b["stages"][0].counts.float()
+        top16 = float(torch.topk(c0, 16).values.sum() / c0.sum())
+        pstack.stage_once(tp)
+        gp = pstack.ffn_graph(tp)
+        ffn_ms_p = timed(gp.replay, pk_steps, 1)
+        flops_launch = tp * CFG["top_k"] * FLOPS_PER_ROW
+        per_launch_p = ffn_ms_p / 1e3 / (pk_steps * L)
+        tflops = flops_launch / per_launch_p / 1e12
+        prefill = dict(tokens=tp, lengths=lengths, ms_per_step=ms / pk_steps,
+                       tok_s=sum_over_ranks(tp) * pk_steps / (ms / 1e3), top16_share_layer0=top16,
+                       zipf=dict(s=ZIPF_S, alpha=ZIPF_ALPHA),
+                       roofline=dict(bound="tensor", kernel="pdx_moe_ffn_grouped tcgen05 (gather + 2x k_grouped_gemm)",
+                                     achieved=tflops, unit="TFLOP/s", peak=pk["bf16_tflops_sustained"],
+                                     frac=tflops / pk["bf16_tflops_sustained"],
+                                     frac_of_burst=tflops / pk["bf16_tflops"], peak_source=pk["source"],
+                                     flops_per_launch=flops_launch, us_per_launch=per_launch_p * 1e6))
+        pstack.release_graphs()
+        del pstack
+
+    # ---- e2e: public API with host buffers (pinned H2D in, D2H out) --------------------
+    t_count = headline_t
+    host_in = activations(t_count, CFG["hidden"], device=dev, seed=5).cpu().pin_memory()
+    host_out = torch.empty((t_count, CFG["hidden"]), dtype=torch.bfloat16).pin_memory()
+    x_dev, y_dev = stack.input(t_count), stack.output(t_count)
+
+    def e2e_step():
+        x_dev.copy_(host_in, non_blocking=True)
+        stack.step(t_count)
+        host_out.copy_(y_dev, non_blocking=True)
+
+    e2e_ms = timed(e2e_step, K, W)
+    e2e = dict(value=sum_over_ranks(t_count) * K / (e2e_ms / 1e3), unit="tok/s",
+               h2d_bytes_per_step=host_in.numel() * 2, d2h_bytes_per_step=host_out.numel() * 2,
+               ms_per_step=e2e_ms / K)
+
+    # ---- CPU baseline (rank 0, N = 1 only) -------------------------------------------
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(headline_t, args.cpu_layers, args.cpu_threads)
+
+    stack.release_graphs()
+    if rank == 0:
+        d = decode[headline_t]
+        line = dict(metric=METRIC, value=d["tok_s"], unit="tok/s", n_gpus=world, steps=K, warmup=W,
+                    ms_per_step=d["ms_per_step"], higher_is_better=True, scaling="weak", vs_baseline=None,
+                    dtype="bf16", data="synthetic",
+                    config=dict(workload=f"config2 decode batch {headline_t}: 48-layer Qwen3-30B-A3B-shape MoE "
+                                         f"stack, all experts resident, one CUDA graph per step",
+                                hidden=CFG["hidden"], experts=CFG["experts"], inter=CFG["inter"],
+                                top_k=CFG["top_k"], layers=L, decode_batch=headline_t,
+                                global_batch=headline_t * world,
+                                parallelism=f"replicas{world}" if world > 1 else "single",
+                                l2="not flushed: each step streams ~%.1f GB of expert weights (> 126 MB L2)"
+                                   % d["weight_gb_per_step"]),
+                    roofline=roofline, cpu_baseline=cpu, e2e=e2e, clocks=d["clocks"],
+                    gpu_launches=d["launches_per_step"] * K,
+                    decode={str(t): {k: v for k, v in r.items() if k != "clocks"} for t, r in decode.items()},
+                    prefill=prefill)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

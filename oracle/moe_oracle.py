@@ -34,9 +34,10 @@ Rounding contract (why each step is written the way it is):
   order exactly; only ``exp`` itself comes from numpy instead of CUDA's
   ``expf`` (both are within 2 ulp, so the BF16 routing weights can differ by
   one BF16 ulp in rare cases).
-* Top-k.  ``torch.topk`` on CUDA orders by value descending and, among equal
-  values, by lower expert index first (both at the k boundary and inside the
-  selected set).  The oracle uses exactly that key.
+* Top-k.  ``torch.topk`` on CUDA selects by value descending, lower expert
+  index winning a tie at the k boundary, and returns equal values inside the
+  selection in descending index order (pinned on the B200).  The oracle
+  reproduces both rules (``topk_torch_cuda``).
 * Renormalisation.  ``weights.sum(-1)`` over k FP32 values uses PyTorch's
   reduction tree (``block_x_reduce``: lanes of width ``last_pow2(k)``, each
   lane summing its strided elements, then shfl_down with offsets 1, 2, 4 ...).
@@ -143,12 +144,21 @@ def softmax_fp32(logit_bits):
     return probs[:, :e_count]
 
 
-def topk_desc_lowindex(values, k):
-    """torch.topk(values, k) on CUDA: value desc, ties -> lower index first."""
+def topk_torch_cuda(values, k):
+    """torch.topk(values, k) as it behaves on CUDA (pinned on the B200).
+
+    The selected set is ordered by value descending with lower indices winning
+    a tie that straddles the k boundary; inside the returned (sorted) set,
+    equal values appear in DESCENDING index order (e.g. values
+    [.1,.5,.3,.5,.3,.5,.2,.3], k=5 -> indices [5,3,1,4,2]).
+    """
     t_count, e_count = values.shape
     idx = np.broadcast_to(np.arange(e_count), values.shape)
-    order = np.lexsort((idx, -values.astype(np.float64)), axis=-1)[:, :k]
-    return np.take_along_axis(values, order, axis=1), order.astype(np.int64)
+    chosen = np.lexsort((idx, -values.astype(np.float64)), axis=-1)[:, :k]
+    cv = np.take_along_axis(values, chosen, axis=1)
+    order = np.lexsort((-chosen, -cv.astype(np.float64)), axis=-1)
+    sel = np.take_along_axis(chosen, order, axis=1)
+    return np.take_along_axis(values, sel, axis=1), sel.astype(np.int64)
 
 
 def torch_sum_lastdim(v):
@@ -185,7 +195,7 @@ def route_from_logits(logit_bits, top_k, normalize):
     if not 0 < top_k <= logit_bits.shape[1]:
         raise ValueError("invalid routing parameters")
     probs = softmax_fp32(logit_bits)
-    weights, selected = topk_desc_lowindex(probs, top_k)
+    weights, selected = topk_torch_cuda(probs, top_k)
     if normalize:
         denom = torch_sum_lastdim(weights)
         weights = (weights / denom[:, None]).astype(np.float32)

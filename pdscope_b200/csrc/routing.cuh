@@ -16,8 +16,9 @@ namespace pdx {
 //    max and the sum use an xor butterfly (offsets 16..1); each lane sums its
 //    own elements in i order; p = exp(x - max) / sum with IEEE division and
 //    CUDA's expf (the same function the reference's kernel calls).
-//  * torch.topk(p, k): value descending, equal values -> lower expert index,
-//    both at the k boundary and inside the selected set.
+//  * torch.topk(p, k): value descending; a tie straddling the k boundary is
+//    won by the lower expert index; inside the returned set equal values are
+//    in descending index order (behaviour of the CUDA kernel, pinned on B200).
 //  * w / w.sum(-1): PyTorch's small-row reduction tree (block_x_reduce) -- lane
 //    j < width = last_pow2(k) holds w_j + w_{j+width}, then shfl_down by
 //    1, 2, 4, ...; lane 0's total divides every weight; result RNE to BF16.
@@ -88,9 +89,18 @@ __device__ __forceinline__ void warp_softmax_topk(const uint16_t* __restrict__ l
         const float denom = __shfl_sync(0xffffffffu, a, 0);
         w = __fdiv_rn(my_p, denom);
     }
+    // torch.topk on CUDA returns equal values in descending index order: place
+    // each selected expert by (p descending, index descending).  Tied entries
+    // carry equal weights, so the renormalisation sum above is unaffected.
+    int pos = 0;
+    for (int j = 0; j < k; ++j) {
+        const float pj = __shfl_sync(0xffffffffu, my_p, j);
+        const int ij = __shfl_sync(0xffffffffu, my_idx, j);
+        if (pj > my_p || (pj == my_p && ij > my_idx)) ++pos;
+    }
     if (static_cast<int>(lane) < k) {
-        sel_out[lane] = my_idx;
-        w_out[lane] = f2bits(w);
+        sel_out[pos] = my_idx;
+        w_out[pos] = f2bits(w);
     }
 }
 

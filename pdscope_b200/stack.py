@@ -1,0 +1,231 @@
+"""A stack of HBM-resident MoE layers driven as one decode/prefill step.
+
+``ResidentMoEStack`` owns every buffer a step needs (no allocation inside a
+step) and can capture the whole multi-layer step as one CUDA graph, so the
+per-layer host work of the reference (``.tolist()`` syncs in grouping,
+pdscope_runtime.py:26, qwen.py:162,171, and one Python call chain per expert)
+disappears from the step.  The activation of layer l+1 is
+``out_l = x_l + MoE_l(x_l)`` (residual fused into the combine kernel).
+
+Also here: seeded synthetic workloads standing in for the BASELINE configs
+(weights ~N(0, 0.02), activations ~N(0, 1); no checkpoint or dataset is used).
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import check, lib
+from .runtime import ExpertSlab, _ptr, _stream
+
+
+@dataclass
+class StageBuffers:
+    """Per-layer device buffers of the staged (route / pack / FFN / combine) path."""
+    logits: torch.Tensor
+    selected: torch.Tensor
+    weights: torch.Tensor
+    counts: torch.Tensor
+    offsets: torch.Tensor
+    tokens: torch.Tensor
+    positions: torch.Tensor
+    packed_w: torch.Tensor
+    inverse: torch.Tensor
+    active: torch.Tensor
+
+
+class ResidentMoEStack:
+    """``layers`` MoE layers with all experts resident; one slab per layer."""
+
+    def __init__(self, gates, slabs, top_k=8, normalize=True):
+        if len(gates) != len(slabs) or not gates:
+            raise ValueError("one router per expert slab is required")
+        self.gates, self.slabs = list(gates), list(slabs)
+        self.experts, self.hidden = self.gates[0].shape
+        self.inter = self.slabs[0].inter
+        self.top_k, self.normalize = top_k, normalize
+        self.device = self.gates[0].device
+        self._graphs = {}
+        self._bufs = {}
+
+    @property
+    def num_layers(self):
+        return len(self.gates)
+
+    # -- buffers ----------------------------------------------------------------
+    def buffers(self, t_count, mode=_lib.FFN_AUTO):
+        key = (t_count, mode)
+        b = self._bufs.get(key)
+        if b is not None:
+            return b
+        dev, L, E, H, k = self.device, self.num_layers, self.experts, self.hidden, self.top_k
+        bf, i32 = dict(dtype=torch.bfloat16, device=dev), dict(dtype=torch.int32, device=dev)
+        # acts[0] is the step input (never overwritten); layers alternate acts[1], acts[2]
+        acts = [torch.zeros((t_count, H), **bf) for _ in range(3)]
+        n = t_count * k
+        stages = [StageBuffers(logits=torch.empty((t_count, E), **bf),
+                               selected=torch.empty((t_count, k), dtype=torch.int64, device=dev),
+                               weights=torch.empty((t_count, k), **bf), counts=torch.empty(E, **i32),
+                               offsets=torch.empty(E + 1, **i32), tokens=torch.empty(n, **i32),
+                               positions=torch.empty(n, **i32), packed_w=torch.empty(n, **bf),
+                               inverse=torch.empty(n, **i32), active=torch.empty(E + 1, **i32))
+                  for _ in range(L)]
+        rows = torch.empty((n, H), **bf)  # expert outputs of the current layer (staged path)
+        ws_layer = lib.pdx_layer_workspace_bytes(t_count, H, E, k, self.inter, mode)
+        ws_stage = max(lib.pdx_route_workspace_bytes(t_count, E), lib.pdx_pack_workspace_bytes(t_count, k, E),
+                       lib.pdx_ffn_workspace_bytes(n, H, self.inter, mode))
+        ws = torch.empty(max(ws_layer, ws_stage), dtype=torch.uint8, device=dev)
+        b = dict(acts=acts, stages=stages, ws=ws, rows=rows)
+        self._bufs[key] = b
+        return b
+
+    @staticmethod
+    def _act_in(acts, l):
+        return acts[0] if l == 0 else acts[1 + (l - 1) % 2]
+
+    @staticmethod
+    def _act_out(acts, l):
+        return acts[1 + l % 2]
+
+    # -- fused path: one C-ABI call per layer -------------------------------------
+    def _step_fused(self, t_count, mode):
+        b = self.buffers(t_count, mode)
+        acts, stages, ws = b["acts"], b["stages"], b["ws"]
+        s = _stream()
+        for l in range(self.num_layers):
+            st = stages[l]
+            x_in, x_out = self._act_in(acts, l), self._act_out(acts, l)
+            check(lib.pdx_moe_layer(_ptr(x_in), _ptr(self.gates[l]), t_count, self.hidden, self.experts,
+                                    self.top_k, int(self.normalize), ctypes.byref(self.slabs[l].struct), self.inter,
+                                    _ptr(x_in), _ptr(x_out), _ptr(st.logits), _ptr(st.selected),
+                                    _ptr(st.weights), _ptr(st.counts), mode, _ptr(ws), ws.numel(), s))
+
+    # -- staged path: route, pack, FFN, combine as separate calls --------------------
+    def route_and_pack(self, l, t_count, mode=_lib.FFN_AUTO):
+        b = self.buffers(t_count, mode)
+        st, ws, s = b["stages"][l], b["ws"], _stream()
+        x = self._act_in(b["acts"], l)
+        check(lib.pdx_route_topk(_ptr(x), _ptr(self.gates[l]), t_count, self.hidden, self.experts, self.top_k,
+                                 int(self.normalize), _ptr(st.logits), _ptr(st.selected), _ptr(st.weights),
+                                 _ptr(ws), ws.numel(), s))
+        check(lib.pdx_pack(_ptr(st.selected), _ptr(st.weights), t_count, self.top_k, self.experts, _ptr(st.counts),
+                           _ptr(st.offsets), _ptr(st.tokens), _ptr(st.positions), _ptr(st.packed_w),
+                           _ptr(st.inverse), _ptr(st.active), _ptr(ws), ws.numel(), s))
+
+    def ffn(self, l, t_count, mode=_lib.FFN_AUTO):
+        b = self.buffers(t_count, mode)
+        st, ws = b["stages"][l], b["ws"]
+        n = t_count * self.top_k
+        check(lib.pdx_moe_ffn_grouped(_ptr(self._act_in(b["acts"], l)), t_count, _ptr(st.tokens),
+                                      _ptr(st.offsets), _ptr(st.active), self.experts, n,
+                                      ctypes.byref(self.slabs[l].struct), self.hidden, self.inter, _ptr(b["rows"]),
+                                      mode, _ptr(ws), ws.numel(), _stream()))
+
+    def combine(self, l, t_count, mode=_lib.FFN_AUTO):
+        b = self.buffers(t_count, mode)
+        st = b["stages"][l]
+        x_in, x_out = self._act_in(b["acts"], l), self._act_out(b["acts"], l)
+        check(lib.pdx_combine(_ptr(b["rows"]), _ptr(st.weights), _ptr(st.inverse), t_count, self.top_k,
+                              self.hidden, _ptr(x_in), _ptr(x_out), _stream()))
+
+    def _step_staged(self, t_count, mode):
+        for l in range(self.num_layers):
+            self.route_and_pack(l, t_count, mode)
+            self.ffn(l, t_count, mode)
+            self.combine(l, t_count, mode)
+
+    # -- public step --------------------------------------------------------------------
+    def input(self, t_count, mode=_lib.FFN_AUTO):
+        return self.buffers(t_count, mode)["acts"][0]
+
+    def output(self, t_count, mode=_lib.FFN_AUTO):
+        return self._act_out(self.buffers(t_count, mode)["acts"], self.num_layers - 1)
+
+    def step(self, t_count, mode=_lib.FFN_AUTO, *, graph=True):
+        """Run every layer on ``input(t_count)``; result in ``output(t_count)``."""
+        if not graph:
+            self._step_fused(t_count, mode)
+            return
+        key = ("fused", t_count, mode)
+        g = self._graphs.get(key)
+        if g is None:
+            self._step_fused(t_count, mode)  # warm: device attributes, tensor maps
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._step_fused(t_count, mode)
+            self._graphs[key] = g
+        g.replay()
+
+    def ffn_graph(self, t_count, mode=_lib.FFN_AUTO):
+        """CUDA graph of the grouped FFN of every layer on the current packing."""
+        key = ("ffn", t_count, mode)
+        g = self._graphs.get(key)
+        if g is None:
+            for l in range(self.num_layers):
+                self.ffn(l, t_count, mode)
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for l in range(self.num_layers):
+                    self.ffn(l, t_count, mode)
+            self._graphs[key] = g
+        return g
+
+    def stage_once(self, t_count, mode=_lib.FFN_AUTO):
+        """One staged step (fills every layer's packing for ffn_graph)."""
+        self._step_staged(t_count, mode)
+
+    def release_graphs(self):
+        self._graphs.clear()
+
+
+# ---------------------------------------------------------------------------
+# Synthetic workloads (seeded, no checkpoint or dataset)
+# ---------------------------------------------------------------------------
+
+QWEN3_30B = dict(hidden=2048, experts=128, inter=768, top_k=8, layers=48)
+QWEN3_235B = dict(hidden=4096, experts=128, inter=1536, top_k=8, layers=94)
+
+# Zipf(s=1.1) router skew: a dedicated hidden coordinate carries a constant
+# activation and gate[e, 0] = -ALPHA * s * log(rank_e), so the logits gain a
+# per-expert offset without changing route() itself.
+ZIPF_S = 1.1
+ZIPF_ALPHA = 0.75  # top-16 experts take ~75% of assignments (measured and reported by bench.py)
+
+
+def build_stack(layers, hidden, experts, inter, top_k=8, device="cuda", seed=0, zipf=False):
+    gen = torch.Generator(device=device).manual_seed(seed)
+    gates, slabs = [], []
+    for l in range(layers):
+        gate = torch.randn(experts, hidden, device=device, generator=gen) * 0.02
+        if zipf:
+            perm = torch.randperm(experts, device=device, generator=gen)
+            ranks = torch.empty(experts, device=device)
+            ranks[perm] = torch.arange(1, experts + 1, device=device, dtype=torch.float32)
+            gate[:, 0] = -ZIPF_ALPHA * ZIPF_S * torch.log(ranks)
+        gates.append(gate.to(torch.bfloat16))
+        slabs.append(ExpertSlab.allocate(experts, hidden, inter, device, generator=gen))
+    return ResidentMoEStack(gates, slabs, top_k=top_k)
+
+
+def prefill_lengths(count=8, lo=256, hi=4096, seed=0):
+    """Ragged prefill batch: ``count`` sequence lengths ~U[lo, hi] (seeded)."""
+    rng = np.random.default_rng(seed)
+    return [int(v) for v in rng.integers(lo, hi + 1, size=count)]
+
+
+def activations(t_count, hidden, device="cuda", seed=1, zipf=False):
+    gen = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(t_count, hidden, device=device, generator=gen)
+    if zipf:
+        x[:, 0] = 1.0
+    return x.to(torch.bfloat16)
+
+
+def expert_bytes(hidden, inter):
+    return 3 * hidden * inter * 2

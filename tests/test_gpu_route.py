@@ -17,17 +17,19 @@ def pdx():
 
 
 def test_torch_topk_tie_order_on_device():
-    """Pin the oracle's tie rule on the reference's own device op: equal values
-    -> lower index first, inside the selection and at the k boundary."""
-    from tests.gpu_util import to_dev  # noqa: F401
+    """Pin the oracle's tie rule on the reference's own device op: a tie at the
+    k boundary is won by the lower index; inside the selection equal values come
+    in descending index order."""
     v = torch.tensor([[0.1, 0.5, 0.3, 0.5, 0.3, 0.5, 0.2, 0.3]], device="cuda")
-    w, i = torch.topk(v, 5, dim=-1)
-    assert i.tolist() == [[1, 3, 5, 2, 4]]
-    probs = torch.rand(4096, 128, device="cuda")
-    probs = (probs * 16).floor() / 16  # many exact ties
-    _, sel = torch.topk(probs, 8, dim=-1)
-    _, ora = mo.topk_desc_lowindex(probs.cpu().numpy(), 8)
-    assert np.array_equal(sel.cpu().numpy(), ora)
+    _, i = torch.topk(v, 5, dim=-1)
+    assert i.tolist() == [[5, 3, 1, 4, 2]]
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    for k in (1, 2, 4, 8):
+        probs = torch.rand(4096, 128, device="cuda", generator=gen)
+        probs = (probs * 16).floor() / 16  # many exact ties
+        _, sel = torch.topk(probs, k, dim=-1)
+        _, ora = mo.topk_torch_cuda(probs.cpu().numpy(), k)
+        assert np.array_equal(sel.cpu().numpy(), ora)
 
 
 @pytest.mark.parametrize("tokens", ROUTE_T)
