@@ -14,9 +14,9 @@ Workload (synthetic seeded data, random-init weights):
     Zipf(1.1) router skew.
   * ``e2e``: the same decode step through the public stack API with the input
     copied host->device from pinned memory and the output copied back every step.
-  * ``roofline``: the grouped expert FFN (k_gateup_gemv + k_down_gemv) timed on
-    its own stream with CUDA events; algorithmic bytes = active experts x
-    9,437,184 B + activation rows.
+  * ``roofline``: the grouped expert FFN of the decode path (row gather + two
+    weight-streaming tcgen05 GEMMs) timed on its own stream with CUDA events;
+    algorithmic bytes = active experts x 9,437,184 B + activation rows.
   * ``cpu_baseline``: the reference's CPU layer path (oracle/cpu_path.py, torch
     CPU ops) on this host's cores, a bounded sample of layers.
 Multi-GPU (N>1): one process per GPU, each a full replica of the stack serving
@@ -306,7 +306,7 @@ def main():
         d = json.loads(tj.read_text()).get("decode_ffn")
         if d:
             traffic = d["dram_bytes_per_active_expert"] * statistics.mean(act)
-    roofline = dict(bound="hbm", kernel="pdx_moe_ffn_grouped GEMV (k_gateup_gemv + k_down_gemv)",
+    roofline = dict(bound="hbm", kernel="pdx_moe_ffn_grouped decode path (k_gather_rows + 2x k_stream_gemm: TMA weight stream, tcgen05 swap-AB)",
                     achieved=achieved, peak=pk["hbm_gbs"], unit="GB/s", frac=achieved / pk["hbm_gbs"],
                     peak_source=pk["source"], frac_of_8000_nominal=achieved / 8000.0, traffic=traffic,
                     bytes_per_launch=bytes_per_launch, us_per_launch=per_launch_s * 1e6)

@@ -79,7 +79,7 @@ typedef struct pdx_expert_weights {
 /* ---------------------------------------------------------------------------
  * a1. Routing.  Replaces route() -- expertbench/adapters/qwen.py:140-152:
  *   logits = F.linear(x, gate)                       (BF16, [T,E])
- *   p = softmax(logits.float()); w, ids = topk(p, k) (desc, ties: lower id)
+ *   p = softmax(logits.float()); w, ids = topk(p, k) (ties as on CUDA)
  *   if normalize: w /= w.sum(-1);  weights = w.to(bf16)
  * Logits are the exact dot products rounded once to BF16 (FP64 accumulation).
  * logits_out may be NULL (then the workspace holds them).
@@ -129,13 +129,17 @@ int pdx_gather_rows(const void *x, const int32_t *tokens, int64_t rows, int64_t 
  * for every packed row p of every active expert, UNWEIGHTED, in packed order,
  * with the reference's BF16 roundings (after each linear, after silu, after
  * the product).  `x` is the [T,H] token matrix; rows are gathered through
- * `tokens`.  mode: 0 = auto, 1 = streaming GEMV (decode), 2 = tcgen05
- * grouped GEMM (prefill).
+ * `tokens`.  mode: 0 = auto; 1 = decode path (weights streamed by TMA as the
+ * tcgen05 M operand, tokens as N, split-K for few experts); 2 = prefill path
+ * (tcgen05 grouped GEMM tiled over tokens); 3 = SIMT weight-streaming GEMV
+ * (an independent implementation kept for cross-checks and for shapes the
+ * tcgen05 paths do not tile).
  */
 #define PDX_FFN_AUTO 0
 #define PDX_FFN_GEMV 1
 #define PDX_FFN_GEMM 2
-size_t pdx_ffn_workspace_bytes(int64_t rows, int64_t H, int64_t I, int32_t mode);
+#define PDX_FFN_SIMT 3
+size_t pdx_ffn_workspace_bytes(int64_t rows, int64_t E, int64_t H, int64_t I, int32_t mode);
 int pdx_moe_ffn_grouped(const void *x, int64_t T, const int32_t *tokens,
                         const int32_t *offsets, const int32_t *active, int64_t E,
                         int64_t rows, const pdx_expert_weights *weights, int64_t H,

@@ -35,9 +35,10 @@ Rounding contract (why each step is written the way it is):
   ``expf`` (both are within 2 ulp, so the BF16 routing weights can differ by
   one BF16 ulp in rare cases).
 * Top-k.  ``torch.topk`` on CUDA selects by value descending, lower expert
-  index winning a tie at the k boundary, and returns equal values inside the
-  selection in descending index order (pinned on the B200).  The oracle
-  reproduces both rules (``topk_torch_cuda``).
+  index winning a tie at the k boundary, and orders the selection with
+  PyTorch's unstable 32-wide bitonic sort, so equal values come out in that
+  network's order (pinned on the B200).  The oracle restates both steps
+  (``topk_torch_cuda``).
 * Renormalisation.  ``weights.sum(-1)`` over k FP32 values uses PyTorch's
   reduction tree (``block_x_reduce``: lanes of width ``last_pow2(k)``, each
   lane summing its strided elements, then shfl_down with offsets 1, 2, 4 ...).
@@ -144,21 +145,73 @@ def softmax_fp32(logit_bits):
     return probs[:, :e_count]
 
 
-def topk_torch_cuda(values, k):
-    """torch.topk(values, k) as it behaves on CUDA (pinned on the B200).
+def _bitonic32_desc(keys, vals):
+    """PyTorch's small bitonic key/value sort (sort size 32, descending, GT
+    comparator, unstable), as used by torch.topk(sorted=True) for k <= 32.
 
-    The selected set is ordered by value descending with lower indices winning
-    a tie that straddles the k boundary; inside the returned (sorted) set,
-    equal values appear in DESCENDING index order (e.g. values
-    [.1,.5,.3,.5,.3,.5,.2,.3], k=5 -> indices [5,3,1,4,2]).
+    ``keys`` [T, n] float32 and ``vals`` [T, n] int64 in gather order, n <= 32;
+    positions >= n are invalid and always sort to the end.  Compare-exchange of
+    (a, b = a | stride): cond = (K[a] > K[b] and valid[a]) or not valid[b];
+    exchange when cond == dir, dir = bit `size` of a while building bitonic
+    runs, False in the final merge.
     """
+    t_count, n = keys.shape
+    size = 32
+    K = np.zeros((t_count, size), np.float32)
+    V = np.full((t_count, size), -1, np.int64)
+    ok = np.zeros((t_count, size), bool)
+    K[:, :n], V[:, :n], ok[:, :n] = keys, vals, True
+    pos = np.arange(size)
+
+    def step(stride, dirs):
+        a = pos[(pos & stride) == 0]
+        b = a | stride
+        cond = ((K[:, a] > K[:, b]) & ok[:, a]) | ~ok[:, b]
+        do = cond == dirs[None, :]
+        for arr in (K, V, ok):
+            xa, xb = arr[:, a].copy(), arr[:, b].copy()
+            arr[:, a] = np.where(do, xb, xa)
+            arr[:, b] = np.where(do, xa, xb)
+
+    s = 2
+    while s < size:
+        stride = s // 2
+        while stride > 0:
+            a = pos[(pos & stride) == 0]
+            step(stride, (a & s) != 0)
+            stride //= 2
+        s *= 2
+    stride = size // 2
+    while stride > 0:
+        step(stride, np.zeros(size // 2, bool))
+        stride //= 2
+    return K[:, :n], V[:, :n]
+
+
+def topk_torch_cuda(values, k):
+    """torch.topk(values, k) (sorted) as it runs on CUDA, restated.
+
+    1. Selection (gatherTopK): every value strictly above the k-th largest, in
+       index order, then values equal to the k-th largest in index order until
+       k are taken -- so a tie at the k boundary is won by the lower index.
+    2. Order: PyTorch's 32-wide bitonic sort (descending, unstable) of that
+       gather order; equal values come out in the network's order, e.g.
+       [.1,.5,.3,.5,.3,.5,.2,.3], k=5 -> [5,3,1,4,2] (pinned on the B200).
+    """
+    if k > 32:
+        raise ValueError("the restated bitonic order covers k <= 32")
     t_count, e_count = values.shape
     idx = np.broadcast_to(np.arange(e_count), values.shape)
     chosen = np.lexsort((idx, -values.astype(np.float64)), axis=-1)[:, :k]
-    cv = np.take_along_axis(values, chosen, axis=1)
-    order = np.lexsort((-chosen, -cv.astype(np.float64)), axis=-1)
-    sel = np.take_along_axis(chosen, order, axis=1)
-    return np.take_along_axis(values, sel, axis=1), sel.astype(np.int64)
+    cv = np.take_along_axis(values, chosen, axis=1).astype(np.float32)
+    kth = cv[:, -1:]
+    gather = np.lexsort((chosen, (cv == kth).astype(np.int8)), axis=-1)
+    g_idx = np.take_along_axis(chosen, gather, axis=1).astype(np.int64)
+    g_val = np.take_along_axis(cv, gather, axis=1)
+    if k == 1:
+        return g_val, g_idx
+    vals, sel = _bitonic32_desc(g_val, g_idx)
+    return vals, sel
 
 
 def torch_sum_lastdim(v):

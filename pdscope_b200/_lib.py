@@ -24,7 +24,7 @@ PDX_DEVERR_WAIT_TIMEOUT = 1
 PDX_DEVERR_BAD_EXPERT = 2
 PDX_DEVERR_BAD_SLOT = 3
 
-FFN_AUTO, FFN_GEMV, FFN_GEMM = 0, 1, 2
+FFN_AUTO, FFN_GEMV, FFN_GEMM, FFN_SIMT = 0, 1, 2, 3
 
 ABI_VERSION = 1
 
@@ -54,7 +54,7 @@ SIGNATURES = {
     "pdx_pack": (ctypes.c_int, [c_vp, c_vp, c_i64, c_i32, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                                 c_vp, c_sz, c_vp]),
     "pdx_gather_rows": (ctypes.c_int, [c_vp, c_vp, c_i64, c_i64, c_vp, c_vp]),
-    "pdx_ffn_workspace_bytes": (c_sz, [c_i64, c_i64, c_i64, c_i32]),
+    "pdx_ffn_workspace_bytes": (c_sz, [c_i64, c_i64, c_i64, c_i64, c_i32]),
     "pdx_moe_ffn_grouped": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64,
                                            ctypes.POINTER(ExpertWeights), c_i64, c_i64, c_vp, c_i32, c_vp,
                                            c_sz, c_vp]),

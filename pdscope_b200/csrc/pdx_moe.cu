@@ -16,6 +16,7 @@
 #include "combine.cu"
 #include "ffn_gemm.cu"
 #include "ffn_gemv.cu"
+#include "ffn_stream.cu"
 #include "pack.cu"
 #include "route.cu"
 
@@ -93,6 +94,11 @@ int device_setup(int* sms_out) {
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_gateup_gemv<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemv_smem));
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_down_gemv<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemv_smem));
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_down_gemv<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemv_smem));
+        const int ss = static_cast<int>(kStreamSmemBytes);
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_stream_gemm<16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ss));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_stream_gemm<16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ss));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_stream_gemm<32, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ss));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_stream_gemm<32, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ss));
         g_num_sms[dev] = sms;
         g_attrs_set[dev] = true;
     }
@@ -146,23 +152,30 @@ int check_route_shape(int64_t T, int64_t H, int64_t E, int32_t k) {
     return PDX_OK;
 }
 
+bool gemm_shape_ok(int64_t H, int64_t I) { return H % 256 == 0 && I % 128 == 0 && H >= 256 && I >= 128; }
+bool stream_shape_ok(int64_t H, int64_t I) { return H % 128 == 0 && I % 128 == 0 && H >= 128 && I >= 128; }
+
 int resolve_mode(int32_t mode, int64_t T, int64_t H, int64_t I) {
-    const bool gemm_ok = (H % 256 == 0) && (I % 128 == 0) && (H >= 256) && (I >= 128);
-    if (mode == PDX_FFN_AUTO) return (T > kGemvMaxTokens && gemm_ok) ? PDX_FFN_GEMM : PDX_FFN_GEMV;
-    return mode;
+    if (mode != PDX_FFN_AUTO) return mode;
+    if (T > kGemvMaxTokens && gemm_shape_ok(H, I)) return PDX_FFN_GEMM;
+    if (stream_shape_ok(H, I)) return PDX_FFN_GEMV;
+    return PDX_FFN_SIMT;
 }
 
 int check_ffn_shape(int64_t H, int64_t I, int32_t mode) {
     if (H < 8 || I < 8 || H % 8 || I % 8)
         return fail(PDX_ERR_UNSUPPORTED, "H=%lld, I=%lld must be positive multiples of 8", static_cast<long long>(H),
                     static_cast<long long>(I));
-    if (mode == PDX_FFN_GEMV) {
+    if (mode == PDX_FFN_SIMT) {
         if (I % 16 || H % 32)
-            return fail(PDX_ERR_UNSUPPORTED, "GEMV path needs I %% 16 == 0 and H %% 32 == 0");
+            return fail(PDX_ERR_UNSUPPORTED, "SIMT path needs I %% 16 == 0 and H %% 32 == 0");
         if (H > 4096 || I > 4096)
-            return fail(PDX_ERR_UNSUPPORTED, "GEMV path supports H, I <= 4096");
+            return fail(PDX_ERR_UNSUPPORTED, "SIMT path supports H, I <= 4096");
+    } else if (mode == PDX_FFN_GEMV) {
+        if (!stream_shape_ok(H, I))
+            return fail(PDX_ERR_UNSUPPORTED, "weight-streaming path needs H %% 128 == 0 and I %% 128 == 0");
     } else if (mode == PDX_FFN_GEMM) {
-        if (H % 256 || I % 128)
+        if (!gemm_shape_ok(H, I))
             return fail(PDX_ERR_UNSUPPORTED, "tcgen05 path needs H %% 256 == 0 and I %% 128 == 0");
     } else {
         return fail(PDX_ERR_INVALID, "unknown FFN mode %d", mode);
@@ -262,10 +275,61 @@ int launch_pack(const int64_t* selected, const uint16_t* weights, int64_t T, int
     return PDX_OK;
 }
 
-size_t ffn_ws_bytes(int64_t rows, int64_t H, int64_t I, int mode) {
-    size_t b = align_up(static_cast<size_t>(rows) * I * 2);  // h
-    if (mode == PDX_FFN_GEMM) b += align_up(static_cast<size_t>(rows) * H * 2);  // gathered rows
+// Split-K / token-tile plan of the weight-streaming path.  It depends only on
+// (rows, E, H, I), so the workspace query and the launch agree.
+constexpr int kPlanSMs = 148;
+
+struct StreamPlan {
+    int nt;
+    int s1, s2;
+    int64_t tiles1, tiles2;
+    size_t partial_bytes, ticket_bytes;
+};
+
+int plan_splits(int num_kb, int64_t est_tiles) {
+    const int64_t want = (8 * kPlanSMs + est_tiles / 2) / std::max<int64_t>(est_tiles, 1);
+    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, std::max(1, num_kb / 4))));
+}
+
+StreamPlan plan_stream(int64_t rows, int64_t E, int64_t H, int64_t I) {
+    StreamPlan p{};
+    const int64_t est_active = std::max<int64_t>(1, std::min(E, rows));
+    const int64_t avg = (rows + est_active - 1) / est_active;
+    p.nt = avg <= 12 ? 16 : 32;
+    const int64_t nb_bound = rows / p.nt + est_active;
+    p.tiles1 = (I / 128) * nb_bound;
+    p.tiles2 = (H / 128) * nb_bound;
+    p.s1 = plan_splits(static_cast<int>(H / 64), (I / 128) * est_active);
+    p.s2 = plan_splits(static_cast<int>(I / 64), (H / 128) * est_active);
+    const int64_t c1 = p.s1 > 1 ? p.tiles1 * p.s1 * 2 * p.nt : 0;
+    const int64_t c2 = p.s2 > 1 ? p.tiles2 * p.s2 * p.nt : 0;
+    p.partial_bytes = static_cast<size_t>(std::max(c1, c2)) * 128 * 4;
+    p.ticket_bytes = static_cast<size_t>(std::max(p.tiles1, p.tiles2)) * 4 * 4;
+    return p;
+}
+
+size_t ffn_ws_bytes(int64_t rows, int64_t E, int64_t H, int64_t I, int mode) {
+    size_t b = align_up(static_cast<size_t>(rows) * I * 2);                        // h
+    if (mode == PDX_FFN_GEMM || mode == PDX_FFN_GEMV) b += align_up(static_cast<size_t>(rows) * H * 2);  // x rows
+    if (mode == PDX_FFN_GEMV) {
+        const StreamPlan p = plan_stream(rows, E, H, I);
+        b += align_up(p.partial_bytes) + align_up(p.ticket_bytes);
+    }
     return b;
+}
+
+template <int NT>
+int launch_stream_pair(const CUtensorMap& tm_g, const CUtensorMap& tm_u, const CUtensorMap& tm_x,
+                       const CUtensorMap& tm_d, const CUtensorMap& tm_h, const StreamPlan& p, StreamArgs a1,
+                       StreamArgs a2, int sms, cudaStream_t stream) {
+    const int grid1 = static_cast<int>(std::min<int64_t>(sms, p.tiles1 * p.s1));
+    k_stream_gemm<NT, true><<<grid1, kStreamThreads, kStreamSmemBytes, stream>>>(tm_g, tm_u, tm_x, a1);
+    PDX_LAUNCHED();
+    if (p.s2 > 1) PDX_CUDA_TRY(cudaMemsetAsync(a2.tickets, 0, p.ticket_bytes, stream));
+    const int grid2 = static_cast<int>(std::min<int64_t>(sms, p.tiles2 * p.s2));
+    k_stream_gemm<NT, false><<<grid2, kStreamThreads, kStreamSmemBytes, stream>>>(tm_d, tm_d, tm_h, a2);
+    PDX_LAUNCHED();
+    return PDX_OK;
 }
 
 int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* offsets, const int32_t* active,
@@ -275,11 +339,21 @@ int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* o
     int st = device_setup(&sms);
     if (st) return st;
     uint16_t* h = static_cast<uint16_t*>(ws.take(static_cast<size_t>(rows) * I * 2));
-    uint16_t* xp = mode == PDX_FFN_GEMM ? static_cast<uint16_t*>(ws.take(static_cast<size_t>(rows) * H * 2)) : nullptr;
+    uint16_t* xp = (mode == PDX_FFN_GEMM || mode == PDX_FFN_GEMV)
+                       ? static_cast<uint16_t*>(ws.take(static_cast<size_t>(rows) * H * 2))
+                       : nullptr;
+    StreamPlan plan{};
+    float* partials = nullptr;
+    unsigned int* tickets = nullptr;
+    if (mode == PDX_FFN_GEMV) {
+        plan = plan_stream(rows, E, H, I);
+        partials = static_cast<float*>(ws.take(std::max<size_t>(plan.partial_bytes, 16)));
+        tickets = static_cast<unsigned int*>(ws.take(plan.ticket_bytes));
+    }
     if (ws.overflow) return fail(PDX_ERR_WORKSPACE, "FFN workspace too small (%zu > %zu bytes)", ws.used, ws.cap);
     const ExpertSlab slab = to_slab(w);
     const int64_t max_active = std::min<int64_t>(E, rows);
-    if (mode == PDX_FFN_GEMV) {
+    if (mode == PDX_FFN_SIMT) {
         const bool small = rows <= 64;
         const int rb = small ? 4 : 16;
         const int rpw_down = small ? 1 : 4;
@@ -308,21 +382,34 @@ int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* o
         PDX_LAUNCHED();
         return PDX_OK;
     }
-    // tcgen05 path: gather -> GEMM1 (gate|up, SwiGLU) -> GEMM2 (down)
+    // tcgen05 paths: gather the packed x rows once
     k_gather_rows<<<static_cast<unsigned>(rows), kCombineThreads, 0, stream>>>(
         static_cast<const uint16_t*>(x), tokens, static_cast<int>(rows), static_cast<int>(H), xp);
     PDX_LAUNCHED();
     const int64_t gs = w->num_slots > 1 ? w->gate_stride / H : 0;
     const int64_t us = w->num_slots > 1 ? w->up_stride / H : 0;
     const int64_t ds = w->num_slots > 1 ? w->down_stride / I : 0;
-    CUtensorMap tm_x, tm_g, tm_u, tm_h, tm_d;
-    if ((st = encode_2d(&tm_x, xp, rows, H, kGemmBM))) return st;
-    if ((st = encode_2d(&tm_g, w->gate, (w->num_slots - 1) * gs + I, H, kGemmBN / 2))) return st;
-    if ((st = encode_2d(&tm_u, w->up, (w->num_slots - 1) * us + I, H, kGemmBN / 2))) return st;
-    if ((st = encode_2d(&tm_h, h, rows, I, kGemmBM))) return st;
-    if ((st = encode_2d(&tm_d, w->down, (w->num_slots - 1) * ds + H, I, kGemmBN))) return st;
     if ((w->num_slots - 1) * std::max(gs, std::max(us, ds)) + H >= (int64_t(1) << 31))
         return fail(PDX_ERR_UNSUPPORTED, "expert slab too large for 32-bit TMA row coordinates");
+    CUtensorMap tm_x, tm_g, tm_u, tm_h, tm_d;
+    if ((st = encode_2d(&tm_g, w->gate, (w->num_slots - 1) * gs + I, H, 128))) return st;
+    if ((st = encode_2d(&tm_u, w->up, (w->num_slots - 1) * us + I, H, 128))) return st;
+    if (mode == PDX_FFN_GEMV) {
+        if ((st = encode_2d(&tm_x, xp, rows, H, plan.nt))) return st;
+        if ((st = encode_2d(&tm_h, h, rows, I, plan.nt))) return st;
+        if ((st = encode_2d(&tm_d, w->down, (w->num_slots - 1) * ds + H, I, 128))) return st;
+        if (plan.s1 > 1) PDX_CUDA_TRY(cudaMemsetAsync(tickets, 0, plan.ticket_bytes, stream));
+        StreamArgs a1{offsets, active, w->slot_of_expert, w->num_slots, gs, us, static_cast<int>(H),
+                      static_cast<int>(I / 128), plan.s1, h, I, partials, tickets};
+        StreamArgs a2{offsets, active, w->slot_of_expert, w->num_slots, ds, ds, static_cast<int>(I),
+                      static_cast<int>(H / 128), plan.s2, static_cast<uint16_t*>(y), H, partials, tickets};
+        if (plan.nt == 16) return launch_stream_pair<16>(tm_g, tm_u, tm_x, tm_d, tm_h, plan, a1, a2, sms, stream);
+        return launch_stream_pair<32>(tm_g, tm_u, tm_x, tm_d, tm_h, plan, a1, a2, sms, stream);
+    }
+    // prefill: token-tiled grouped GEMM
+    if ((st = encode_2d(&tm_x, xp, rows, H, kGemmBM))) return st;
+    if ((st = encode_2d(&tm_h, h, rows, I, kGemmBM))) return st;
+    if ((st = encode_2d(&tm_d, w->down, (w->num_slots - 1) * ds + H, I, kGemmBN))) return st;
     const int64_t m_tiles_bound = rows / kGemmBM + max_active;
     GemmArgs a1{offsets, active, w->slot_of_expert, w->num_slots, gs, us, static_cast<int>(H),
                 static_cast<int>(I), 1, h, I};
@@ -449,9 +536,11 @@ int pdx_gather_rows(const void* x, const int32_t* tokens, int64_t rows, int64_t 
     return ok();
 }
 
-size_t pdx_ffn_workspace_bytes(int64_t rows, int64_t H, int64_t I, int32_t mode) {
+size_t pdx_ffn_workspace_bytes(int64_t rows, int64_t E, int64_t H, int64_t I, int32_t mode) {
+    rows = std::max<int64_t>(rows, 1);
+    E = std::max<int64_t>(E, 1);
     const int m = resolve_mode(mode, rows, H, I);
-    return ffn_ws_bytes(rows, H, I, m) + kAlign;
+    return ffn_ws_bytes(rows, E, H, I, m) + kAlign;
 }
 
 int pdx_moe_ffn_grouped(const void* x, int64_t T, const int32_t* tokens, const int32_t* offsets,
@@ -474,7 +563,7 @@ int pdx_moe_ffn_grouped(const void* x, int64_t T, const int32_t* tokens, const i
 size_t pdx_expert_ffn_workspace_bytes(int64_t n, int64_t H, int64_t I) {
     const int64_t nn = std::max<int64_t>(n, 1);
     const int m = resolve_mode(PDX_FFN_AUTO, nn, H, I);
-    return align_up(8) * 2 + align_up(nn * 4) + ffn_ws_bytes(nn, H, I, m) + kAlign;
+    return align_up(8) * 2 + align_up(nn * 4) + ffn_ws_bytes(nn, 1, H, I, m) + kAlign;
 }
 
 int pdx_expert_ffn(const void* x, int64_t n, const void* gate, const void* up, const void* down, int64_t H, int64_t I,
@@ -526,7 +615,7 @@ size_t pdx_layer_workspace_bytes(int64_t T, int64_t H, int64_t E, int32_t top_k,
     carve_pack(c, T, top_k, E, nullptr);
     c.take(N * H * 2);           // y
     const int m = resolve_mode(mode, T, H, I);
-    return c.used + ffn_ws_bytes(N, H, I, m) + kAlign;
+    return c.used + ffn_ws_bytes(N, E, H, I, m) + kAlign;
 }
 
 int pdx_moe_layer(const void* x, const void* gate, int64_t T, int64_t H, int64_t E, int32_t top_k, int32_t normalize,

@@ -16,9 +16,11 @@ namespace pdx {
 //    max and the sum use an xor butterfly (offsets 16..1); each lane sums its
 //    own elements in i order; p = exp(x - max) / sum with IEEE division and
 //    CUDA's expf (the same function the reference's kernel calls).
-//  * torch.topk(p, k): value descending; a tie straddling the k boundary is
-//    won by the lower expert index; inside the returned set equal values are
-//    in descending index order (behaviour of the CUDA kernel, pinned on B200).
+//  * torch.topk(p, k): the selected set is the k largest, a tie at the k
+//    boundary won by the lower expert index; the returned order is that of
+//    PyTorch's 32-wide bitonic sort applied to the gather order (above-k-th
+//    values by index, then k-th-value ties by index), so equal values come
+//    out in the network's order (behaviour pinned on the B200).
 //  * w / w.sum(-1): PyTorch's small-row reduction tree (block_x_reduce) -- lane
 //    j < width = last_pow2(k) holds w_j + w_{j+width}, then shfl_down by
 //    1, 2, 4, ...; lane 0's total divides every weight; result RNE to BF16.
@@ -78,7 +80,7 @@ __device__ __forceinline__ void warp_softmax_topk(const uint16_t* __restrict__ l
         if (lane == owner) taken |= 1u << owner_i;
         if (static_cast<int>(lane) == r) { my_p = p_sel; my_idx = static_cast<int>(win_idx); }
     }
-    float w = my_p;
+    float denom = 1.f;
     if (normalize) {
         int width = 1;
         while (width * 2 <= k) width <<= 1;
@@ -86,21 +88,50 @@ __device__ __forceinline__ void warp_softmax_topk(const uint16_t* __restrict__ l
         float a = my_p;
         if (static_cast<int>(lane) + width < k) a = a + second;
         for (int off = 1; off < width; off <<= 1) a += __shfl_down_sync(0xffffffffu, a, off);
-        const float denom = __shfl_sync(0xffffffffu, a, 0);
-        w = __fdiv_rn(my_p, denom);
+        denom = __shfl_sync(0xffffffffu, a, 0);
     }
-    // torch.topk on CUDA returns equal values in descending index order: place
-    // each selected expert by (p descending, index descending).  Tied entries
-    // carry equal weights, so the renormalisation sum above is unaffected.
-    int pos = 0;
+    // ---- order the selection as torch.topk(sorted=True) returns it on CUDA ----
+    // (1) gather order: values above the k-th largest in index order, then the
+    //     values equal to it in index order;
+    const float kth = __shfl_sync(0xffffffffu, my_p, k - 1);
+    int g = 0;
     for (int j = 0; j < k; ++j) {
         const float pj = __shfl_sync(0xffffffffu, my_p, j);
         const int ij = __shfl_sync(0xffffffffu, my_idx, j);
-        if (pj > my_p || (pj == my_p && ij > my_idx)) ++pos;
+        const int cj = pj == kth, cr = my_p == kth;
+        if (cj < cr || (cj == cr && ij < my_idx)) ++g;
+    }
+    float key = 0.f;
+    int val = -1;
+    bool ok = false;
+    for (int j = 0; j < k; ++j) {
+        const int gj = __shfl_sync(0xffffffffu, g, j);
+        const float pj = __shfl_sync(0xffffffffu, my_p, j);
+        const int ij = __shfl_sync(0xffffffffu, my_idx, j);
+        if (gj == static_cast<int>(lane)) { key = pj; val = ij; ok = true; }
+    }
+    // (2) PyTorch's 32-wide bitonic key/value sort (descending, unstable): one
+    //     position per lane, compare-exchange of (a, a|stride) where
+    //     cond = (K[a] > K[b] && valid[a]) || !valid[b], exchanged when
+    //     cond == dir (dir = bit `size` of a while building, false when merging).
+    if (k > 1) {
+        for (int size = 2; size <= 32; size <<= 1) {
+            for (int st = size >> 1; st > 0; st >>= 1) {
+                const bool dir = size < 32 && ((lane & ~static_cast<uint32_t>(st)) & static_cast<uint32_t>(size)) != 0;
+                const float ko = __shfl_xor_sync(0xffffffffu, key, st);
+                const int vo = __shfl_xor_sync(0xffffffffu, val, st);
+                const bool oko = __shfl_xor_sync(0xffffffffu, ok ? 1 : 0, st) != 0;
+                const bool lower = (lane & static_cast<uint32_t>(st)) == 0;
+                const float ka = lower ? key : ko, kb = lower ? ko : key;
+                const bool oka = lower ? ok : oko, okb = lower ? oko : ok;
+                const bool cond = (ka > kb && oka) || !okb;
+                if (cond == dir) { key = ko; val = vo; ok = oko; }
+            }
+        }
     }
     if (static_cast<int>(lane) < k) {
-        sel_out[pos] = my_idx;
-        w_out[pos] = f2bits(w);
+        sel_out[lane] = val;
+        w_out[lane] = f2bits(normalize ? __fdiv_rn(key, denom) : key);
     }
 }
 

@@ -77,7 +77,7 @@ class ResidentMoEStack:
         rows = torch.empty((n, H), **bf)  # expert outputs of the current layer (staged path)
         ws_layer = lib.pdx_layer_workspace_bytes(t_count, H, E, k, self.inter, mode)
         ws_stage = max(lib.pdx_route_workspace_bytes(t_count, E), lib.pdx_pack_workspace_bytes(t_count, k, E),
-                       lib.pdx_ffn_workspace_bytes(n, H, self.inter, mode))
+                       lib.pdx_ffn_workspace_bytes(n, E, H, self.inter, mode))
         ws = torch.empty(max(ws_layer, ws_stage), dtype=torch.uint8, device=dev)
         b = dict(acts=acts, stages=stages, ws=ws, rows=rows)
         self._bufs[key] = b

@@ -50,7 +50,7 @@ def _check_layer(res, x, gate, wg, wu, wd, k):
     return got
 
 
-@pytest.mark.parametrize("mode", (0, 1, 2))
+@pytest.mark.parametrize("mode", (0, 1, 2, 3))
 def test_small_layer_golden(pdx, golden, mode):
     """The golden small layer (E=16, k=4, H=256, I=128, T=32)."""
     x, gate, wg, wu, wd = mo.synthetic_layer(4242, 32, 256, 16, 128)
