@@ -117,6 +117,25 @@ int pdx_pack(const int64_t *selected, const void *weights, int64_t T, int32_t to
              int32_t *positions, void *packed_w, int32_t *inverse, int32_t *active,
              void *workspace, size_t workspace_bytes, pdx_stream_t stream);
 
+/* Allocation-free packing.  No counterpart in the reference: PDScope always
+ * packs with torch allocations.  Same contract and outputs as pdx_pack, for
+ * callers that cannot allocate device memory where they pack (a plugin inside
+ * a host process whose allocator owns the device's memory, an FFI caller with
+ * no device allocator, a latency-critical path that cannot afford
+ * cudaMalloc's device-wide synchronisation).  Its scratch is a fixed
+ * file-scope device array of PDX_PACK_STATIC_MAX_HIST_INTS ints (256 KiB, held
+ * by every GPU that loads the library until exit); sizes needing more,
+ * ceil(T*top_k/4096)*E > PDX_PACK_STATIC_MAX_HIST_INTS when T*top_k > 8192,
+ * return PDX_ERR_UNSUPPORTED.  All calls share that array: calls whose kernels
+ * overlap on the GPU race.  The first call on a device resolves the array's
+ * device address (cudaGetSymbolAddress) with that device current; make it
+ * before any stream capture. */
+#define PDX_PACK_STATIC_MAX_HIST_INTS 65536
+int pdx_pack_static(const int64_t *selected, const void *weights, int64_t T, int32_t top_k,
+                    int64_t E, int32_t *counts, int32_t *offsets, int32_t *tokens,
+                    int32_t *positions, void *packed_w, int32_t *inverse, int32_t *active,
+                    pdx_stream_t stream);
+
 /* a4. Row gather x[tokens[p]] -> out[p]  (inputs[flat_tokens],
  * pdscope_runtime.py:333-336). */
 int pdx_gather_rows(const void *x, const int32_t *tokens, int64_t rows, int64_t H,

@@ -53,6 +53,8 @@ SIGNATURES = {
     "pdx_pack_workspace_bytes": (c_sz, [c_i64, c_i32, c_i64]),
     "pdx_pack": (ctypes.c_int, [c_vp, c_vp, c_i64, c_i32, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                                 c_vp, c_sz, c_vp]),
+    "pdx_pack_static": (ctypes.c_int, [c_vp, c_vp, c_i64, c_i32, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                       c_vp]),
     "pdx_gather_rows": (ctypes.c_int, [c_vp, c_vp, c_i64, c_i64, c_vp, c_vp]),
     "pdx_ffn_workspace_bytes": (c_sz, [c_i64, c_i64, c_i64, c_i64, c_i32]),
     "pdx_moe_ffn_grouped": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64,

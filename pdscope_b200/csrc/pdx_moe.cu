@@ -666,3 +666,6 @@ int pdx_device_error(pdx_stream_t stream, uint32_t* code_out) {
 }
 
 }  // extern "C"
+
+// Allocation-free packing (fixed device scratch); uses the helpers above.
+#include "pack_static.cu"
