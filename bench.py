@@ -54,7 +54,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("pdx", "reference"), default="pdx")
     ap.add_argument("--layers", type=int, default=CFG["layers"])
-    ap.add_argument("--decode-batch", type=int, default=64)
+    ap.add_argument("--decode-batch", type=int, default=64, help="headline decode batch")
+    ap.add_argument("--decode-batches", default="1,8", help="other decode batches reported beside the headline")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--prefill-steps", type=int, default=3)
     ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU baseline sample")
@@ -268,7 +269,8 @@ def main():
     # ---- decode: batches 1, 8 and the headline batch --------------------------------
     decode = {}
     headline_t = args.decode_batch
-    for t_count in sorted({1, 8, headline_t}):
+    extra = [int(v) for v in args.decode_batches.split(",") if v.strip()]
+    for t_count in sorted(set(extra) | {headline_t}):
         stack.input(t_count).copy_(activations(t_count, CFG["hidden"], device=dev, seed=10 + t_count + 1000 * rank))
         launches0 = _lib.lib.pdx_launch_count()
         stack.step(t_count)  # capture (counts the kernels of one step)

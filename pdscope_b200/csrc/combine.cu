@@ -36,6 +36,8 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(const uint16_t* __r
                                                              const int32_t* __restrict__ inverse, int T, int k,
                                                              int H, const uint16_t* __restrict__ residual,
                                                              uint16_t* __restrict__ out) {
+    griddep_wait();
+    griddep_launch();
     const int t = static_cast<int>(blockIdx.x);
     if (t >= T) return;
     __shared__ int s_row[32];
@@ -60,21 +62,40 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(const uint16_t* __r
 #pragma unroll
             for (int i = 0; i < 8; ++i) acc[i] = 0.f;
         }
-        for (int s = 0; s < k; ++s) {
-            float v[8];
-            unpack8(__ldg(reinterpret_cast<const uint4*>(y + static_cast<size_t>(s_row[s]) * H + c)), v);
-            const float w = s_w[s];
+        // issue the loads of up to 8 expert rows before accumulating (slot order)
+        for (int s0 = 0; s0 < k; s0 += 8) {
+            uint4 rv[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i] += round_bf16(v[i] * w);
+            for (int j = 0; j < 8; ++j)
+                if (s0 + j < k)
+                    rv[j] = __ldg(reinterpret_cast<const uint4*>(y + static_cast<size_t>(s_row[s0 + j]) * H + c));
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (s0 + j < k) {
+                    float v[8];
+                    unpack8(rv[j], v);
+                    const float w = s_w[s0 + j];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc[i] += round_bf16(v[i] * w);
+                }
+            }
         }
         *reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H + c) = pack8(acc);
     }
 }
 
-// out[p] = x[tokens[p]]  (inputs[flat_tokens], pdscope_runtime.py:333-336)
+// out[p] = x[tokens[p]]  (inputs[flat_tokens], pdscope_runtime.py:333-336).
+// CTA 0 also clears `zero_words` words (the split-K tickets of the FFN kernels
+// that follow), so no memset node separates the kernels of the chain.
 __global__ void __launch_bounds__(kCombineThreads) k_gather_rows(const uint16_t* __restrict__ x,
                                                                  const int32_t* __restrict__ tokens, int rows,
-                                                                 int H, uint16_t* __restrict__ out) {
+                                                                 int H, uint16_t* __restrict__ out,
+                                                                 unsigned int* __restrict__ zero_ptr,
+                                                                 int zero_words) {
+    griddep_wait();
+    griddep_launch();
+    if (blockIdx.x == 0)
+        for (int i = threadIdx.x; i < zero_words; i += blockDim.x) zero_ptr[i] = 0u;
     const int p = static_cast<int>(blockIdx.x);
     if (p >= rows) return;
     const size_t src = static_cast<size_t>(tokens[p]) * H;

@@ -36,7 +36,7 @@ constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
 constexpr uint32_t kTmemCols = 512;  // two 256-column FP32 accumulators
 constexpr int kMaxActive = 1024;
 constexpr size_t kGemmSmemBytes = 1024 /*alignment slack*/ + kGemmStages * kStageBytes + 256 /*barriers*/ +
-                                  (kMaxActive + 1) * 4 /*tile prefix*/;
+                                  4 * (kMaxActive + 1) * 4 /*tile prefix, segment start, rows, slot*/;
 
 struct GemmArgs {
     const int32_t* offsets;
@@ -54,13 +54,12 @@ struct GemmArgs {
 
 // ---- tile schedule ------------------------------------------------------------
 struct TileInfo {
-    int e;
+    int a;  // index into the active-expert tables
     int m;
     int n;
 };
 
-__device__ __forceinline__ TileInfo decode_tile(int tile, const int* prefix, int n_active, int n_tiles,
-                                                const int32_t* active) {
+__device__ __forceinline__ TileInfo decode_tile(int tile, const int* prefix, int n_active, int n_tiles) {
     int lo = 0, hi = n_active - 1;  // largest a with prefix[a] <= tile
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
@@ -68,7 +67,7 @@ __device__ __forceinline__ TileInfo decode_tile(int tile, const int* prefix, int
     }
     const int local = tile - prefix[lo];
     TileInfo ti;
-    ti.e = active[1 + lo];
+    ti.a = lo;
     ti.m = local / n_tiles;
     ti.n = local % n_tiles;
     return ti;
@@ -90,10 +89,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     int* s_misc = reinterpret_cast<int*>(tmem_slot + 2);  // [0] = total tiles, [1] = n_active
     int* prefix = reinterpret_cast<int*>(smem + kGemmStages * kStageBytes + 256);
+    int* t_seg0 = prefix + (kMaxActive + 1);
+    int* t_rows = t_seg0 + (kMaxActive + 1);
+    int* t_slot = t_rows + (kMaxActive + 1);
 
     const int warp = static_cast<int>(threadIdx.x >> 5);
     const uint32_t lane = lane_id();
-    const int n_active = min(args.active[0], kMaxActive);
+
     const int out_cols_per_tile = args.swiglu ? kGemmBN / 2 : kGemmBN;
     const int n_tiles = args.n_cols / out_cols_per_tile;
     const int num_kb = args.K / kGemmBK;
@@ -123,6 +125,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
+    // Everything above is independent of the previous kernel; from here on the
+    // routing/packing results (and the previous FFN stage) are read.
+    griddep_wait();
+    griddep_launch();
+    const int n_active = min(args.active[0], kMaxActive);
     // per-expert m-tile counts -> exclusive prefix (warp 2)
     if (warp == 2) {
         const int per = (n_active + 31) / 32;
@@ -131,9 +138,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int i = 0; i < per; ++i)
             if (b + i < n_active) {
                 const int e = args.active[1 + b + i];
-                const int rows = args.offsets[e + 1] - args.offsets[e];
+                const int seg0 = args.offsets[e];
+                const int rows = args.offsets[e + 1] - seg0;
+                int64_t slot = args.slot_of_expert ? args.slot_of_expert[e] : e;
+                if (slot < 0 || slot >= args.num_slots) {
+                    raise_error(PDX_DEVERR_BAD_SLOT);
+                    slot = 0;  // keeps the pipeline consistent; the call is flagged invalid
+                }
                 const int tiles = ((rows + kGemmBM - 1) / kGemmBM) * n_tiles;
                 prefix[b + i] = tiles;
+                t_seg0[b + i] = seg0;
+                t_rows[b + i] = rows;
+                t_slot[b + i] = static_cast<int>(slot);
                 local += tiles;
             }
         int inc = local;
@@ -164,13 +180,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             uint32_t phase = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-                const TileInfo ti = decode_tile(tile, prefix, n_active, n_tiles, args.active);
-                int64_t slot = args.slot_of_expert ? args.slot_of_expert[ti.e] : ti.e;
-                if (slot < 0 || slot >= args.num_slots) {
-                    raise_error(PDX_DEVERR_BAD_SLOT);
-                    slot = 0;  // keep the pipeline consistent; the result is flagged invalid
-                }
-                const int row_a = args.offsets[ti.e] + ti.m * kGemmBM;
+                const TileInfo ti = decode_tile(tile, prefix, n_active, n_tiles);
+                const int64_t slot = t_slot[ti.a];
+                const int row_a = t_seg0[ti.a] + ti.m * kGemmBM;
                 const int row_b0 = static_cast<int>(slot * args.b0_rows_per_slot) + ti.n * out_cols_per_tile;
                 const int row_b1 = static_cast<int>(slot * args.b1_rows_per_slot) + ti.n * out_cols_per_tile;
                 for (int kb = 0; kb < num_kb; ++kb) {
@@ -232,9 +244,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t acc_phase = static_cast<uint32_t>(lt >> 1) & 1u;
             if (!mbar_wait(&tmem_full[b], acc_phase, abort_flag)) break;
             tc_fence_after();
-            const TileInfo ti = decode_tile(tile, prefix, n_active, n_tiles, args.active);
-            const int seg0 = args.offsets[ti.e];
-            const int n_e = args.offsets[ti.e + 1] - seg0;
+            const TileInfo ti = decode_tile(tile, prefix, n_active, n_tiles);
+            const int seg0 = t_seg0[ti.a];
+            const int n_e = t_rows[ti.a];
             const int r = ti.m * kGemmBM + row_in_tile;
             const bool valid = r < n_e;
             uint16_t* orow = args.out + static_cast<int64_t>(seg0 + r) * args.out_ld + ti.n * out_cols_per_tile;

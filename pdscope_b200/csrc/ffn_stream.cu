@@ -33,8 +33,10 @@ constexpr uint32_t kStreamBMaxBytes = 64 * kStreamBK * 2;         // up to 64 to
 constexpr uint32_t kStreamStageBytes = 2 * kStreamABytes + kStreamBMaxBytes;  // 40 KiB
 constexpr uint32_t kStreamTmemCols = 256;
 constexpr int kStreamMaxActive = 1024;
+// after the stages: barriers (256 B), then four int tables over the active
+// experts -- tile prefix, segment start, row count, weight slot
 constexpr size_t kStreamSmemBytes =
-    1024 + kStreamStages * kStreamStageBytes + 256 + (kStreamMaxActive + 1) * 4;
+    1024 + kStreamStages * kStreamStageBytes + 256 + 4 * (kStreamMaxActive + 1) * 4;
 
 struct StreamArgs {
     const int32_t* offsets;
@@ -72,10 +74,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     int* s_misc = reinterpret_cast<int*>(tmem_slot + 2);  // [0] total tiles
     int* prefix = reinterpret_cast<int*>(smem + kStreamStages * kStreamStageBytes + 256);
+    int* t_seg0 = prefix + (kStreamMaxActive + 1);
+    int* t_rows = t_seg0 + (kStreamMaxActive + 1);
+    int* t_slot = t_rows + (kStreamMaxActive + 1);
 
     const int warp = static_cast<int>(threadIdx.x >> 5);
     const uint32_t lane = lane_id();
-    const int n_active = min(args.active[0], kStreamMaxActive);
+
     const int num_kb = args.K / kStreamBK;
     const int splits = args.splits;
 
@@ -103,6 +108,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
+    // Everything above is independent of the previous kernel; from here on the
+    // routing/packing results (and the previous FFN stage) are read.
+    griddep_wait();
+    griddep_launch();
+    const int n_active = min(args.active[0], kStreamMaxActive);
     // tiles per active expert = m_blocks * ceil(n_e / NT) -> exclusive prefix (warp 2)
     if (warp == 2) {
         const int per = (n_active + 31) / 32;
@@ -111,9 +121,18 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         for (int i = 0; i < per; ++i)
             if (b + i < n_active) {
                 const int e = args.active[1 + b + i];
-                const int rows = args.offsets[e + 1] - args.offsets[e];
+                const int seg0 = args.offsets[e];
+                const int rows = args.offsets[e + 1] - seg0;
+                int64_t slot = args.slot_of_expert ? args.slot_of_expert[e] : e;
+                if (slot < 0 || slot >= args.num_slots) {
+                    raise_error(PDX_DEVERR_BAD_SLOT);
+                    slot = 0;  // keeps the pipeline consistent; the call is flagged invalid
+                }
                 const int tiles = args.m_blocks * ((rows + NT - 1) / NT);
                 prefix[b + i] = tiles;
+                t_seg0[b + i] = seg0;
+                t_rows[b + i] = rows;
+                t_slot[b + i] = static_cast<int>(slot);
                 local += tiles;
             }
         int inc = local;
@@ -137,8 +156,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     const uint32_t tmem_base = *tmem_slot;
     const int total_units = s_misc[0] * splits;
 
-    // unit u -> tile u / splits (slices of one tile adjacent), slice u % splits
-    auto decode = [&](int u, int& e, int& ib, int& nb, int& kb0, int& kb1) {
+    // unit u -> tile u / splits (slices of one tile adjacent), slice u % splits;
+    // everything needed comes from the shared tables (no global loads per unit)
+    auto decode = [&](int u, int& a, int& ib, int& nb, int& kb0, int& kb1) {
         const int tile = u / splits;
         const int s = u % splits;
         int lo = 0, hi = n_active - 1;
@@ -146,9 +166,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
             const int mid = (lo + hi + 1) >> 1;
             if (prefix[mid] <= tile) lo = mid; else hi = mid - 1;
         }
-        e = args.active[1 + lo];
-        const int rows = args.offsets[e + 1] - args.offsets[e];
-        const int nbc = (rows + NT - 1) / NT;
+        a = lo;
+        const int nbc = (t_rows[lo] + NT - 1) / NT;
         const int local = tile - prefix[lo];
         ib = local / nbc;
         nb = local % nbc;
@@ -164,16 +183,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
             uint32_t phase = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
-                int e, ib, nb, kb0, kb1;
-                decode(u, e, ib, nb, kb0, kb1);
-                int64_t slot = args.slot_of_expert ? args.slot_of_expert[e] : e;
-                if (slot < 0 || slot >= args.num_slots) {
-                    raise_error(PDX_DEVERR_BAD_SLOT);
-                    slot = 0;
-                }
+                int a, ib, nb, kb0, kb1;
+                decode(u, a, ib, nb, kb0, kb1);
+                const int64_t slot = t_slot[a];
                 const int row_a0 = static_cast<int>(slot * args.a0_rows_per_slot) + ib * kStreamBM;
                 const int row_a1 = static_cast<int>(slot * args.a1_rows_per_slot) + ib * kStreamBM;
-                const int row_b = args.offsets[e] + nb * NT;
+                const int row_b = t_seg0[a] + nb * NT;
                 for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
                     unsigned char* sa = smem + stage * kStreamStageBytes;
@@ -194,8 +209,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         int lt = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++lt) {
-            int e, ib, nb, kb0, kb1;
-            decode(u, e, ib, nb, kb0, kb1);
+            int a, ib, nb, kb0, kb1;
+            decode(u, a, ib, nb, kb0, kb1);
             const int b = lt & 1;
             const uint32_t acc_phase = static_cast<uint32_t>(lt >> 1) & 1u;
             if (!mbar_wait(&tmem_empty[b], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
@@ -231,8 +246,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         const int i_row = q * 32 + static_cast<int>(lane);  // weight row within the tile
         int lt = 0;
         for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++lt) {
-            int e, ib, nb, kb0, kb1;
-            const int tile = decode(u, e, ib, nb, kb0, kb1);
+            int a, ib, nb, kb0, kb1;
+            const int tile = decode(u, a, ib, nb, kb0, kb1);
             const int b = lt & 1;
             const uint32_t acc_phase = static_cast<uint32_t>(lt >> 1) & 1u;
             if (!mbar_wait(&tmem_full[b], acc_phase, abort_flag)) break;
@@ -273,8 +288,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
                     for (int c = 0; c < kCols; ++c) acc[c] += __ldcg(p + c * kStreamBM + i_row);
                 }
             }
-            const int seg0 = args.offsets[e];
-            const int seg1 = args.offsets[e + 1];
+            const int seg0 = t_seg0[a];
+            const int seg1 = seg0 + t_rows[a];
             const int col = ib * kStreamBM + i_row;
 #pragma unroll
             for (int t = 0; t < NT; ++t) {

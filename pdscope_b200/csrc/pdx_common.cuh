@@ -149,6 +149,15 @@ __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
 
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialisation may start before its predecessor in the stream finishes;
+// griddep_wait() blocks until the predecessor has completed and its memory is
+// visible (every kernel of the chain calls it, so the guarantee is
+// transitive).  griddep_launch() lets the next kernel of the chain start its
+// prologue early.  Both are no-ops for a normal launch.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ bool elect_one() {
     uint32_t pred = 0;
     asm volatile(

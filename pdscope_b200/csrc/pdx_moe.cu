@@ -12,6 +12,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "combine.cu"
 #include "ffn_gemm.cu"
@@ -51,6 +52,32 @@ int ok() {
     do {                                                                                            \
         g_launches.fetch_add(1, std::memory_order_relaxed);                                         \
         cudaError_t _e = cudaGetLastError();                                                        \
+        if (_e != cudaSuccess) return fail(PDX_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(_e)); \
+    } while (0)
+
+// Launch with programmatic stream serialisation (PDL): the kernel may begin
+// while its predecessor in the stream is still running; it synchronises with
+// griddep_wait() before touching the predecessor's results.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+#define PDX_PDL_TRY(expr)                                                                             \
+    do {                                                                                              \
+        g_launches.fetch_add(1, std::memory_order_relaxed);                                           \
+        cudaError_t _e = (expr);                                                                      \
         if (_e != cudaSuccess) return fail(PDX_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(_e)); \
     } while (0)
 
@@ -213,41 +240,36 @@ struct RouteBufs {
     uint16_t* logits;
     int64_t* selected;
     uint16_t* weights;
-    unsigned int* ticket;
+    unsigned int* tickets;  // 1 + token blocks
 };
 
+size_t route_ticket_bytes(int64_t T) { return static_cast<size_t>(1 + (T + kRouteTB - 1) / kRouteTB) * 4; }
+
+// Routing: exact logits with top-k fused per token block (the k_topk launch is
+// only kept for pdx_topk_from_logits); with fused_pack the last token block
+// also packs (decode-sized batches).
 int launch_route(const void* x, const void* gate, int64_t T, int64_t H, int64_t E, int32_t k, int32_t normalize,
                  const RouteBufs& b, const PackOut* fused_pack, cudaStream_t stream) {
     const int n_tb = static_cast<int>((T + kRouteTB - 1) / kRouteTB);
     const int n_eb = static_cast<int>((E + kRouteEB - 1) / kRouteEB);
     RouteTail tail{};
-    const bool use_tail = T <= kTailMaxTokens;
+    PDX_CUDA_TRY(cudaMemsetAsync(b.tickets, 0, route_ticket_bytes(T), stream));
+    tail.enabled = 1;
+    tail.k = k;
+    tail.normalize = normalize;
+    tail.tickets = b.tickets;
+    tail.selected = b.selected;
+    tail.weights = b.weights;
     size_t smem = 0;
-    if (use_tail) {
-        PDX_CUDA_TRY(cudaMemsetAsync(b.ticket, 0, sizeof(unsigned int), stream));
-        tail.enabled = 1;
-        tail.k = k;
-        tail.normalize = normalize;
-        tail.ticket = b.ticket;
-        tail.selected = b.selected;
-        tail.weights = b.weights;
-        if (fused_pack) {
-            tail.do_pack = 1;
-            tail.pack = *fused_pack;
-            smem = static_cast<size_t>(E + E + 1 + (kRouteWarps * E)) * sizeof(int);
-        }
+    if (fused_pack) {
+        tail.do_pack = 1;
+        tail.pack = *fused_pack;
+        smem = static_cast<size_t>(E + E + 1 + (kRouteWarps * E)) * sizeof(int);
     }
     k_router_logits<<<n_tb * n_eb, kRouteWarps * 32, smem, stream>>>(
         static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gate), static_cast<int>(T), static_cast<int>(H),
         static_cast<int>(E), b.logits, tail);
     PDX_LAUNCHED();
-    if (!use_tail) {
-        const int warps_per_cta = 8;
-        const int grid = static_cast<int>((T + warps_per_cta - 1) / warps_per_cta);
-        k_topk<<<grid, warps_per_cta * 32, 0, stream>>>(b.logits, static_cast<int>(T), static_cast<int>(E), k,
-                                                        normalize, b.selected, b.weights);
-        PDX_LAUNCHED();
-    }
     return PDX_OK;
 }
 
@@ -304,7 +326,7 @@ StreamPlan plan_stream(int64_t rows, int64_t E, int64_t H, int64_t I) {
     const int64_t c1 = p.s1 > 1 ? p.tiles1 * p.s1 * 2 * p.nt : 0;
     const int64_t c2 = p.s2 > 1 ? p.tiles2 * p.s2 * p.nt : 0;
     p.partial_bytes = static_cast<size_t>(std::max(c1, c2)) * 128 * 4;
-    p.ticket_bytes = static_cast<size_t>(std::max(p.tiles1, p.tiles2)) * 4 * 4;
+    p.ticket_bytes = static_cast<size_t>(std::max(p.tiles1, p.tiles2)) * 4 * 4;  // per GEMM
     return p;
 }
 
@@ -313,7 +335,7 @@ size_t ffn_ws_bytes(int64_t rows, int64_t E, int64_t H, int64_t I, int mode) {
     if (mode == PDX_FFN_GEMM || mode == PDX_FFN_GEMV) b += align_up(static_cast<size_t>(rows) * H * 2);  // x rows
     if (mode == PDX_FFN_GEMV) {
         const StreamPlan p = plan_stream(rows, E, H, I);
-        b += align_up(p.partial_bytes) + align_up(p.ticket_bytes);
+        b += align_up(p.partial_bytes) + align_up(2 * p.ticket_bytes);
     }
     return b;
 }
@@ -323,12 +345,11 @@ int launch_stream_pair(const CUtensorMap& tm_g, const CUtensorMap& tm_u, const C
                        const CUtensorMap& tm_d, const CUtensorMap& tm_h, const StreamPlan& p, StreamArgs a1,
                        StreamArgs a2, int sms, cudaStream_t stream) {
     const int grid1 = static_cast<int>(std::min<int64_t>(sms, p.tiles1 * p.s1));
-    k_stream_gemm<NT, true><<<grid1, kStreamThreads, kStreamSmemBytes, stream>>>(tm_g, tm_u, tm_x, a1);
-    PDX_LAUNCHED();
-    if (p.s2 > 1) PDX_CUDA_TRY(cudaMemsetAsync(a2.tickets, 0, p.ticket_bytes, stream));
+    PDX_PDL_TRY(launch_pdl(k_stream_gemm<NT, true>, dim3(grid1), dim3(kStreamThreads), kStreamSmemBytes, stream,
+                           tm_g, tm_u, tm_x, a1));
     const int grid2 = static_cast<int>(std::min<int64_t>(sms, p.tiles2 * p.s2));
-    k_stream_gemm<NT, false><<<grid2, kStreamThreads, kStreamSmemBytes, stream>>>(tm_d, tm_d, tm_h, a2);
-    PDX_LAUNCHED();
+    PDX_PDL_TRY(launch_pdl(k_stream_gemm<NT, false>, dim3(grid2), dim3(kStreamThreads), kStreamSmemBytes, stream,
+                           tm_d, tm_d, tm_h, a2));
     return PDX_OK;
 }
 
@@ -348,7 +369,7 @@ int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* o
     if (mode == PDX_FFN_GEMV) {
         plan = plan_stream(rows, E, H, I);
         partials = static_cast<float*>(ws.take(std::max<size_t>(plan.partial_bytes, 16)));
-        tickets = static_cast<unsigned int*>(ws.take(plan.ticket_bytes));
+        tickets = static_cast<unsigned int*>(ws.take(2 * plan.ticket_bytes));  // GEMM1 | GEMM2
     }
     if (ws.overflow) return fail(PDX_ERR_WORKSPACE, "FFN workspace too small (%zu > %zu bytes)", ws.used, ws.cap);
     const ExpertSlab slab = to_slab(w);
@@ -382,10 +403,11 @@ int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* o
         PDX_LAUNCHED();
         return PDX_OK;
     }
-    // tcgen05 paths: gather the packed x rows once
-    k_gather_rows<<<static_cast<unsigned>(rows), kCombineThreads, 0, stream>>>(
-        static_cast<const uint16_t*>(x), tokens, static_cast<int>(rows), static_cast<int>(H), xp);
-    PDX_LAUNCHED();
+    // tcgen05 paths: gather the packed x rows once (and clear the split-K tickets)
+    const int zero_words = mode == PDX_FFN_GEMV ? static_cast<int>(2 * plan.ticket_bytes / 4) : 0;
+    PDX_PDL_TRY(launch_pdl(k_gather_rows, dim3(static_cast<unsigned>(rows)), dim3(kCombineThreads), 0, stream,
+                           static_cast<const uint16_t*>(x), tokens, static_cast<int>(rows), static_cast<int>(H), xp,
+                           tickets, zero_words));
     const int64_t gs = w->num_slots > 1 ? w->gate_stride / H : 0;
     const int64_t us = w->num_slots > 1 ? w->up_stride / H : 0;
     const int64_t ds = w->num_slots > 1 ? w->down_stride / I : 0;
@@ -398,11 +420,11 @@ int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* o
         if ((st = encode_2d(&tm_x, xp, rows, H, plan.nt))) return st;
         if ((st = encode_2d(&tm_h, h, rows, I, plan.nt))) return st;
         if ((st = encode_2d(&tm_d, w->down, (w->num_slots - 1) * ds + H, I, 128))) return st;
-        if (plan.s1 > 1) PDX_CUDA_TRY(cudaMemsetAsync(tickets, 0, plan.ticket_bytes, stream));
         StreamArgs a1{offsets, active, w->slot_of_expert, w->num_slots, gs, us, static_cast<int>(H),
                       static_cast<int>(I / 128), plan.s1, h, I, partials, tickets};
         StreamArgs a2{offsets, active, w->slot_of_expert, w->num_slots, ds, ds, static_cast<int>(I),
-                      static_cast<int>(H / 128), plan.s2, static_cast<uint16_t*>(y), H, partials, tickets};
+                      static_cast<int>(H / 128), plan.s2, static_cast<uint16_t*>(y), H, partials,
+                      tickets + plan.ticket_bytes / 4};
         if (plan.nt == 16) return launch_stream_pair<16>(tm_g, tm_u, tm_x, tm_d, tm_h, plan, a1, a2, sms, stream);
         return launch_stream_pair<32>(tm_g, tm_u, tm_x, tm_d, tm_h, plan, a1, a2, sms, stream);
     }
@@ -414,13 +436,13 @@ int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* o
     GemmArgs a1{offsets, active, w->slot_of_expert, w->num_slots, gs, us, static_cast<int>(H),
                 static_cast<int>(I), 1, h, I};
     const int grid1 = static_cast<int>(std::min<int64_t>(sms, m_tiles_bound * (I / (kGemmBN / 2))));
-    k_grouped_gemm<<<grid1, kGemmThreads, kGemmSmemBytes, stream>>>(tm_x, tm_g, tm_u, a1);
-    PDX_LAUNCHED();
+    PDX_PDL_TRY(launch_pdl(k_grouped_gemm, dim3(grid1), dim3(kGemmThreads), kGemmSmemBytes, stream, tm_x, tm_g,
+                           tm_u, a1));
     GemmArgs a2{offsets, active, w->slot_of_expert, w->num_slots, ds, ds, static_cast<int>(I),
                 static_cast<int>(H), 0, static_cast<uint16_t*>(y), H};
     const int grid2 = static_cast<int>(std::min<int64_t>(sms, m_tiles_bound * (H / kGemmBN)));
-    k_grouped_gemm<<<grid2, kGemmThreads, kGemmSmemBytes, stream>>>(tm_h, tm_d, tm_d, a2);
-    PDX_LAUNCHED();
+    PDX_PDL_TRY(launch_pdl(k_grouped_gemm, dim3(grid2), dim3(kGemmThreads), kGemmSmemBytes, stream, tm_h, tm_d,
+                           tm_d, a2));
     return PDX_OK;
 }
 
@@ -469,7 +491,8 @@ int pdx_abi_version(void) { return PDX_ABI_VERSION; }
 uint64_t pdx_launch_count(void) { return g_launches.load(); }
 
 size_t pdx_route_workspace_bytes(int64_t T, int64_t E) {
-    return align_up(256) + align_up(static_cast<size_t>(std::max<int64_t>(T, 0)) * std::max<int64_t>(E, 0) * 2);
+    T = std::max<int64_t>(T, 1);
+    return align_up(route_ticket_bytes(T)) + align_up(static_cast<size_t>(T) * std::max<int64_t>(E, 0) * 2);
 }
 
 int pdx_route_topk(const void* x, const void* gate, int64_t T, int64_t H, int64_t E, int32_t top_k, int32_t normalize,
@@ -482,7 +505,7 @@ int pdx_route_topk(const void* x, const void* gate, int64_t T, int64_t H, int64_
         return fail(PDX_ERR_WORKSPACE, "workspace must be non-null and 256-byte aligned");
     Carver c{static_cast<char*>(workspace), workspace_bytes};
     RouteBufs b;
-    b.ticket = static_cast<unsigned int*>(c.take(256));
+    b.tickets = static_cast<unsigned int*>(c.take(route_ticket_bytes(T)));
     b.logits = logits_out ? static_cast<uint16_t*>(logits_out) : static_cast<uint16_t*>(c.take(T * E * 2));
     b.selected = selected_out;
     b.weights = static_cast<uint16_t*>(weights_out);
@@ -531,7 +554,7 @@ int pdx_gather_rows(const void* x, const int32_t* tokens, int64_t rows, int64_t 
     if (rows == 0) return ok();
     k_gather_rows<<<static_cast<unsigned>(rows), kCombineThreads, 0, stream>>>(
         static_cast<const uint16_t*>(x), tokens, static_cast<int>(rows), static_cast<int>(H),
-        static_cast<uint16_t*>(out));
+        static_cast<uint16_t*>(out), nullptr, 0);
     PDX_LAUNCHED();
     return ok();
 }
@@ -608,7 +631,7 @@ size_t pdx_layer_workspace_bytes(int64_t T, int64_t H, int64_t E, int32_t top_k,
     top_k = std::max<int32_t>(top_k, 1);
     const int64_t N = T * top_k;
     Carver c{nullptr, SIZE_MAX};
-    c.take(256);                 // ticket
+    c.take(route_ticket_bytes(T));  // route tickets
     c.take(T * E * 2);           // logits
     c.take(N * 8);               // selected
     c.take(N * 2);               // weights
@@ -633,7 +656,7 @@ int pdx_moe_layer(const void* x, const void* gate, int64_t T, int64_t H, int64_t
     const int64_t N = T * top_k;
     Carver c{static_cast<char*>(workspace), workspace_bytes};
     RouteBufs rb;
-    rb.ticket = static_cast<unsigned int*>(c.take(256));
+    rb.tickets = static_cast<unsigned int*>(c.take(route_ticket_bytes(T)));
     rb.logits = logits_out ? static_cast<uint16_t*>(logits_out) : static_cast<uint16_t*>(c.take(T * E * 2));
     rb.selected = selected_out ? selected_out : static_cast<int64_t*>(c.take(N * 8));
     rb.weights = weights_out ? static_cast<uint16_t*>(weights_out) : static_cast<uint16_t*>(c.take(N * 2));
@@ -645,10 +668,11 @@ int pdx_moe_layer(const void* x, const void* gate, int64_t T, int64_t H, int64_t
     if (!fused && (st = launch_pack(rb.selected, rb.weights, T, top_k, E, pb.o, pb.chunk_hist, stream))) return st;
     if ((st = launch_ffn(x, T, pb.o.tokens, pb.o.offsets, pb.o.active, E, N, weights, H, I, y, m, c, stream)))
         return st;
-    k_combine<<<static_cast<unsigned>(T), kCombineThreads, 0, stream>>>(
-        y, rb.weights, pb.o.inverse, static_cast<int>(T), top_k, static_cast<int>(H),
-        static_cast<const uint16_t*>(residual), static_cast<uint16_t*>(out));
-    PDX_LAUNCHED();
+    PDX_PDL_TRY(launch_pdl(k_combine, dim3(static_cast<unsigned>(T)), dim3(kCombineThreads), 0, stream,
+                           static_cast<const uint16_t*>(y), static_cast<const uint16_t*>(rb.weights),
+                           static_cast<const int32_t*>(pb.o.inverse), static_cast<int>(T), static_cast<int>(top_k),
+                           static_cast<int>(H), static_cast<const uint16_t*>(residual),
+                           static_cast<uint16_t*>(out)));
     return ok();
 }
 

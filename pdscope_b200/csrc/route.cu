@@ -9,13 +9,14 @@ namespace pdx {
 constexpr int kRouteTB = 8;       // tokens per CTA block
 constexpr int kRouteEB = 8;       // experts per CTA block
 constexpr int kRouteWarps = 8;    // warps per CTA, each owning a share of K
+static_assert(kRouteWarps == kRouteTB, "the fused tail routes one token per warp");
 
 struct RouteTail {
-    int enabled;           // 1: last CTA runs top-k (+ pack) for every token
+    int enabled;           // 1: top-k in this kernel (per token block), 0: k_topk follows
     int k;
     int normalize;
-    int do_pack;
-    unsigned int* ticket;  // zeroed by the host before the launch
+    int do_pack;           // 1: the last token block to finish also packs every token
+    unsigned int* tickets; // [1 + token blocks], zeroed by the host before the launch
     int64_t* selected;
     uint16_t* weights;
     PackOut pack;
@@ -101,19 +102,29 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_router_logits(const uint16
         if (t < T && e < E) logits[static_cast<size_t>(t) * E + e] = f64_to_bf16_bits(sum);
     }
     if (!tail.enabled) return;
-    // ---- fused tail: the last CTA to finish routes and packs every token ----
+    // ---- fused tail -------------------------------------------------------------
+    // The CTA that completes a token block (its n_eb expert blocks all written)
+    // routes those 8 tokens, one warp each; with do_pack, the last token block to
+    // finish then packs every token.  Threadfence-reduction pattern: writers
+    // fence before the ticket, the winner fences after it.
     __shared__ unsigned int s_ticket;
+    const int tb = static_cast<int>(blockIdx.x) / n_eb;
+    const int n_tb = (T + kRouteTB - 1) / kRouteTB;
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) s_ticket = atomicAdd(tail.ticket, 1u);
+    if (threadIdx.x == 0) s_ticket = atomicAdd(&tail.tickets[1 + tb], 1u);
     __syncthreads();
-    if (s_ticket != gridDim.x - 1) return;
+    if (s_ticket != static_cast<unsigned int>(n_eb - 1)) return;
     __threadfence();
-    const int nwarps = static_cast<int>(blockDim.x >> 5);
-    topk_rows_dispatch(logits, T, E, tail.k, tail.normalize != 0, tail.selected, tail.weights, warp, nwarps);
+    const int t = tb * kRouteTB + warp;  // kRouteWarps == kRouteTB: one token per warp
+    if (t < T) topk_row(logits, t, E, tail.k, tail.normalize != 0, tail.selected, tail.weights);
     if (!tail.do_pack) return;
-    __threadfence_block();
+    __threadfence();
     __syncthreads();
+    if (threadIdx.x == 0) s_ticket = atomicAdd(&tail.tickets[0], 1u);
+    __syncthreads();
+    if (s_ticket != static_cast<unsigned int>(n_tb - 1)) return;
+    __threadfence();
     extern __shared__ int smem_i[];
     int* hist = smem_i;
     int* excl = hist + E;

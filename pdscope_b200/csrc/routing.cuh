@@ -90,6 +90,19 @@ __device__ __forceinline__ void warp_softmax_topk(const uint16_t* __restrict__ l
         for (int off = 1; off < width; off <<= 1) a += __shfl_down_sync(0xffffffffu, a, off);
         denom = __shfl_sync(0xffffffffu, a, 0);
     }
+    // No two selected probabilities equal: every correct sort gives the
+    // selection order, so the bitonic ordering below is only needed with ties.
+    {
+        const float next_p = __shfl_down_sync(0xffffffffu, my_p, 1);
+        const bool tie_here = static_cast<int>(lane) + 1 < k && next_p == my_p;
+        if (!__any_sync(0xffffffffu, tie_here)) {
+            if (static_cast<int>(lane) < k) {
+                sel_out[lane] = my_idx;
+                w_out[lane] = f2bits(normalize ? __fdiv_rn(my_p, denom) : my_p);
+            }
+            return;
+        }
+    }
     // ---- order the selection as torch.topk(sorted=True) returns it on CUDA ----
     // (1) gather order: values above the k-th largest in index order, then the
     //     values equal to it in index order;
@@ -142,6 +155,20 @@ __device__ __forceinline__ void block_topk_rows(const uint16_t* logits, int T, i
     for (int t = warp_begin; t < T; t += warp_stride)
         warp_softmax_topk<EPL>(logits + static_cast<size_t>(t) * E, E, k, normalize,
                                selected + static_cast<size_t>(t) * k, weights + static_cast<size_t>(t) * k);
+}
+
+// one token by the calling warp, dispatch on E (<= 1024)
+__device__ __forceinline__ void topk_row(const uint16_t* logits, int t, int E, int k, bool normalize,
+                                         int64_t* selected, uint16_t* weights) {
+    const uint16_t* row = logits + static_cast<size_t>(t) * E;
+    int64_t* so = selected + static_cast<size_t>(t) * k;
+    uint16_t* wo = weights + static_cast<size_t>(t) * k;
+    if (E <= 32) warp_softmax_topk<1>(row, E, k, normalize, so, wo);
+    else if (E <= 64) warp_softmax_topk<2>(row, E, k, normalize, so, wo);
+    else if (E <= 128) warp_softmax_topk<4>(row, E, k, normalize, so, wo);
+    else if (E <= 256) warp_softmax_topk<8>(row, E, k, normalize, so, wo);
+    else if (E <= 512) warp_softmax_topk<16>(row, E, k, normalize, so, wo);
+    else warp_softmax_topk<32>(row, E, k, normalize, so, wo);
 }
 
 // dispatch on E (<= 1024)
