@@ -243,6 +243,8 @@ def main():
     K, W = max(1, args.steps), max(3, args.warmup)
     pk = peaks()
     L = args.layers
+    if world > 1:
+        return run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L)
     stack = build_stack(L, CFG["hidden"], CFG["experts"], CFG["inter"], CFG["top_k"], device=dev, seed=rank)
     torch.cuda.synchronize(dev)
 
@@ -290,6 +292,7 @@ def main():
                                weight_gb_per_step=sum(act) * EXPERT_BYTES / 1e9,
                                launches_per_step=launches_per_step, clocks=clocks)
         decode[t_count]["hbm_gbs_step"] = decode[t_count]["weight_gb_per_step"] / (decode[t_count]["ms_per_step"] / 1e3)
+        decode[t_count]["stage_us_per_layer"] = stack.stage_times_us(t_count)
 
     # ---- roofline of the dominant kernel: grouped FFN GEMV at the headline batch ----
     t_count = headline_t
@@ -336,6 +339,7 @@ def main():
         b = pstack.buffers(tp)
         c0 = b["stages"][0].counts.float()
         top16 = float(torch.topk(c0, 16).values.sum() / c0.sum())
+        stages_p = pstack.stage_times_us(tp, layers=4, repeats=1)
         pstack.stage_once(tp)
         gp = pstack.ffn_graph(tp)
         ffn_ms_p = timed(gp.replay, pk_steps, 1)
@@ -344,6 +348,7 @@ def main():
         tflops = flops_launch / per_launch_p / 1e12
         prefill = dict(tokens=tp, lengths=lengths, ms_per_step=ms / pk_steps,
                        tok_s=sum_over_ranks(tp) * pk_steps / (ms / 1e3), top16_share_layer0=top16,
+                       stage_us_per_layer=stages_p,
                        zipf=dict(s=ZIPF_S, alpha=ZIPF_ALPHA),
                        roofline=dict(bound="tensor", kernel="pdx_moe_ffn_grouped tcgen05 (gather + 2x k_grouped_gemm)",
                                      achieved=tflops, unit="TFLOP/s", peak=pk["bf16_tflops_sustained"],
@@ -395,6 +400,111 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+    return 0
+
+
+def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
+    """N > 1: the 48-layer stack with experts sharded 128/N per GPU (expert e on
+    rank e // (128/N)), NCCL all-to-all dispatch/combine, decode batch per rank
+    fixed (weak scaling); one CUDA graph per step on every rank."""
+    import torch
+    from pdscope_b200 import _lib
+    from pdscope_b200.expert_parallel import ExpertParallelStack, TorchDistExchange
+    from pdscope_b200.runtime import ExpertSlab
+    from pdscope_b200.stack import activations
+
+    E, H, I, k = CFG["experts"], CFG["hidden"], CFG["inter"], CFG["top_k"]
+    if E % world:
+        raise SystemExit(f"{E} experts do not divide over {world} GPUs")
+    el = E // world
+    g_gate = torch.Generator(device=dev).manual_seed(0)          # routers replicated on every rank
+    g_w = torch.Generator(device=dev).manual_seed(1000 + rank)   # this rank's experts
+    gates = [(torch.randn(E, H, device=dev, generator=g_gate) * 0.02).to(torch.bfloat16) for _ in range(L)]
+    slabs = [ExpertSlab.allocate(el, H, I, dev, generator=g_w) for _ in range(L)]
+    stack = ExpertParallelStack(gates, slabs, rank=rank, world=world, exchange=TorchDistExchange(), top_k=k)
+    torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn, steps, warm):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        s = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(steps):
+            fn()
+        e1.record(s)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        return max_over_ranks(e0.elapsed_time(e1))
+
+    decode = {}
+    headline_t = args.decode_batch
+    extra = [int(v) for v in args.decode_batches.split(",") if v.strip()]
+    clocks = None
+    for t_count in sorted(set(extra) | {headline_t}):
+        x, _ = stack.io(t_count)
+        x.copy_(activations(t_count, H, device=dev, seed=10 + t_count + 1000 * rank))
+        n0 = _lib.lib.pdx_launch_count()
+        stack.step(t_count)
+        torch.cuda.synchronize(dev)
+        launches = (_lib.lib.pdx_launch_count() - n0) // 2
+        if t_count == headline_t:
+            sampler = ClockSampler(local_rank)
+            with sampler:
+                ms = timed(lambda: stack.step(t_count), K, W)
+            clocks = sampler.summary()
+        else:
+            ms = timed(lambda: stack.step(t_count), K, W)
+        local_bytes = L * el * EXPERT_BYTES  # every local expert receives rows at these batch sizes x ranks
+        decode[t_count] = dict(ms_per_step=ms / K, tok_s=world * t_count * K / (ms / 1e3),
+                               launches_per_step=launches,
+                               local_weight_gb_per_step=local_bytes / 1e9,
+                               hbm_gbs_step_per_gpu=local_bytes / 1e9 / (ms / K / 1e3))
+    t_count = headline_t
+    x, y = stack.io(t_count)
+    host_in = activations(t_count, H, device=dev, seed=5 + rank).cpu().pin_memory()
+    host_out = torch.empty((t_count, H), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        x.copy_(host_in, non_blocking=True)
+        stack.step(t_count)
+        host_out.copy_(y, non_blocking=True)
+
+    e2e_ms = timed(e2e_step, K, W)
+    stack.release_graphs()
+    d = decode[headline_t]
+    if rank == 0:
+        line = dict(metric=METRIC, value=d["tok_s"], unit="tok/s", n_gpus=world, steps=K, warmup=W,
+                    ms_per_step=d["ms_per_step"], higher_is_better=True, scaling="weak", vs_baseline=None,
+                    dtype="bf16", data="synthetic",
+                    config=dict(workload=f"config2 decode batch {headline_t} per GPU: 48-layer Qwen3-30B-A3B-shape "
+                                         f"MoE stack, expert parallel {el} experts/GPU, NCCL all-to-all "
+                                         f"dispatch/combine, one CUDA graph per step",
+                                hidden=H, experts=E, inter=I, top_k=k, layers=L, decode_batch=headline_t,
+                                global_batch=headline_t * world, parallelism=f"ep{world}",
+                                l2="not flushed: each step streams the rank's %.1f GB of expert weights"
+                                   % d["local_weight_gb_per_step"]),
+                    roofline=dict(bound="hbm", kernel="whole expert-parallel decode step (local expert weights "
+                                                      "per step / step time, per GPU)",
+                                  achieved=d["hbm_gbs_step_per_gpu"], peak=pk["hbm_gbs"], unit="GB/s",
+                                  frac=d["hbm_gbs_step_per_gpu"] / pk["hbm_gbs"], peak_source=pk["source"],
+                                  traffic=None),
+                    cpu_baseline=None,
+                    e2e=dict(value=world * t_count * K / (e2e_ms / 1e3), unit="tok/s",
+                             h2d_bytes_per_step=host_in.numel() * 2, d2h_bytes_per_step=host_out.numel() * 2,
+                             ms_per_step=e2e_ms / K),
+                    clocks=clocks, gpu_launches=d["launches_per_step"] * K,
+                    decode={str(t): r for t, r in decode.items()}, prefill=None)
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
     return 0
 
 

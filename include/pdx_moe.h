@@ -148,7 +148,7 @@ int pdx_gather_rows(const void *x, const int32_t *tokens, int64_t rows, int64_t 
  * for every packed row p of every active expert, UNWEIGHTED, in packed order,
  * with the reference's BF16 roundings (after each linear, after silu, after
  * the product).  `x` is the [T,H] token matrix; rows are gathered through
- * `tokens`.  mode: 0 = auto; 1 = decode path (weights streamed by TMA as the
+ * `tokens` (tokens == NULL: x already holds the `rows` rows in packed order).  mode: 0 = auto; 1 = decode path (weights streamed by TMA as the
  * tcgen05 M operand, tokens as N, split-K for few experts); 2 = prefill path
  * (tcgen05 grouped GEMM tiled over tokens); 3 = SIMT weight-streaming GEMV
  * (an independent implementation kept for cross-checks and for shapes the
@@ -201,6 +201,52 @@ int pdx_moe_layer(const void *x, const void *gate, int64_t T, int64_t H, int64_t
                   int64_t *selected_out, void *weights_out, int32_t *counts_out,
                   int32_t mode, void *workspace, size_t workspace_bytes,
                   pdx_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Expert parallelism.  No counterpart in the reference (single-GPU); these
+ * lay the same layer out over `ranks` GPUs with expert e on rank e / EL,
+ * EL = E / ranks; the exchange itself is NCCL all-to-all (see
+ * pdscope_b200/expert_parallel.py).
+ *
+ * pdx_ep_dispatch: after route + pack, copy each packed row p (expert e,
+ * destination d = e / EL, position pos = p - offsets[d*EL]) from x[tokens[p]]
+ * to send_rows[d*capacity + pos] and set inv_ep[positions[p]] = d*capacity +
+ * pos.  capacity must be >= T*min(top_k, EL) (the most rows one rank can send
+ * to another).
+ */
+int pdx_ep_dispatch(const void *x, const int32_t *tokens, const int32_t *positions,
+                    const int32_t *offsets, int64_t T, int32_t top_k, int64_t H, int64_t E,
+                    int32_t ranks, int64_t capacity, void *send_rows, int32_t *inv_ep,
+                    pdx_stream_t stream);
+
+/* pdx_ep_layout: from recv_counts[s*EL + l] (rows received from rank s for
+ * local expert l) build the regrouped layout in which each local expert's
+ * rows from every source are contiguous (sources in rank order):
+ * offsets_l[EL+1] (offsets_l[EL] = rows received), active_l[EL+1] (format of
+ * pdx_pack's active) and perm[g] = receive-buffer row of regrouped row g.
+ * capacity > 0: source block s starts at s*capacity in the receive buffer;
+ * capacity == 0: blocks are back to back.  rows_cap = rows of the receive
+ * buffer (and of perm); nothing is written past it. */
+int pdx_ep_layout(const int32_t *recv_counts, int32_t ranks, int64_t local_experts,
+                  int64_t capacity, int64_t rows_cap, int32_t *offsets_l, int32_t *active_l,
+                  int32_t *perm, pdx_stream_t stream);
+
+/* pdx_ep_regroup: grouped[g] = recv[perm[g]]; pdx_ep_ungroup:
+ * recv_layout[perm[g]] = grouped[g]; both for g < offsets_l[EL] (read on the
+ * device), rows_cap = rows of the receive buffer.  Between them,
+ * pdx_moe_ffn_grouped runs on `grouped` with tokens = NULL, offsets_l,
+ * active_l and the rank's EL local experts. */
+int pdx_ep_regroup(const void *recv, const int32_t *perm, const int32_t *offsets_l,
+                   int64_t local_experts, int64_t rows_cap, int64_t H, void *grouped,
+                   pdx_stream_t stream);
+int pdx_ep_ungroup(const void *grouped, const int32_t *perm, const int32_t *offsets_l,
+                   int64_t local_experts, int64_t rows_cap, int64_t H, void *recv_layout,
+                   pdx_stream_t stream);
+
+/* pdx_ep_combine: pdx_combine over y[y_rows, H] addressed through inv_ep. */
+int pdx_ep_combine(const void *y, int64_t y_rows, const void *weights, const int32_t *inv_ep,
+                   int64_t T, int32_t top_k, int64_t H, const void *residual, void *out,
+                   pdx_stream_t stream);
 
 /* Synchronise `stream`, then read and clear this device's error word.
  * *code_out receives a PDX_DEVERR_* value; returns PDX_ERR_DEVICE if nonzero. */

@@ -67,6 +67,12 @@ SIGNATURES = {
     "pdx_moe_layer": (ctypes.c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_i32,
                                      ctypes.POINTER(ExpertWeights), c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                                      c_i32, c_vp, c_sz, c_vp]),
+    "pdx_ep_dispatch": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i64, c_i64, c_i32, c_i64, c_vp, c_vp,
+                                       c_vp]),
+    "pdx_ep_layout": (ctypes.c_int, [c_vp, c_i32, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp]),
+    "pdx_ep_regroup": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),
+    "pdx_ep_ungroup": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),
+    "pdx_ep_combine": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i32, c_i64, c_vp, c_vp, c_vp]),
     "pdx_device_error": (ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_uint32)]),
 }
 

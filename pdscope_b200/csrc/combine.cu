@@ -31,10 +31,11 @@ __device__ __forceinline__ uint4 pack8(const float* f) {
 }
 
 // out[t] = bf16( residual[t] + sum_{s<k} bf16(y[inverse[t*k+s]] * w[t*k+s]) )
+// y has y_rows rows; inverse entries outside [0, y_rows) are flagged and skipped.
 __global__ void __launch_bounds__(kCombineThreads) k_combine(const uint16_t* __restrict__ y,
                                                              const uint16_t* __restrict__ weights,
                                                              const int32_t* __restrict__ inverse, int T, int k,
-                                                             int H, const uint16_t* __restrict__ residual,
+                                                             int H, int y_rows, const uint16_t* __restrict__ residual,
                                                              uint16_t* __restrict__ out) {
     griddep_wait();
     griddep_launch();
@@ -45,7 +46,7 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(const uint16_t* __r
     if (threadIdx.x < static_cast<unsigned>(k)) {
         int row = inverse[static_cast<size_t>(t) * k + threadIdx.x];
         float w = bits2f(weights[static_cast<size_t>(t) * k + threadIdx.x]);
-        if (row < 0 || row >= T * k) {  // not a permutation of [0, T*k): flag, contribute nothing
+        if (row < 0 || row >= y_rows) {  // not a valid row of y: flag, contribute nothing
             raise_error(PDX_DEVERR_BAD_EXPERT);
             row = 0;
             w = 0.f;
@@ -102,6 +103,14 @@ __global__ void __launch_bounds__(kCombineThreads) k_gather_rows(const uint16_t*
     for (int c = static_cast<int>(threadIdx.x) * 8; c < H; c += blockDim.x * 8)
         *reinterpret_cast<uint4*>(out + static_cast<size_t>(p) * H + c) =
             __ldg(reinterpret_cast<const uint4*>(x + src + c));
+}
+
+// Clears n words (the split-K tickets) when the FFN reads rows already in
+// packed order and no gather kernel runs.
+__global__ void k_zero_words(unsigned int* __restrict__ p, int n) {
+    griddep_wait();
+    griddep_launch();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = 0u;
 }
 
 }  // namespace pdx

@@ -111,8 +111,9 @@ __global__ void __launch_bounds__(kGemvThreads) k_gateup_gemv(const uint16_t* __
             const int vec_per_row = H / 8;
             for (int i = threadIdx.x; i < nt * vec_per_row; i += blockDim.x) {
                 const int t = i / vec_per_row, v = i % vec_per_row;
+                const int src_row = tokens ? tokens[c0 + t] : c0 + t;  // NULL: rows already in packed order
                 reinterpret_cast<uint4*>(xs + t * H)[v] =
-                    __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(tokens[c0 + t]) * H) + v);
+                    __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(src_row) * H) + v);
             }
             __syncthreads();
 #pragma unroll 1

@@ -19,6 +19,7 @@
 #include "ffn_gemv.cu"
 #include "ffn_stream.cu"
 #include "pack.cu"
+#include "ep.cu"
 #include "route.cu"
 
 namespace pdx {
@@ -403,11 +404,19 @@ int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* o
         PDX_LAUNCHED();
         return PDX_OK;
     }
-    // tcgen05 paths: gather the packed x rows once (and clear the split-K tickets)
+    // tcgen05 paths: gather the packed x rows once (and clear the split-K tickets);
+    // with tokens == NULL the rows of x are already in packed order.
     const int zero_words = mode == PDX_FFN_GEMV ? static_cast<int>(2 * plan.ticket_bytes / 4) : 0;
-    PDX_PDL_TRY(launch_pdl(k_gather_rows, dim3(static_cast<unsigned>(rows)), dim3(kCombineThreads), 0, stream,
-                           static_cast<const uint16_t*>(x), tokens, static_cast<int>(rows), static_cast<int>(H), xp,
-                           tickets, zero_words));
+    if (tokens) {
+        PDX_PDL_TRY(launch_pdl(k_gather_rows, dim3(static_cast<unsigned>(rows)), dim3(kCombineThreads), 0, stream,
+                               static_cast<const uint16_t*>(x), tokens, static_cast<int>(rows), static_cast<int>(H),
+                               xp, tickets, zero_words));
+    } else {
+        xp = static_cast<uint16_t*>(const_cast<void*>(x));
+        if (zero_words > 0)
+            PDX_PDL_TRY(launch_pdl(k_zero_words, dim3(std::min(64, (zero_words + 255) / 256)), dim3(256), 0, stream,
+                                   tickets, zero_words));
+    }
     const int64_t gs = w->num_slots > 1 ? w->gate_stride / H : 0;
     const int64_t us = w->num_slots > 1 ? w->up_stride / H : 0;
     const int64_t ds = w->num_slots > 1 ? w->down_stride / I : 0;
@@ -570,7 +579,7 @@ int pdx_moe_ffn_grouped(const void* x, int64_t T, const int32_t* tokens, const i
                         const int32_t* active, int64_t E, int64_t rows, const pdx_expert_weights* weights, int64_t H,
                         int64_t I, void* y_out, int32_t mode, void* workspace, size_t workspace_bytes,
                         pdx_stream_t stream) {
-    if (!x || !tokens || !offsets || !active || !y_out) return fail(PDX_ERR_INVALID, "null FFN argument");
+    if (!x || !offsets || !active || !y_out) return fail(PDX_ERR_INVALID, "null FFN argument");
     if (T < 1 || rows < 1 || E < 1) return fail(PDX_ERR_INVALID, "empty FFN batch");
     const int m = resolve_mode(mode, T, H, I);
     int st = check_ffn_shape(H, I, m);
@@ -620,7 +629,8 @@ int pdx_combine(const void* y, const void* weights, const int32_t* inverse, int6
     if (H < 8 || H % 8) return fail(PDX_ERR_UNSUPPORTED, "H must be a positive multiple of 8");
     k_combine<<<static_cast<unsigned>(T), kCombineThreads, 0, stream>>>(
         static_cast<const uint16_t*>(y), static_cast<const uint16_t*>(weights), inverse, static_cast<int>(T), top_k,
-        static_cast<int>(H), static_cast<const uint16_t*>(residual), static_cast<uint16_t*>(out));
+        static_cast<int>(H), static_cast<int>(T * top_k), static_cast<const uint16_t*>(residual),
+        static_cast<uint16_t*>(out));
     PDX_LAUNCHED();
     return ok();
 }
@@ -671,7 +681,71 @@ int pdx_moe_layer(const void* x, const void* gate, int64_t T, int64_t H, int64_t
     PDX_PDL_TRY(launch_pdl(k_combine, dim3(static_cast<unsigned>(T)), dim3(kCombineThreads), 0, stream,
                            static_cast<const uint16_t*>(y), static_cast<const uint16_t*>(rb.weights),
                            static_cast<const int32_t*>(pb.o.inverse), static_cast<int>(T), static_cast<int>(top_k),
-                           static_cast<int>(H), static_cast<const uint16_t*>(residual),
+                           static_cast<int>(H), static_cast<int>(N), static_cast<const uint16_t*>(residual),
+                           static_cast<uint16_t*>(out)));
+    return ok();
+}
+
+int pdx_ep_dispatch(const void* x, const int32_t* tokens, const int32_t* positions, const int32_t* offsets, int64_t T,
+                    int32_t top_k, int64_t H, int64_t E, int32_t ranks, int64_t capacity, void* send_rows,
+                    int32_t* inv_ep, pdx_stream_t stream) {
+    if (!x || !tokens || !positions || !offsets || !send_rows || !inv_ep) return fail(PDX_ERR_INVALID, "null EP argument");
+    if (T < 1 || top_k < 1 || ranks < 1 || E % ranks || capacity < 1)
+        return fail(PDX_ERR_INVALID, "EP dispatch needs T, top_k >= 1, E divisible by ranks, capacity >= 1");
+    if (H < 8 || H % 8) return fail(PDX_ERR_UNSUPPORTED, "H must be a positive multiple of 8");
+    if (static_cast<int64_t>(ranks) * capacity >= (int64_t(1) << 31)) return fail(PDX_ERR_UNSUPPORTED, "capacity too large");
+    const int64_t rows = T * top_k;
+    PDX_PDL_TRY(launch_pdl(k_ep_dispatch, dim3(static_cast<unsigned>(rows)), dim3(256), 0, stream,
+                           static_cast<const uint16_t*>(x), tokens, positions, offsets, static_cast<int>(rows),
+                           static_cast<int>(H), static_cast<int>(E), static_cast<int>(E / ranks), capacity,
+                           static_cast<uint16_t*>(send_rows), inv_ep));
+    return ok();
+}
+
+int pdx_ep_layout(const int32_t* recv_counts, int32_t ranks, int64_t local_experts, int64_t capacity,
+                  int64_t rows_cap, int32_t* offsets_l, int32_t* active_l, int32_t* perm, pdx_stream_t stream) {
+    if (!recv_counts || !offsets_l || !active_l || !perm) return fail(PDX_ERR_INVALID, "null EP argument");
+    if (ranks < 1 || local_experts < 1 || capacity < 0) return fail(PDX_ERR_INVALID, "invalid EP layout");
+    if (ranks * local_experts > kEpMaxExperts) return fail(PDX_ERR_UNSUPPORTED, "more than %d experts", kEpMaxExperts);
+    if (rows_cap < 0 || rows_cap >= (int64_t(1) << 31)) return fail(PDX_ERR_UNSUPPORTED, "receive buffer too large");
+    PDX_PDL_TRY(launch_pdl(k_ep_layout, dim3(1), dim3(1024), 0, stream, recv_counts, static_cast<int>(ranks),
+                           static_cast<int>(local_experts), capacity, static_cast<int>(rows_cap), offsets_l,
+                           active_l, perm));
+    return ok();
+}
+
+int pdx_ep_regroup(const void* recv, const int32_t* perm, const int32_t* offsets_l, int64_t local_experts,
+                   int64_t rows_cap, int64_t H, void* grouped, pdx_stream_t stream) {
+    if (!recv || !perm || !offsets_l || !grouped) return fail(PDX_ERR_INVALID, "null EP argument");
+    if (H < 8 || H % 8) return fail(PDX_ERR_UNSUPPORTED, "H must be a positive multiple of 8");
+    if (rows_cap < 1) return ok();
+    PDX_PDL_TRY(launch_pdl(k_ep_regroup, dim3(static_cast<unsigned>(rows_cap)), dim3(256), 0, stream,
+                           static_cast<const uint16_t*>(recv), perm, offsets_l, static_cast<int>(local_experts),
+                           static_cast<int>(rows_cap), static_cast<int>(H), static_cast<uint16_t*>(grouped)));
+    return ok();
+}
+
+int pdx_ep_ungroup(const void* grouped, const int32_t* perm, const int32_t* offsets_l, int64_t local_experts,
+                   int64_t rows_cap, int64_t H, void* recv_layout, pdx_stream_t stream) {
+    if (!grouped || !perm || !offsets_l || !recv_layout) return fail(PDX_ERR_INVALID, "null EP argument");
+    if (H < 8 || H % 8) return fail(PDX_ERR_UNSUPPORTED, "H must be a positive multiple of 8");
+    if (rows_cap < 1) return ok();
+    PDX_PDL_TRY(launch_pdl(k_ep_ungroup, dim3(static_cast<unsigned>(rows_cap)), dim3(256), 0, stream,
+                           static_cast<const uint16_t*>(grouped), perm, offsets_l, static_cast<int>(local_experts),
+                           static_cast<int>(rows_cap), static_cast<int>(H), static_cast<uint16_t*>(recv_layout)));
+    return ok();
+}
+
+int pdx_ep_combine(const void* y, int64_t y_rows, const void* weights, const int32_t* inv_ep, int64_t T,
+                   int32_t top_k, int64_t H, const void* residual, void* out, pdx_stream_t stream) {
+    if (!y || !weights || !inv_ep || !out) return fail(PDX_ERR_INVALID, "null combine argument");
+    if (T < 1 || top_k < 1 || y_rows < 1) return fail(PDX_ERR_INVALID, "empty combine");
+    if (top_k > kMaxTopK) return fail(PDX_ERR_UNSUPPORTED, "top_k > %d", kMaxTopK);
+    if (H < 8 || H % 8) return fail(PDX_ERR_UNSUPPORTED, "H must be a positive multiple of 8");
+    PDX_PDL_TRY(launch_pdl(k_combine, dim3(static_cast<unsigned>(T)), dim3(kCombineThreads), 0, stream,
+                           static_cast<const uint16_t*>(y), static_cast<const uint16_t*>(weights), inv_ep,
+                           static_cast<int>(T), static_cast<int>(top_k), static_cast<int>(H),
+                           static_cast<int>(y_rows), static_cast<const uint16_t*>(residual),
                            static_cast<uint16_t*>(out)));
     return ok();
 }

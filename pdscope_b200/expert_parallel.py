@@ -1,0 +1,281 @@
+"""Expert parallelism for the MoE layer: experts sharded over GPUs.
+
+The reference is single-GPU (one process, experts resident or offloaded).
+This module serves the same layer with the 128 experts split evenly over the
+ranks of a process group -- expert e on rank e // EL, EL = E / ranks -- and
+one NCCL all-to-all each way over NVLink.  Each rank owns its own tokens;
+routing is replicated (every rank holds the router).
+
+Per layer on every rank:
+  1. route + pack locally (all E experts)                     pdx_route_topk, pdx_pack
+  2. dispatch: packed rows for rank d are the contiguous range of experts
+     [d*EL, (d+1)*EL); all-to-all of the per-expert counts, then of the rows
+  3. the received rows are laid out as "virtual experts" (source rank, local
+     expert) that reuse the local weight slots; one grouped FFN   pdx_ep_layout,
+                                                                 pdx_moe_ffn_grouped
+  4. all-to-all of the unweighted rows back, weighted combine in slot order
+                                                                 pdx_ep_combine / pdx_combine
+Two exchange forms:
+  * padded (decode, T <= 64): every (source, destination) block has the fixed
+    capacity T*min(k, EL) rows, so sizes never leave the device (no host sync;
+    the whole step can be captured in a CUDA graph);
+  * exact (prefill): the counts are read back to size an exact all-to-all
+    (one host sync per layer, like the reference's grouping sync).
+Arithmetic per row is identical to the single-GPU layer, so outputs match it
+bit for bit (the same rows meet the same weights; combine order is slot order).
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import check, lib
+from .runtime import ExpertSlab, Packed, _ptr, _stream, pack as _pack
+
+PADDED_MAX_TOKENS = 64
+
+
+@dataclass
+class Layout:
+    """Regrouped receive buffer: local expert l's rows from all sources at
+    [offsets[l], offsets[l+1]); perm[g] = receive-buffer row of regrouped row g."""
+    offsets: torch.Tensor   # int32 [EL+1]
+    active: torch.Tensor    # int32 [EL+1]
+    perm: torch.Tensor      # int32 [rows_cap]
+    experts: int            # EL
+
+
+class DeviceOps:
+    """The sm_100a kernels used by ExpertParallelMoE (libpdx_moe)."""
+
+    def route(self, x, gate, top_k, normalize):
+        t_count, hidden = x.shape
+        experts = gate.shape[0]
+        dev = x.device
+        logits = torch.empty((t_count, experts), dtype=torch.bfloat16, device=dev)
+        sel = torch.empty((t_count, top_k), dtype=torch.int64, device=dev)
+        w = torch.empty((t_count, top_k), dtype=torch.bfloat16, device=dev)
+        ws = torch.empty(lib.pdx_route_workspace_bytes(t_count, experts), dtype=torch.uint8, device=dev)
+        check(lib.pdx_route_topk(_ptr(x), _ptr(gate), t_count, hidden, experts, top_k, int(normalize), _ptr(logits),
+                                 _ptr(sel), _ptr(w), _ptr(ws), ws.numel(), _stream()))
+        return sel, w
+
+    def pack(self, sel, w, experts):
+        return _pack(sel, w, experts)
+
+    def gather(self, x, tokens):
+        rows = tokens.numel()
+        out = torch.empty((rows, x.shape[1]), dtype=x.dtype, device=x.device)
+        check(lib.pdx_gather_rows(_ptr(x), _ptr(tokens), rows, x.shape[1], _ptr(out), _stream()))
+        return out
+
+    def dispatch(self, x, p, top_k, experts, ranks, capacity):
+        t_count, hidden = x.shape
+        send = torch.zeros((ranks * capacity, hidden), dtype=x.dtype, device=x.device)
+        inv_ep = torch.empty(t_count * top_k, dtype=torch.int32, device=x.device)
+        check(lib.pdx_ep_dispatch(_ptr(x), _ptr(p.tokens), _ptr(p.positions), _ptr(p.offsets), t_count, top_k,
+                                  hidden, experts, ranks, capacity, _ptr(send), _ptr(inv_ep), _stream()))
+        return send, inv_ep
+
+    def layout(self, recv_counts, ranks, local_experts, capacity, rows_cap):
+        dev = recv_counts.device
+        lay = Layout(offsets=torch.empty(local_experts + 1, dtype=torch.int32, device=dev),
+                     active=torch.empty(local_experts + 1, dtype=torch.int32, device=dev),
+                     perm=torch.empty(max(rows_cap, 1), dtype=torch.int32, device=dev), experts=local_experts)
+        check(lib.pdx_ep_layout(_ptr(recv_counts), ranks, local_experts, capacity, rows_cap, _ptr(lay.offsets),
+                                _ptr(lay.active), _ptr(lay.perm), _stream()))
+        return lay
+
+    def regroup(self, recv, lay):
+        out = torch.empty_like(recv)
+        check(lib.pdx_ep_regroup(_ptr(recv), _ptr(lay.perm), _ptr(lay.offsets), lay.experts, recv.shape[0],
+                                 recv.shape[1], _ptr(out), _stream()))
+        return out
+
+    def ungroup(self, grouped, lay):
+        out = torch.empty_like(grouped)
+        check(lib.pdx_ep_ungroup(_ptr(grouped), _ptr(lay.perm), _ptr(lay.offsets), lay.experts, grouped.shape[0],
+                                 grouped.shape[1], _ptr(out), _stream()))
+        return out
+
+    def ffn(self, rows_in, lay, slab, mode=_lib.FFN_AUTO):
+        rows, hidden = rows_in.shape
+        y = torch.empty_like(rows_in)
+        ws = torch.empty(lib.pdx_ffn_workspace_bytes(rows, lay.experts, hidden, slab.inter, mode),
+                         dtype=torch.uint8, device=rows_in.device)
+        check(lib.pdx_moe_ffn_grouped(_ptr(rows_in), rows, None, _ptr(lay.offsets), _ptr(lay.active), lay.experts,
+                                      rows, ctypes.byref(slab.struct), hidden, slab.inter, _ptr(y), mode, _ptr(ws),
+                                      ws.numel(), _stream()))
+        return y
+
+    def combine(self, y, y_rows, weights, inverse, residual):
+        t_count, k = weights.shape
+        out = torch.empty((t_count, y.shape[1]), dtype=torch.bfloat16, device=y.device)
+        check(lib.pdx_ep_combine(_ptr(y), y_rows, _ptr(weights), _ptr(inverse), t_count, k, y.shape[1],
+                                 _ptr(residual), _ptr(out), _stream()))
+        return out
+
+
+class TorchDistExchange:
+    """All-to-all over a torch.distributed process group (NCCL on GPUs).
+
+    BF16 payloads travel as raw bytes (a uint8 view keeps dim 0, so row splits
+    still apply) so every backend can carry them."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self.dist, self.group = dist, group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+
+    def all_to_all(self, inp, out_rows=None, in_splits=None, out_splits=None):
+        shape = (out_rows if out_rows is not None else inp.shape[0],) + tuple(inp.shape[1:])
+        out = torch.empty(shape, dtype=inp.dtype, device=inp.device)
+        a = out.view(torch.uint8) if out.dtype == torch.bfloat16 else out
+        b = inp.view(torch.uint8) if inp.dtype == torch.bfloat16 else inp
+        self.dist.all_to_all_single(a, b, output_split_sizes=out_splits, input_split_sizes=in_splits,
+                                    group=self.group)
+        return out
+
+
+@dataclass
+class Dispatched:
+    """State of one layer between the exchanges on one rank."""
+    t_count: int
+    weights: torch.Tensor
+    packed: Packed
+    mode: str
+    capacity: int
+    send: torch.Tensor
+    inverse: torch.Tensor
+    send_splits: list | None = None
+
+
+class ExpertParallelMoE:
+    """One MoE layer whose experts are sharded over the ranks of a group.
+
+    ``gate`` [E, H] is the full router (replicated); ``local_slab`` holds this
+    rank's EL = E / world experts in slots 0..EL-1 (global expert rank*EL + l
+    in slot l).
+    """
+
+    def __init__(self, gate, local_slab, *, rank, world, exchange=None, top_k=8, normalize=True, ops=None):
+        self.gate, self.slab = gate, local_slab
+        self.experts, self.hidden = gate.shape
+        if self.experts % world:
+            raise ValueError("experts must divide evenly over the ranks")
+        self.local = self.experts // world
+        if local_slab.num_slots < self.local:
+            raise ValueError("local slab holds fewer experts than this rank owns")
+        self.rank, self.world = rank, world
+        self.top_k, self.normalize = top_k, normalize
+        self.exchange = exchange
+        self.ops = ops or DeviceOps()
+
+    def capacity(self, t_count):
+        return t_count * min(self.top_k, self.local)
+
+    # ---- phase 1: route, pack, lay out the send buffer --------------------------
+    def dispatch(self, x, mode=None):
+        t_count = x.shape[0]
+        mode = mode or ("padded" if t_count <= PADDED_MAX_TOKENS else "exact")
+        sel, w = self.ops.route(x, self.gate, self.top_k, self.normalize)
+        p = self.ops.pack(sel, w, self.experts)
+        if mode == "padded":
+            cap = self.capacity(t_count)
+            send, inv = self.ops.dispatch(x, p, self.top_k, self.experts, self.world, cap)
+            return Dispatched(t_count, w, p, mode, cap, send, inv)
+        send = self.ops.gather(x, p.tokens)
+        return Dispatched(t_count, w, p, mode, 0, send, p.inverse)
+
+    # ---- phase 2: experts of this rank on the received rows -----------------------
+    def compute(self, recv, recv_counts, capacity):
+        """Regroup by local expert, one grouped FFN, back to the receive layout."""
+        if recv.shape[0] == 0:
+            return recv
+        lay = self.ops.layout(recv_counts, self.world, self.local, capacity, recv.shape[0])
+        grouped = self.ops.regroup(recv, lay)
+        mode = _lib.FFN_GEMV if capacity > 0 else _lib.FFN_AUTO   # decode: weight-streaming path
+        y = self.ops.ffn(grouped, lay, self.slab, mode)
+        return self.ops.ungroup(y, lay)
+
+    # ---- phase 3: weighted combine of the returned rows -----------------------------
+    def finish(self, d, back, residual=None):
+        return self.ops.combine(back, back.shape[0], d.weights, d.inverse, residual)
+
+    # ---- the whole layer over the exchange -------------------------------------------
+    def forward(self, x, residual=None, mode=None):
+        ex = self.exchange
+        d = self.dispatch(x, mode)
+        recv_counts = ex.all_to_all(d.packed.counts)
+        if d.mode == "padded":
+            recv = ex.all_to_all(d.send)
+            y = self.compute(recv, recv_counts, d.capacity)
+            back = ex.all_to_all(y)
+        else:
+            sc = d.packed.counts.view(self.world, self.local).sum(1).tolist()   # host sync (sizes)
+            rc = recv_counts.view(self.world, self.local).sum(1).tolist()
+            recv = ex.all_to_all(d.send, out_rows=sum(rc), in_splits=sc, out_splits=rc)
+            y = self.compute(recv, recv_counts, 0)
+            back = ex.all_to_all(y, out_rows=sum(sc), in_splits=rc, out_splits=sc)
+        return self.finish(d, back, residual)
+
+
+def local_slab_of(full_slab, rank, world):
+    """Slots [rank*EL, (rank+1)*EL) of a full-layer slab as a rank-local slab (a view)."""
+    el = full_slab.num_slots // world
+    per = 3 * full_slab.inter * full_slab.hidden
+    return ExpertSlab(full_slab.storage[rank * el * per:(rank + 1) * el * per], full_slab.hidden, full_slab.inter)
+
+
+class ExpertParallelStack:
+    """``layers`` expert-parallel MoE layers driven as one step on every rank.
+
+    Layer l+1's input is ``x_l + MoE_l(x_l)`` (residual fused into the
+    combine).  ``step`` replays one CUDA graph per batch size holding every
+    layer's kernels and NCCL exchanges (padded exchange only: all ranks must
+    use the same batch size).
+    """
+
+    def __init__(self, gates, local_slabs, *, rank, world, exchange, top_k=8):
+        self.layers = [ExpertParallelMoE(g, s, rank=rank, world=world, exchange=exchange, top_k=top_k)
+                       for g, s in zip(gates, local_slabs)]
+        self.hidden = gates[0].shape[1]
+        self.device = gates[0].device
+        self._graphs, self._io = {}, {}
+
+    def io(self, t_count):
+        if t_count not in self._io:
+            self._io[t_count] = (torch.zeros((t_count, self.hidden), dtype=torch.bfloat16, device=self.device),
+                                 torch.zeros((t_count, self.hidden), dtype=torch.bfloat16, device=self.device))
+        return self._io[t_count]
+
+    def _run(self, t_count, mode):
+        x, out = self.io(t_count)
+        h = x
+        for layer in self.layers:
+            h = layer.forward(h, residual=h, mode=mode)
+        out.copy_(h)
+
+    def step(self, t_count, *, graph=True):
+        mode = "padded" if t_count <= PADDED_MAX_TOKENS else "exact"
+        if not graph or mode == "exact":
+            self._run(t_count, mode)
+            return
+        g = self._graphs.get(t_count)
+        if g is None:
+            self._run(t_count, mode)          # warm: workspaces, device attributes
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._run(t_count, mode)
+            self._graphs[t_count] = g
+        g.replay()
+
+    def release_graphs(self):
+        """Drop the captured graphs (they hold NCCL work; release before
+        destroying the process group)."""
+        self._graphs.clear()

@@ -180,6 +180,39 @@ class ResidentMoEStack:
         """One staged step (fills every layer's packing for ffn_graph)."""
         self._step_staged(t_count, mode)
 
+    def stage_times_us(self, t_count, mode=_lib.FFN_AUTO, layers=8, repeats=3):
+        """Mean device time per layer of each stage of the staged path, from CUDA
+        events on the current stream: route (logits + top-k), pack, FFN, combine."""
+        b = self.buffers(t_count, mode)
+        st_ws, s = b["ws"], _stream()
+        names = ("route", "pack", "ffn", "combine")
+        tot = dict.fromkeys(names, 0.0)
+        n = 0
+        for _ in range(repeats):
+            for l in range(min(layers, self.num_layers)):
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+                st = b["stages"][l]
+                x = self._act_in(b["acts"], l)
+                ev[0].record()
+                check(lib.pdx_route_topk(_ptr(x), _ptr(self.gates[l]), t_count, self.hidden, self.experts,
+                                         self.top_k, int(self.normalize), _ptr(st.logits), _ptr(st.selected),
+                                         _ptr(st.weights), _ptr(st_ws), st_ws.numel(), s))
+                ev[1].record()
+                check(lib.pdx_pack(_ptr(st.selected), _ptr(st.weights), t_count, self.top_k, self.experts,
+                                   _ptr(st.counts), _ptr(st.offsets), _ptr(st.tokens), _ptr(st.positions),
+                                   _ptr(st.packed_w), _ptr(st.inverse), _ptr(st.active), _ptr(st_ws),
+                                   st_ws.numel(), s))
+                ev[2].record()
+                self.ffn(l, t_count, mode)
+                ev[3].record()
+                self.combine(l, t_count, mode)
+                ev[4].record()
+                torch.cuda.synchronize(self.device)
+                for i, name in enumerate(names):
+                    tot[name] += ev[i].elapsed_time(ev[i + 1]) * 1e3
+                n += 1
+        return {name: tot[name] / n for name in names}
+
     def release_graphs(self):
         self._graphs.clear()
 
