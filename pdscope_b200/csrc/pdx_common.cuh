@@ -133,7 +133,7 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 
-// 2-D tiled TMA load (no multicast): box at (x = inner, y = outer) -> smem.
+// 2-D tiled TMA load of one box into this CTA's shared memory: (x = inner, y = outer).
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, uint64_t* bar, int32_t x,
                                             int32_t y) {
     asm volatile(
