@@ -117,6 +117,8 @@ int device_setup(int* sms_out) {
         if (major != 10) return fail(PDX_ERR_UNSUPPORTED, "pdx_moe is built for sm_100a; device %d is sm_%d", dev, major);
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_grouped_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           static_cast<int>(kGemmSmemBytes)));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_router_logits_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(kTileSmemBytes)));
         const int gemv_smem = 128 * 1024;
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_gateup_gemv<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemv_smem));
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_gateup_gemv<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemv_smem));
@@ -251,6 +253,26 @@ size_t route_ticket_bytes(int64_t T) { return static_cast<size_t>(1 + (T + kRout
 // also packs (decode-sized batches).
 int launch_route(const void* x, const void* gate, int64_t T, int64_t H, int64_t E, int32_t k, int32_t normalize,
                  const RouteBufs& b, const PackOut* fused_pack, cudaStream_t stream) {
+    if (T > kTailMaxTokens) {
+        // prefill sizes: tiled FP64 logits, then one warp per token for top-k
+        int sms = 0;
+        int st = device_setup(&sms);
+        if (st) return st;
+        const int n_tt = static_cast<int>((T + kTileT - 1) / kTileT);
+        const int n_et = static_cast<int>((E + kTileE - 1) / kTileE);
+        k_router_logits_tiled<<<n_tt * n_et, kTileThreads, kTileSmemBytes, stream>>>(
+            static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gate), static_cast<int>(T),
+            static_cast<int>(H), static_cast<int>(E), b.logits);
+        PDX_LAUNCHED();
+        const int warps_per_cta = 8;
+        const int grid = static_cast<int>((T + warps_per_cta - 1) / warps_per_cta);
+        k_topk<<<grid, warps_per_cta * 32, 0, stream>>>(b.logits, static_cast<int>(T), static_cast<int>(E), k,
+                                                        normalize, b.selected, b.weights);
+        PDX_LAUNCHED();
+        if (fused_pack) return fail(PDX_ERR_UNSUPPORTED, "fused pack is only available for T <= %lld",
+                                    static_cast<long long>(kTailMaxTokens));
+        return PDX_OK;
+    }
     const int n_tb = static_cast<int>((T + kRouteTB - 1) / kRouteTB);
     const int n_eb = static_cast<int>((E + kRouteEB - 1) / kRouteEB);
     RouteTail tail{};

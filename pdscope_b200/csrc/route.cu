@@ -132,6 +132,117 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_router_logits(const uint16
     block_pack_all(tail.selected, tail.weights, T, tail.k, E, hist, excl, warp_hist, tail.pack);
 }
 
+// Prefill-size logits: a shared-memory-tiled FP64 GEMM.  A CTA of 128 threads
+// owns 64 tokens x 128 experts; K advances in chunks of 32 staged in shared
+// memory as FP64 (each BF16 operand converted once per CTA, transposed so a
+// thread's operands are one LDS.64 each).  Thread (tx, ty) accumulates tokens
+// ty + 8i and experts tx + 16j (i, j < 8): the strided ownership makes the
+// expert reads of a warp 16 consecutive doubles (conflict-free) and the token
+// reads broadcasts.  The next chunk is loaded from global memory into
+// registers while the current one is multiplied.  Same exact-sum contract as
+// k_router_logits (FP64 accumulation of exact BF16 products, one rounding).
+constexpr int kTileT = 64;
+constexpr int kTileE = 128;
+constexpr int kTileK = 32;
+constexpr int kTileThreads = 128;
+constexpr size_t kTileSmemBytes = 2 * (kTileK * kTileT + kTileK * kTileE) * sizeof(double);
+
+__global__ void __launch_bounds__(kTileThreads, 2) k_router_logits_tiled(const uint16_t* __restrict__ x,
+                                                                         const uint16_t* __restrict__ gate, int T,
+                                                                         int H, int E,
+                                                                         uint16_t* __restrict__ logits) {
+    extern __shared__ __align__(16) double smem_route[];
+    double* xs = smem_route;                            // [2][kTileK][kTileT]
+    double* gs = smem_route + 2 * kTileK * kTileT;      // [2][kTileK][kTileE]
+    const int tid = static_cast<int>(threadIdx.x);
+    const int tx = tid % 16, ty = tid / 16;
+    const int n_et = (E + kTileE - 1) / kTileE;
+    const int t0 = (static_cast<int>(blockIdx.x) / n_et) * kTileT;
+    const int e0 = (static_cast<int>(blockIdx.x) % n_et) * kTileE;
+    // global -> register staging: x chunk = 64 rows x 32 bf16 (256 x 16 B, 2 per
+    // thread); gate chunk = 128 rows x 32 bf16 (512 x 16 B, 4 per thread)
+    uint4 xr[2], gr[4];
+    auto load_chunk = [&](int k0) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int idx = tid + r * kTileThreads;       // 0..255
+            const int row = idx / 4, seg = idx % 4;       // 4 x 16 B per 32-wide row
+            const int t = t0 + row, k = k0 + seg * 8;
+            xr[r] = (t < T && k < H) ? __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * H + k))
+                                     : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int idx = tid + r * kTileThreads;       // 0..511
+            const int row = idx / 4, seg = idx % 4;
+            const int e = e0 + row, k = k0 + seg * 8;
+            gr[r] = (e < E && k < H) ? __ldg(reinterpret_cast<const uint4*>(gate + static_cast<size_t>(e) * H + k))
+                                     : make_uint4(0, 0, 0, 0);
+        }
+    };
+    auto store_chunk = [&](int buf) {
+        double* xb = xs + buf * kTileK * kTileT;
+        double* gb = gs + buf * kTileK * kTileE;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int idx = tid + r * kTileThreads;
+            const int row = idx / 4, seg = idx % 4;
+            const uint32_t w[4] = {xr[r].x, xr[r].y, xr[r].z, xr[r].w};
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                xb[(seg * 8 + q) * kTileT + row] = bits_to_f64((q & 1) ? (w[q >> 1] >> 16) : (w[q >> 1] & 0xFFFFu));
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int idx = tid + r * kTileThreads;
+            const int row = idx / 4, seg = idx % 4;
+            const uint32_t w[4] = {gr[r].x, gr[r].y, gr[r].z, gr[r].w};
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                gb[(seg * 8 + q) * kTileE + row] = bits_to_f64((q & 1) ? (w[q >> 1] >> 16) : (w[q >> 1] & 0xFFFFu));
+        }
+    };
+    double acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0;
+    const int n_chunks = (H + kTileK - 1) / kTileK;
+    load_chunk(0);
+    store_chunk(0);
+    __syncthreads();
+    for (int c = 0; c < n_chunks; ++c) {
+        const int buf = c & 1;
+        if (c + 1 < n_chunks) load_chunk((c + 1) * kTileK);
+        const double* xb = xs + buf * kTileK * kTileT;
+        const double* gb = gs + buf * kTileK * kTileE;
+#pragma unroll 4
+        for (int kk = 0; kk < kTileK; ++kk) {
+            double xv[8], gv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xv[i] = xb[kk * kTileT + ty + 8 * i];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) gv[j] = gb[kk * kTileE + tx + 16 * j];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = fma(xv[i], gv[j], acc[i][j]);
+        }
+        if (c + 1 < n_chunks) store_chunk(buf ^ 1);
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int t = t0 + ty + 8 * i;
+        if (t >= T) continue;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = e0 + tx + 16 * j;
+            if (e < E) logits[static_cast<size_t>(t) * E + e] = f64_to_bf16_bits(acc[i][j]);
+        }
+    }
+}
+
 // Softmax + top-k + renormalisation, one warp per token.
 __global__ void __launch_bounds__(256) k_topk(const uint16_t* __restrict__ logits, int T, int E, int k,
                                               int normalize, int64_t* __restrict__ selected,

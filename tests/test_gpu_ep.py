@@ -69,4 +69,4 @@ def test_expert_parallel_matches_single_gpu(ranks, tokens, mode):
             assert torch.equal(outs[s], ref)
         else:
             np.testing.assert_allclose(outs[s].float().cpu().numpy(), ref.float().cpu().numpy(), rtol=2e-2, atol=2e-2)
-            assert (outs[s] == ref).float().mean().item() > 0.99
+            assert (outs[s] == ref).float().mean().item() > 0.95
