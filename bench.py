@@ -61,6 +61,14 @@ def parse():
     ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU baseline sample")
     ap.add_argument("--cpu-threads", type=int, default=0, help="0 = all usable cores")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--ep-shape", choices=("30b", "235b"), default="30b",
+                    help="N>1 expert-parallel workload: 30b (config 2 per GPU) or 235b (config 5)")
+    ap.add_argument("--offload", action="store_true",
+                    help="config 4 instead: experts in pinned host memory, 24 GiB HBM cap, hot 16/layer")
+    ap.add_argument("--offload-prefills", default="512,1024,2048,4096")
+    ap.add_argument("--offload-decode-steps", type=int, default=64)
+    ap.add_argument("--offload-cap-gib", type=float, default=24.0)
+    ap.add_argument("--offload-hot", type=int, default=16)
     return ap.parse_args()
 
 
@@ -245,6 +253,8 @@ def main():
     L = args.layers
     if world > 1:
         return run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L)
+    if args.offload:
+        return run_offload(args, dev, W, pk, L)
     stack = build_stack(L, CFG["hidden"], CFG["experts"], CFG["inter"], CFG["top_k"], device=dev, seed=rank)
     torch.cuda.synchronize(dev)
 
@@ -403,23 +413,165 @@ def main():
     return 0
 
 
+def run_offload(args, dev, W, pk, L):
+    """Config 4: the 48-layer stack with the process capped at 24 GiB of HBM,
+    16 hot experts per layer (by Zipf rank, written and read back as a
+    ``layer,expert`` hot file) resident, all other experts in pinned host memory
+    and fetched by the copy engine; the gate-fallback predictor prefetches the
+    next layer.  One request per prefill length (prefill, then single-token
+    decode steps), as the reference's offload runs.  Host-link roofline: pinned
+    H2D GB/s measured in the same process."""
+    import tempfile
+    import torch
+    from pdscope_b200 import _lib
+    from pdscope_b200.offload import (OffloadMoEStack, PinnedHostBuffer, load_hot_file, measure_h2d_gbs,
+                                      write_hot_file, zipf_hot_sets)
+    from pdscope_b200.stack import activations, ZIPF_ALPHA, ZIPF_S
+
+    H, E, I, k = CFG["hidden"], CFG["experts"], CFG["inter"], CFG["top_k"]
+    per = EXPERT_BYTES // 2
+    total = torch.cuda.get_device_properties(dev).total_memory
+    cap = int(args.offload_cap_gib * 2 ** 30)
+    torch.cuda.set_per_process_memory_fraction(min(1.0, cap / total), dev)
+    link_gbs = measure_h2d_gbs(dev)
+    torch.cuda.empty_cache()
+
+    gen = torch.Generator(device=dev).manual_seed(0)
+    host_buf = PinnedHostBuffer(L * E * per * 2)
+    host = host_buf.tensor.view(torch.bfloat16).view(L, E, per)
+    gates = []
+    for l in range(L):
+        gate = torch.randn(E, H, device=dev, generator=gen) * 0.02
+        perm = torch.randperm(E, device=dev, generator=gen)
+        ranks = torch.empty(E, device=dev)
+        ranks[perm] = torch.arange(1, E + 1, device=dev, dtype=torch.float32)
+        gate[:, 0] = -ZIPF_ALPHA * ZIPF_S * torch.log(ranks)
+        gates.append(gate.to(torch.bfloat16))
+        for e0 in range(0, E, 16):
+            chunk = (torch.randn((16, per), device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+            host[l, e0:e0 + 16].copy_(chunk)
+    del chunk
+    torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
+    with tempfile.TemporaryDirectory() as td:
+        hot_path = Path(td) / "hot_offload.txt"
+        write_hot_file(hot_path, zipf_hot_sets(gates, E))          # full Zipf ranking, hottest first
+        hot = load_hot_file(hot_path, args.offload_hot, L)
+    hot_bytes = sum(len(h) for h in hot) * EXPERT_BYTES
+    reserve = int(1.5 * 2 ** 30)   # activations, packing and FFN workspace at the largest prefill
+    free = cap - torch.cuda.memory_allocated(dev) - hot_bytes - reserve
+    slots = max(E, free // EXPERT_BYTES)
+    stack = OffloadMoEStack(gates, host, hot, hidden=H, inter=I, cache_slots=slots, top_k=k)
+
+    prefills = [int(v) for v in args.offload_prefills.split(",") if v.strip()]
+    n_dec = max(1, args.offload_decode_steps)
+    for w in range(W):   # warm: tensor maps, device attributes, allocator
+        stack.forward(activations(16 if w == 0 else 1, H, device=dev, seed=900 + w, zipf=True))
+    torch.cuda.synchronize(dev)
+    s = torch.cuda.current_stream(dev)
+
+    def timed(inputs):
+        before = stack.stats.as_dict()
+        l0 = _lib.lib.pdx_launch_count()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for x in inputs:
+            stack.forward(x)
+        e1.record(s)
+        torch.cuda.synchronize(dev)
+        after = stack.stats.as_dict()
+        d = {key: after[key] - before[key] for key in after}
+        d["launches"] = _lib.lib.pdx_launch_count() - l0
+        return e0.elapsed_time(e1) / 1e3, d
+
+    requests = []
+    with ClockSampler(dev.index or 0) as sampler:
+        for r, P in enumerate(prefills):
+            xp = activations(P, H, device=dev, seed=2000 + r, zipf=True)
+            dec = [activations(1, H, device=dev, seed=3000 + 100 * r + i, zipf=True) for i in range(n_dec)]
+            tp, dp = timed([xp])
+            td_, dd = timed(dec)
+            nonhot_uses = dd["expert_uses"] - dd["hot_hits"]
+            requests.append(dict(
+                prefill_tokens=P, prefill_s=tp, prefill_tok_s=P / tp,
+                prefill_h2d_gb=dp["h2d_bytes"] / 1e9, prefill_h2d_gbs=dp["h2d_bytes"] / 1e9 / tp,
+                prefill_link_frac=dp["h2d_bytes"] / 1e9 / tp / link_gbs,
+                decode_steps=n_dec, decode_s=td_, decode_tok_s=n_dec / td_,
+                decode_h2d_gb=dd["h2d_bytes"] / 1e9, decode_h2d_gbs=dd["h2d_bytes"] / 1e9 / td_,
+                decode_link_frac=dd["h2d_bytes"] / 1e9 / td_ / link_gbs,
+                decode_hot_hit_rate=dd["hot_hits"] / max(1, dd["expert_uses"]),
+                decode_ring_hit_rate=dd["cache_hits"] / max(1, nonhot_uses),
+                decode_prefetch_used=dd["prefetch_used"], decode_prefetch_copies=dd["prefetch_copies"],
+                decode_demand_copies=dd["demand_copies"], launches=dp["launches"] + dd["launches"]))
+    clocks = sampler.summary()
+    dec_vals = [q["decode_tok_s"] for q in requests]
+    line = dict(metric="offload single-request decode tok/s (config 4), Qwen3-30B-A3B-shape MoE, 1 B200, "
+                       "24 GiB HBM cap; host-link roofline",
+                value=statistics.mean(dec_vals), unit="tok/s", n_gpus=1, steps=len(requests), warmup=W,
+                ms_per_step=1e3 / statistics.mean(dec_vals), higher_is_better=True, scaling="weak",
+                vs_baseline=None, dtype="bf16", data="synthetic",
+                config=dict(workload="config4 offload: 48 layers, hot %d/layer by Zipf rank, rest in pinned host "
+                                     "memory, prefills %s then %d decode steps each" % (args.offload_hot,
+                                                                                       prefills, n_dec),
+                            hbm_cap_gib=args.offload_cap_gib, hot_gib=hot_bytes / 2 ** 30,
+                            cache_ring_slots=int(slots), cache_ring_gib=slots * EXPERT_BYTES / 2 ** 30,
+                            host_gib=L * E * EXPERT_BYTES / 2 ** 30, zipf=dict(s=ZIPF_S, alpha=ZIPF_ALPHA),
+                            value="mean decode tok/s over the requests"),
+                roofline=dict(bound="host link", achieved=max(q["prefill_h2d_gbs"] for q in requests),
+                              peak=link_gbs, unit="GB/s",
+                              frac=max(q["prefill_h2d_gbs"] for q in requests) / link_gbs,
+                              peak_source="pinned cudaMemcpyAsync H2D, 1 GiB, measured in this run",
+                              traffic=None),
+                requests=requests, clocks=clocks,
+                gpu_launches=sum(q["launches"] for q in requests),
+                reference_a100_for_context=dict(prefill_tok_s={"512": 343.92, "1024": 597.18, "2048": 1086.83,
+                                                               "4096": 1671.54},
+                                                decode_tok_s={"512": 7.984, "1024": 7.689, "2048": 7.902,
+                                                              "4096": 7.765},
+                                                note="whole model (attention + MoE) on A100 PCIe with kt CPU "
+                                                     "experts; not like for like"))
+    print(json.dumps(line), flush=True)
+    del stack
+    host_buf.close()
+    return 0
+
+
 def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
-    """N > 1: the 48-layer stack with experts sharded 128/N per GPU (expert e on
-    rank e // (128/N)), NCCL all-to-all dispatch/combine, decode batch per rank
-    fixed (weak scaling); one CUDA graph per step on every rank."""
+    """N > 1: experts sharded 128/N per GPU (expert e on rank e // (128/N)),
+    NCCL all-to-all dispatch/combine, one CUDA graph per decode step.
+
+    ``--ep-shape 30b`` (default; the driver's scaling runs): the 48-layer
+    Qwen3-30B-A3B stack, decode batch per rank fixed (weak scaling).
+    ``--ep-shape 235b`` (config 5): Qwen3-235B-A22B shape (H=4096, I=1536,
+    94 layers, as many as fit in HBM at 2 GPUs), decode batch 256 tokens in all
+    (256/N per rank) and a Zipf(1.1) prefill of 16 sequences ~U[512, 4096]
+    split over the ranks."""
     import torch
     from pdscope_b200 import _lib
     from pdscope_b200.expert_parallel import ExpertParallelStack, TorchDistExchange
     from pdscope_b200.runtime import ExpertSlab
-    from pdscope_b200.stack import activations
+    from pdscope_b200.stack import activations, prefill_lengths, ZIPF_ALPHA, ZIPF_S
 
-    E, H, I, k = CFG["experts"], CFG["hidden"], CFG["inter"], CFG["top_k"]
+    big = args.ep_shape == "235b"
+    E, k = CFG["experts"], CFG["top_k"]
+    H, I = (4096, 1536) if big else (CFG["hidden"], CFG["inter"])
+    expert_bytes = 3 * H * I * 2
     if E % world:
         raise SystemExit(f"{E} experts do not divide over {world} GPUs")
     el = E // world
+    if big:
+        fit = int(150e9 // (el * expert_bytes))      # leave ~30 GB of HBM for activations and workspaces
+        L = min(94 if args.layers == CFG["layers"] else args.layers, fit)
     g_gate = torch.Generator(device=dev).manual_seed(0)          # routers replicated on every rank
     g_w = torch.Generator(device=dev).manual_seed(1000 + rank)   # this rank's experts
-    gates = [(torch.randn(E, H, device=dev, generator=g_gate) * 0.02).to(torch.bfloat16) for _ in range(L)]
+    gates = []
+    for _ in range(L):
+        g = torch.randn(E, H, device=dev, generator=g_gate) * 0.02
+        if big:   # Zipf(1.1) skew through hidden column 0 (used by the prefill; decode inputs keep it random)
+            ranks = torch.randperm(E, device=dev, generator=g_gate).float() + 1
+            g[:, 0] = -ZIPF_ALPHA * ZIPF_S * torch.log(ranks)
+        gates.append(g.to(torch.bfloat16))
     slabs = [ExpertSlab.allocate(el, H, I, dev, generator=g_w) for _ in range(L)]
     stack = ExpertParallelStack(gates, slabs, rank=rank, world=world, exchange=TorchDistExchange(), top_k=k)
     torch.cuda.synchronize(dev)
@@ -427,6 +579,11 @@ def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
     def max_over_ranks(v):
         t = torch.tensor([v], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(v):
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return float(t.item())
 
     def timed(fn, steps, warm):
@@ -446,10 +603,14 @@ def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
         return max_over_ranks(e0.elapsed_time(e1))
 
     decode = {}
-    headline_t = args.decode_batch
-    extra = [int(v) for v in args.decode_batches.split(",") if v.strip()]
+    if big:
+        headline_t = max(1, 256 // world)
+        batches = [headline_t]
+    else:
+        headline_t = args.decode_batch
+        batches = sorted(set(int(v) for v in args.decode_batches.split(",") if v.strip()) | {headline_t})
     clocks = None
-    for t_count in sorted(set(extra) | {headline_t}):
+    for t_count in batches:
         x, _ = stack.io(t_count)
         x.copy_(activations(t_count, H, device=dev, seed=10 + t_count + 1000 * rank))
         n0 = _lib.lib.pdx_launch_count()
@@ -463,7 +624,7 @@ def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
             clocks = sampler.summary()
         else:
             ms = timed(lambda: stack.step(t_count), K, W)
-        local_bytes = L * el * EXPERT_BYTES  # every local expert receives rows at these batch sizes x ranks
+        local_bytes = L * el * expert_bytes  # every local expert receives rows at these batch sizes x ranks
         decode[t_count] = dict(ms_per_step=ms / K, tok_s=world * t_count * K / (ms / 1e3),
                                launches_per_step=launches,
                                local_weight_gb_per_step=local_bytes / 1e9,
@@ -480,16 +641,44 @@ def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
 
     e2e_ms = timed(e2e_step, K, W)
     stack.release_graphs()
+
+    prefill = None
+    if big and not args.no_prefill:
+        lengths = prefill_lengths(16, lo=512, hi=4096, seed=0)
+        mine = lengths[rank::world]                    # sequences of this rank
+        tp = sum(mine)
+        xp = activations(tp, H, device=dev, seed=77 + rank, zipf=True)
+        xin, _ = stack.io(tp)
+        xin.copy_(xp)
+        stack.step(tp, graph=False)                    # warm (exact exchange: one host sync per layer)
+        ms = timed(lambda: stack.step(tp, graph=False), max(1, args.prefill_steps), 1)
+        total = sum_over_ranks(tp)
+        flops = total * k * 6 * H * I * L
+        prefill = dict(tokens_total=int(total), lengths=lengths, tokens_this_rank=tp,
+                       ms_per_step=ms / max(1, args.prefill_steps),
+                       tok_s=total * max(1, args.prefill_steps) / (ms / 1e3),
+                       tflops_per_gpu=flops / world / (ms / max(1, args.prefill_steps) / 1e3) / 1e12,
+                       zipf=dict(s=ZIPF_S, alpha=ZIPF_ALPHA))
+        prefill["frac_of_sustained_bf16"] = prefill["tflops_per_gpu"] / pk["bf16_tflops_sustained"]
+
     d = decode[headline_t]
     if rank == 0:
+        if big:
+            workload = (f"config5 decode batch {headline_t * world} in all ({headline_t} per GPU): {L}-layer "
+                        f"Qwen3-235B-A22B-shape MoE stack (H={H}, I={I}), expert parallel {el} experts/GPU, "
+                        f"NCCL all-to-all dispatch/combine, one CUDA graph per step")
+            scaling = "strong"
+        else:
+            workload = (f"config2 decode batch {headline_t} per GPU: 48-layer Qwen3-30B-A3B-shape "
+                        f"MoE stack, expert parallel {el} experts/GPU, NCCL all-to-all "
+                        f"dispatch/combine, one CUDA graph per step")
+            scaling = "weak"
         line = dict(metric=METRIC, value=d["tok_s"], unit="tok/s", n_gpus=world, steps=K, warmup=W,
-                    ms_per_step=d["ms_per_step"], higher_is_better=True, scaling="weak", vs_baseline=None,
+                    ms_per_step=d["ms_per_step"], higher_is_better=True, scaling=scaling, vs_baseline=None,
                     dtype="bf16", data="synthetic",
-                    config=dict(workload=f"config2 decode batch {headline_t} per GPU: 48-layer Qwen3-30B-A3B-shape "
-                                         f"MoE stack, expert parallel {el} experts/GPU, NCCL all-to-all "
-                                         f"dispatch/combine, one CUDA graph per step",
-                                hidden=H, experts=E, inter=I, top_k=k, layers=L, decode_batch=headline_t,
-                                global_batch=headline_t * world, parallelism=f"ep{world}",
+                    config=dict(workload=workload, hidden=H, experts=E, inter=I, top_k=k, layers=L,
+                                decode_batch=headline_t, global_batch=headline_t * world,
+                                parallelism=f"ep{world}",
                                 l2="not flushed: each step streams the rank's %.1f GB of expert weights"
                                    % d["local_weight_gb_per_step"]),
                     roofline=dict(bound="hbm", kernel="whole expert-parallel decode step (local expert weights "
@@ -502,7 +691,7 @@ def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
                              h2d_bytes_per_step=host_in.numel() * 2, d2h_bytes_per_step=host_out.numel() * 2,
                              ms_per_step=e2e_ms / K),
                     clocks=clocks, gpu_launches=d["launches_per_step"] * K,
-                    decode={str(t): r for t, r in decode.items()}, prefill=None)
+                    decode={str(t): r for t, r in decode.items()}, prefill=prefill)
         print(json.dumps(line), flush=True)
     dist.destroy_process_group()
     return 0

@@ -24,7 +24,7 @@ PDX_DEVERR_WAIT_TIMEOUT = 1
 PDX_DEVERR_BAD_EXPERT = 2
 PDX_DEVERR_BAD_SLOT = 3
 
-FFN_AUTO, FFN_GEMV, FFN_GEMM, FFN_SIMT = 0, 1, 2, 3
+FFN_AUTO, FFN_GEMV, FFN_GEMM, FFN_SIMT, FFN_GEMM_1CTA, FFN_GEMM_PAIR = 0, 1, 2, 3, 4, 5
 
 ABI_VERSION = 1
 

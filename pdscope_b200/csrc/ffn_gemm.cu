@@ -73,6 +73,98 @@ __device__ __forceinline__ TileInfo decode_tile(int tile, const int* prefix, int
     return ti;
 }
 
+// Per-active-expert tables of a grouped GEMM (one warp): exclusive prefix of
+// output tiles (row tiles of ``bm`` x ``n_tiles`` column tiles), segment start,
+// row count and weight slot.  s_misc[0] = total tiles, s_misc[1] = n_active.
+__device__ __forceinline__ void build_tile_tables(const GemmArgs& args, int n_active, int n_tiles, int bm,
+                                                  int* prefix, int* t_seg0, int* t_rows, int* t_slot, int* s_misc) {
+    const uint32_t lane = lane_id();
+    const int per = (n_active + 31) / 32;
+    const int b = static_cast<int>(lane) * per;
+    int local = 0;
+    for (int i = 0; i < per; ++i)
+        if (b + i < n_active) {
+            const int e = args.active[1 + b + i];
+            const int seg0 = args.offsets[e];
+            const int rows = args.offsets[e + 1] - seg0;
+            int64_t slot = args.slot_of_expert ? args.slot_of_expert[e] : e;
+            if (slot < 0 || slot >= args.num_slots) {
+                raise_error(PDX_DEVERR_BAD_SLOT);
+                slot = 0;  // keeps the pipeline consistent; the call is flagged invalid
+            }
+            const int tiles = ((rows + bm - 1) / bm) * n_tiles;
+            prefix[b + i] = tiles;
+            t_seg0[b + i] = seg0;
+            t_rows[b + i] = rows;
+            t_slot[b + i] = static_cast<int>(slot);
+            local += tiles;
+        }
+    int inc = local;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, inc, off);
+        if (static_cast<int>(lane) >= off) inc += y;
+    }
+    int run = inc - local;
+    for (int i = 0; i < per; ++i)
+        if (b + i < n_active) {
+            const int t = prefix[b + i];
+            prefix[b + i] = run;
+            run += t;
+        }
+    if (lane == 31) { s_misc[0] = inc; s_misc[1] = n_active; }
+}
+
+// One accumulator row (this thread's TMEM lane) -> BF16 output row.
+// swiglu: columns [0,128) hold gate, [128,256) up; h = bf16(bf16(silu(bf16(g))) * bf16(u)).
+// otherwise: y = bf16(acc) over 256 columns.
+__device__ __forceinline__ void epilogue_row(int swiglu, uint32_t taddr, uint16_t* orow, bool valid) {
+    if (swiglu) {
+#pragma unroll 1
+        for (int c = 0; c < kGemmBN / 2; c += 16) {
+            uint32_t g[16], u[16];
+            tmem_ld16(taddr + c, g);
+            tmem_ld16(taddr + kGemmBN / 2 + c, u);
+            tmem_wait_ld();
+            uint32_t packed[8];
+#pragma unroll
+            for (int i = 0; i < 16; i += 2) {
+                float hv[2];
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const float gb = round_bf16(__uint_as_float(g[i + j]));
+                    const float ub = round_bf16(__uint_as_float(u[i + j]));
+                    const float s = round_bf16(__fdiv_rn(gb, 1.0f + expf(-gb)));
+                    hv[j] = s * ub;
+                }
+                packed[i / 2] = static_cast<uint32_t>(f2bits(hv[0])) | (static_cast<uint32_t>(f2bits(hv[1])) << 16);
+            }
+            if (valid) {
+                uint4* dst = reinterpret_cast<uint4*>(orow + c);
+                dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+            }
+        }
+    } else {
+#pragma unroll 1
+        for (int c = 0; c < kGemmBN; c += 16) {
+            uint32_t v[16];
+            tmem_ld16(taddr + c, v);
+            tmem_wait_ld();
+            uint32_t packed[8];
+#pragma unroll
+            for (int i = 0; i < 16; i += 2)
+                packed[i / 2] = static_cast<uint32_t>(f2bits(__uint_as_float(v[i]))) |
+                                (static_cast<uint32_t>(f2bits(__uint_as_float(v[i + 1]))) << 16);
+            if (valid) {
+                uint4* dst = reinterpret_cast<uint4*>(orow + c);
+                dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+            }
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_grouped_gemm(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b0,
                    const __grid_constant__ CUtensorMap tm_b1, GemmArgs args) {
@@ -130,43 +222,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     griddep_wait();
     griddep_launch();
     const int n_active = min(args.active[0], kMaxActive);
-    // per-expert m-tile counts -> exclusive prefix (warp 2)
-    if (warp == 2) {
-        const int per = (n_active + 31) / 32;
-        const int b = static_cast<int>(lane) * per;
-        int local = 0;
-        for (int i = 0; i < per; ++i)
-            if (b + i < n_active) {
-                const int e = args.active[1 + b + i];
-                const int seg0 = args.offsets[e];
-                const int rows = args.offsets[e + 1] - seg0;
-                int64_t slot = args.slot_of_expert ? args.slot_of_expert[e] : e;
-                if (slot < 0 || slot >= args.num_slots) {
-                    raise_error(PDX_DEVERR_BAD_SLOT);
-                    slot = 0;  // keeps the pipeline consistent; the call is flagged invalid
-                }
-                const int tiles = ((rows + kGemmBM - 1) / kGemmBM) * n_tiles;
-                prefix[b + i] = tiles;
-                t_seg0[b + i] = seg0;
-                t_rows[b + i] = rows;
-                t_slot[b + i] = static_cast<int>(slot);
-                local += tiles;
-            }
-        int inc = local;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, inc, off);
-            if (static_cast<int>(lane) >= off) inc += y;
-        }
-        int run = inc - local;
-        for (int i = 0; i < per; ++i)
-            if (b + i < n_active) {
-                const int t = prefix[b + i];
-                prefix[b + i] = run;
-                run += t;
-            }
-        if (lane == 31) { s_misc[0] = inc; s_misc[1] = n_active; }
-    }
+    if (warp == 2) build_tile_tables(args, n_active, n_tiles, kGemmBM, prefix, t_seg0, t_rows, t_slot, s_misc);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -251,50 +307,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const bool valid = r < n_e;
             uint16_t* orow = args.out + static_cast<int64_t>(seg0 + r) * args.out_ld + ti.n * out_cols_per_tile;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * kGemmBN);
-            if (args.swiglu) {
-#pragma unroll 1
-                for (int c = 0; c < kGemmBN / 2; c += 16) {
-                    uint32_t g[16], u[16];
-                    tmem_ld16(taddr + c, g);
-                    tmem_ld16(taddr + kGemmBN / 2 + c, u);
-                    tmem_wait_ld();
-                    uint32_t packed[8];
-#pragma unroll
-                    for (int i = 0; i < 16; i += 2) {
-                        float hv[2];
-#pragma unroll
-                        for (int j = 0; j < 2; ++j) {
-                            const float gb = round_bf16(__uint_as_float(g[i + j]));
-                            const float ub = round_bf16(__uint_as_float(u[i + j]));
-                            const float s = round_bf16(__fdiv_rn(gb, 1.0f + expf(-gb)));
-                            hv[j] = s * ub;
-                        }
-                        packed[i / 2] = static_cast<uint32_t>(f2bits(hv[0])) | (static_cast<uint32_t>(f2bits(hv[1])) << 16);
-                    }
-                    if (valid) {
-                        uint4* dst = reinterpret_cast<uint4*>(orow + c);
-                        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-                    }
-                }
-            } else {
-#pragma unroll 1
-                for (int c = 0; c < kGemmBN; c += 16) {
-                    uint32_t v[16];
-                    tmem_ld16(taddr + c, v);
-                    tmem_wait_ld();
-                    uint32_t packed[8];
-#pragma unroll
-                    for (int i = 0; i < 16; i += 2)
-                        packed[i / 2] = static_cast<uint32_t>(f2bits(__uint_as_float(v[i]))) |
-                                        (static_cast<uint32_t>(f2bits(__uint_as_float(v[i + 1]))) << 16);
-                    if (valid) {
-                        uint4* dst = reinterpret_cast<uint4*>(orow + c);
-                        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-                    }
-                }
-            }
+            epilogue_row(args.swiglu, taddr, orow, valid);
             tc_fence_before();
             mbar_arrive(&tmem_empty[b]);
         }
@@ -318,6 +331,251 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
+// ---- CTA-pair variant: 256 x 256 output tiles (tcgen05 cta_group::2) -------------
+//
+// A cluster of two CTAs on two SMs computes one 256-row x 256-column tile per
+// step.  Each CTA stages its own 128 rows of A and half of B's 256 rows (the
+// gate half or the up half in the SwiGLU GEMM, rows n0..n0+127 or
+// n0+128..n0+255 of Wd in the down GEMM), so per MMA K-block a CTA moves
+// 32 KiB instead of the 48 KiB of the single-CTA 128 x 256 tile: a third less
+// L2-to-SM traffic per FLOP.  The even CTA (rank 0) issues the MMAs for both;
+// each CTA's TMEM holds its own 128 rows of the accumulator.
+//   full_bar   rank 0 only; both CTAs' TMA loads count their bytes on it
+//   empty_bar  in each CTA; rank 0's MMA commits to both
+//   tmem_full  in each CTA; rank 0's MMA commits to both
+//   tmem_empty rank 0 only; one arrival per epilogue warp of either CTA (8)
+// Each CTA's TMA loads fill only its own shared memory.  Every wait is
+// bounded; a timeout sets the abort flag of both CTAs.
+constexpr int kPairStages = 6;
+constexpr uint32_t kPairTileA = 128 * kGemmBK * 2;  // 16 KiB: this CTA's 128 rows of A
+constexpr uint32_t kPairTileB = 128 * kGemmBK * 2;  // 16 KiB: this CTA's half of B
+constexpr uint32_t kPairStageBytes = kPairTileA + kPairTileB;
+constexpr int kPairBM = 256;
+constexpr size_t kGemmPairSmemBytes = 1024 + kPairStages * kPairStageBytes + 256 + 4 * (kMaxActive + 1) * 4;
+
+__device__ __forceinline__ void pair_abort(volatile int* abort_flag, uint32_t peer_abort_addr) {
+    *abort_flag = 1;
+    st_shared_remote_u32(peer_abort_addr, 1u);
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    k_grouped_gemm_pair(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b0,
+                        const __grid_constant__ CUtensorMap tm_b1, GemmArgs args) {
+    extern __shared__ __align__(1024) unsigned char smem_pair[];
+    // identical offsets in both CTAs: the MMA reads the peer's stage at the same address
+    const uint32_t raw_addr = smem_u32(smem_pair);
+    unsigned char* smem = smem_pair + ((1024u - (raw_addr & 1023u)) & 1023u);
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + kPairStages * kPairStageBytes);
+    uint64_t* empty_bar = full_bar + kPairStages;
+    uint64_t* tmem_full = empty_bar + kPairStages;
+    uint64_t* tmem_empty = tmem_full + 2;
+    uint64_t* drain_bar = tmem_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int* s_misc = reinterpret_cast<int*>(tmem_slot + 2);
+    int* prefix = reinterpret_cast<int*>(smem + kPairStages * kPairStageBytes + 256);
+    int* t_seg0 = prefix + (kMaxActive + 1);
+    int* t_rows = t_seg0 + (kMaxActive + 1);
+    int* t_slot = t_rows + (kMaxActive + 1);
+
+    const int warp = static_cast<int>(threadIdx.x >> 5);
+    const uint32_t lane = lane_id();
+    const uint32_t crank = cluster_ctarank();
+    const uint32_t peer = crank ^ 1u;
+    const int pair = static_cast<int>(blockIdx.x >> 1);
+    const int n_pairs = static_cast<int>(gridDim.x >> 1);
+    const uint32_t peer_abort = mapa_shared(smem_u32(const_cast<int*>(abort_flag)), peer);
+
+    const int out_cols_per_tile = args.swiglu ? kGemmBN / 2 : kGemmBN;
+    const int n_tiles = args.n_cols / out_cols_per_tile;
+    const int num_kb = args.K / kGemmBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kPairStages; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tmem_full[b], 1);
+            mbar_init(&tmem_empty[b], 8);
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tm_a);
+        tma_prefetch_desc(&tm_b0);
+        if (args.swiglu) tma_prefetch_desc(&tm_b1);
+    }
+    if (warp == 1) {  // same warp in both CTAs allocates the pair's TMEM
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    griddep_wait();
+    griddep_launch();
+    const int n_active = min(args.active[0], kMaxActive);
+    if (warp == 2) build_tile_tables(args, n_active, n_tiles, kPairBM, prefix, t_seg0, t_rows, t_slot, s_misc);
+    tc_fence_before();
+    cluster_sync_all();  // barriers of both CTAs initialised before any remote arrival
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total_tiles = s_misc[0];
+    // rank 0's barriers, addressed from either CTA
+    const uint32_t full0 = mapa_shared(smem_u32(full_bar), 0);
+    const uint32_t tmem_empty0 = mapa_shared(smem_u32(tmem_empty), 0);
+
+    if (warp == 0) {
+        // ---------------- TMA producer (both CTAs) ----------------
+        if (elect_one()) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int tile = pair; tile < total_tiles && ok; tile += n_pairs) {
+                const TileInfo ti = decode_tile(tile, prefix, n_active, n_tiles);
+                const int64_t slot = t_slot[ti.a];
+                const int row_a = t_seg0[ti.a] + ti.m * kPairBM + static_cast<int>(crank) * 128;
+                // SwiGLU: rank 0 stages 128 gate rows (tm_b0), rank 1 the matching 128
+                // up rows (tm_b1).  Down: rows n0..n0+127 / n0+128..n0+255 of Wd (tm_b0).
+                const bool use_b1 = args.swiglu && crank == 1;
+                int row_b;
+                if (args.swiglu)
+                    row_b = static_cast<int>(slot * (crank ? args.b1_rows_per_slot : args.b0_rows_per_slot)) +
+                            ti.n * out_cols_per_tile;
+                else
+                    row_b = static_cast<int>(slot * args.b0_rows_per_slot) + ti.n * kGemmBN +
+                            static_cast<int>(crank) * 128;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
+                        pair_abort(abort_flag, peer_abort);
+                        ok = false;
+                        break;
+                    }
+                    unsigned char* sa = smem + stage * kPairStageBytes;
+                    if (crank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * kPairStageBytes);
+                    const uint32_t fb = full0 + static_cast<uint32_t>(stage) * 8u;
+                    tma_load_2d_pair(sa, &tm_a, fb, kb * kGemmBK, row_a);
+                    if (use_b1)
+                        tma_load_2d_pair(sa + kPairTileA, &tm_b1, fb, kb * kGemmBK, row_b);
+                    else
+                        tma_load_2d_pair(sa + kPairTileA, &tm_b0, fb, kb * kGemmBK, row_b);
+                    if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
+                }
+            }
+            // tail: every stage's last release (a commit from rank 0) has landed
+            // before this CTA's shared memory can go away
+            for (int i = 0; i < kPairStages && ok; ++i) {
+                if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
+                    pair_abort(abort_flag, peer_abort);
+                    break;
+                }
+                if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (rank 0 only) ----------------
+        if (crank == 0) {
+            constexpr uint32_t idesc = bf16_idesc(kPairBM, kGemmBN);
+            const uint32_t empty_local = smem_u32(empty_bar), empty_peer = mapa_shared(empty_local, 1);
+            const uint32_t tfull_local = smem_u32(tmem_full), tfull_peer = mapa_shared(tfull_local, 1);
+            int stage = 0;
+            uint32_t phase = 0;
+            int lt = 0;
+            bool ok = true;
+            for (int tile = pair; tile < total_tiles && ok; tile += n_pairs, ++lt) {
+                const int b = lt & 1;
+                const uint32_t acc_phase = static_cast<uint32_t>(lt >> 1) & 1u;
+                if (!mbar_wait(&tmem_empty[b], acc_phase ^ 1u, abort_flag)) {
+                    pair_abort(abort_flag, peer_abort);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * kGemmBN);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
+                        pair_abort(abort_flag, peer_abort);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (elect_one()) {
+                        const uint32_t sa = smem_u32(smem + stage * kPairStageBytes);
+                        const uint64_t a0 = sw128_desc(sa), b0 = sw128_desc(sa + kPairTileA);
+#pragma unroll
+                        for (int kk = 0; kk < kGemmBK / 16; ++kk)
+                            umma_bf16_pair(d_tmem, a0 + 2u * kk, b0 + 2u * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+                        umma_commit_pair(empty_local + static_cast<uint32_t>(stage) * 8u);
+                        umma_commit_pair(empty_peer + static_cast<uint32_t>(stage) * 8u);
+                    }
+                    __syncwarp();
+                    if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                if (elect_one()) {
+                    umma_commit_pair(tfull_local + static_cast<uint32_t>(b) * 8u);
+                    umma_commit_pair(tfull_peer + static_cast<uint32_t>(b) * 8u);
+                }
+                __syncwarp();
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+        const int q = warp & 3;
+        const int row_in_tile = static_cast<int>(crank) * 128 + q * 32 + static_cast<int>(lane);
+        int lt = 0;
+        for (int tile = pair; tile < total_tiles; tile += n_pairs, ++lt) {
+            const int b = lt & 1;
+            const uint32_t acc_phase = static_cast<uint32_t>(lt >> 1) & 1u;
+            if (!mbar_wait(&tmem_full[b], acc_phase, abort_flag)) {
+                pair_abort(abort_flag, peer_abort);
+                break;
+            }
+            tc_fence_after();
+            const TileInfo ti = decode_tile(tile, prefix, n_active, n_tiles);
+            const int seg0 = t_seg0[ti.a];
+            const int n_e = t_rows[ti.a];
+            const int r = ti.m * kPairBM + row_in_tile;
+            const bool valid = r < n_e;
+            uint16_t* orow = args.out + static_cast<int64_t>(seg0 + r) * args.out_ld + ti.n * out_cols_per_tile;
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * kGemmBN);
+            epilogue_row(args.swiglu, taddr, orow, valid);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(tmem_empty0 + static_cast<uint32_t>(b) * 8u);
+        }
+    }
+
+    // -- teardown -------------------------------------------------------------------
+    // The peer may raise this CTA's abort flag at any time, so every thread acts
+    // on one snapshot taken after the roles have finished.
+    __syncthreads();
+    if (threadIdx.x == 0) s_misc[2] = *abort_flag;
+    if (warp == 1 && crank == 0) {
+        // rank 0: every MMA it issued has completed (a no-op wait on the normal path)
+        if (elect_one()) umma_commit_pair(smem_u32(drain_bar));
+        __syncwarp();
+        volatile int never = 0;
+        mbar_wait(drain_bar, 0, &never);
+    }
+    __syncthreads();
+    if (s_misc[2]) {
+        // let this CTA's in-flight TMA copies land before its shared memory is released
+        const unsigned long long t0 = global_timer_ns();
+        while (global_timer_ns() - t0 < 2000000ull) __nanosleep(1000);
+    }
+    tc_fence_before();
+    cluster_sync_all();  // no remote arrival or MMA read of this CTA's memory is still pending
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
                      : "memory");
     }
 }

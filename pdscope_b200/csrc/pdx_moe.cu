@@ -58,7 +58,19 @@ int ok() {
 
 // Launch with programmatic stream serialisation (PDL): the kernel may begin
 // while its predecessor in the stream is still running; it synchronises with
-// griddep_wait() before touching the predecessor's results.
+// griddep_wait() before touching the predecessor's results.  The overlap pays
+// for the short decode kernels; prefill-size launches (hundreds of µs each)
+// clear g_pdl_enabled so an early-launched dependent (e.g. a 10^5-CTA row
+// gather) never holds SM resources the next GEMM's CTA pairs are waiting for.
+#ifndef PDX_PREFILL_PDL
+#define PDX_PREFILL_PDL 0
+#endif
+thread_local bool g_pdl_enabled = true;
+struct PdlScope {
+    bool saved;
+    explicit PdlScope(bool on) : saved(g_pdl_enabled) { g_pdl_enabled = on; }
+    ~PdlScope() { g_pdl_enabled = saved; }
+};
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                        Args&&... args) {
@@ -71,7 +83,7 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = g_pdl_enabled ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
@@ -101,6 +113,14 @@ struct Carver {
 
 constexpr int kMaxDevices = 64;
 int g_num_sms[kMaxDevices] = {0};
+int g_pair_clusters[kMaxDevices] = {0};
+constexpr int64_t kPairMinRowsPerExpert = 192;  // auto: CTA-pair tiles when rows >= this x E
+
+int cur_device() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    return (dev >= 0 && dev < kMaxDevices) ? dev : 0;
+}
 bool g_attrs_set[kMaxDevices] = {false};
 std::mutex g_dev_mutex;
 
@@ -119,6 +139,20 @@ int device_setup(int* sms_out) {
                                           static_cast<int>(kGemmSmemBytes)));
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_router_logits_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           static_cast<int>(kTileSmemBytes)));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_grouped_gemm_pair, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(kGemmPairSmemBytes)));
+        {   // CTA pairs that can be resident at once (one CTA per SM)
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(2 * (sms / 2));
+            cfg.blockDim = dim3(kGemmThreads);
+            cfg.dynamicSmemBytes = kGemmPairSmemBytes;
+            int clusters = 0;
+            if (cudaOccupancyMaxActiveClusters(&clusters, k_grouped_gemm_pair, &cfg) != cudaSuccess || clusters < 1) {
+                cudaGetLastError();
+                clusters = sms / 2;
+            }
+            g_pair_clusters[dev] = std::min(clusters, sms / 2);
+        }
         const int gemv_smem = 128 * 1024;
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_gateup_gemv<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemv_smem));
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_gateup_gemv<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemv_smem));
@@ -183,6 +217,7 @@ int check_route_shape(int64_t T, int64_t H, int64_t E, int32_t k) {
 }
 
 bool gemm_shape_ok(int64_t H, int64_t I) { return H % 256 == 0 && I % 128 == 0 && H >= 256 && I >= 128; }
+bool is_gemm_mode(int mode) { return mode == PDX_FFN_GEMM || mode == PDX_FFN_GEMM_1CTA || mode == PDX_FFN_GEMM_PAIR; }
 bool stream_shape_ok(int64_t H, int64_t I) { return H % 128 == 0 && I % 128 == 0 && H >= 128 && I >= 128; }
 
 int resolve_mode(int32_t mode, int64_t T, int64_t H, int64_t I) {
@@ -204,7 +239,7 @@ int check_ffn_shape(int64_t H, int64_t I, int32_t mode) {
     } else if (mode == PDX_FFN_GEMV) {
         if (!stream_shape_ok(H, I))
             return fail(PDX_ERR_UNSUPPORTED, "weight-streaming path needs H %% 128 == 0 and I %% 128 == 0");
-    } else if (mode == PDX_FFN_GEMM) {
+    } else if (is_gemm_mode(mode)) {
         if (!gemm_shape_ok(H, I))
             return fail(PDX_ERR_UNSUPPORTED, "tcgen05 path needs H %% 256 == 0 and I %% 128 == 0");
     } else {
@@ -244,9 +279,31 @@ struct RouteBufs {
     int64_t* selected;
     uint16_t* weights;
     unsigned int* tickets;  // 1 + token blocks
+    double* partials;       // split-K router partials (T > kTailMaxTokens)
 };
 
 size_t route_ticket_bytes(int64_t T) { return static_cast<size_t>(1 + (T + kRouteTB - 1) / kRouteTB) * 4; }
+
+// Split-K partials of the tiled router (T > kTailMaxTokens only).
+constexpr int kMaxRouterSplits = 4;
+size_t route_partial_bytes(int64_t T, int64_t E) {
+    return T > kTailMaxTokens ? static_cast<size_t>(kMaxRouterSplits) * T * E * sizeof(double) : 0;
+}
+
+// K splits per router tile: the count minimising waves/splits (time in units of
+// one whole-K tile) over `slots` resident CTAs; ties keep fewer splits (less
+// partial traffic).  Each split keeps >= 8 K chunks.
+int router_splits(int64_t tiles, int64_t H, int slots) {
+    int best = 1;
+    double best_t = 1e30;
+    for (int s = 1; s <= kMaxRouterSplits; ++s) {
+        if (s > 1 && H / s < 8 * kTileK) break;
+        const int64_t units = tiles * s;
+        const double t = static_cast<double>((units + slots - 1) / slots) / s;
+        if (t < best_t - 1e-9) { best_t = t; best = s; }
+    }
+    return best;
+}
 
 // Routing: exact logits with top-k fused per token block (the k_topk launch is
 // only kept for pdx_topk_from_logits); with fused_pack the last token block
@@ -258,16 +315,22 @@ int launch_route(const void* x, const void* gate, int64_t T, int64_t H, int64_t 
         int sms = 0;
         int st = device_setup(&sms);
         if (st) return st;
-        const int n_tt = static_cast<int>((T + kTileT - 1) / kTileT);
-        const int n_et = static_cast<int>((E + kTileE - 1) / kTileE);
-        k_router_logits_tiled<<<n_tt * n_et, kTileThreads, kTileSmemBytes, stream>>>(
+        const int64_t tiles = ((T + kTileT - 1) / kTileT) * ((E + kTileE - 1) / kTileE);
+        const int splits = router_splits(tiles, H, 2 * sms);
+        const int k_per_split = static_cast<int>(((H + splits - 1) / splits + kTileK - 1) / kTileK * kTileK);
+        k_router_logits_tiled<<<static_cast<unsigned>(tiles * splits), kTileThreads, kTileSmemBytes, stream>>>(
             static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gate), static_cast<int>(T),
-            static_cast<int>(H), static_cast<int>(E), b.logits);
+            static_cast<int>(H), static_cast<int>(E), splits, k_per_split, b.logits, b.partials);
         PDX_LAUNCHED();
         const int warps_per_cta = 8;
         const int grid = static_cast<int>((T + warps_per_cta - 1) / warps_per_cta);
-        k_topk<<<grid, warps_per_cta * 32, 0, stream>>>(b.logits, static_cast<int>(T), static_cast<int>(E), k,
-                                                        normalize, b.selected, b.weights);
+        if (splits > 1)
+            k_topk_partials<<<grid, warps_per_cta * 32, 0, stream>>>(b.partials, splits, static_cast<int>(T),
+                                                                     static_cast<int>(E), k, normalize, b.logits,
+                                                                     b.selected, b.weights);
+        else
+            k_topk<<<grid, warps_per_cta * 32, 0, stream>>>(b.logits, static_cast<int>(T), static_cast<int>(E), k,
+                                                            normalize, b.selected, b.weights);
         PDX_LAUNCHED();
         if (fused_pack) return fail(PDX_ERR_UNSUPPORTED, "fused pack is only available for T <= %lld",
                                     static_cast<long long>(kTailMaxTokens));
@@ -355,7 +418,7 @@ StreamPlan plan_stream(int64_t rows, int64_t E, int64_t H, int64_t I) {
 
 size_t ffn_ws_bytes(int64_t rows, int64_t E, int64_t H, int64_t I, int mode) {
     size_t b = align_up(static_cast<size_t>(rows) * I * 2);                        // h
-    if (mode == PDX_FFN_GEMM || mode == PDX_FFN_GEMV) b += align_up(static_cast<size_t>(rows) * H * 2);  // x rows
+    if (is_gemm_mode(mode) || mode == PDX_FFN_GEMV) b += align_up(static_cast<size_t>(rows) * H * 2);  // x rows
     if (mode == PDX_FFN_GEMV) {
         const StreamPlan p = plan_stream(rows, E, H, I);
         b += align_up(p.partial_bytes) + align_up(2 * p.ticket_bytes);
@@ -383,7 +446,7 @@ int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* o
     int st = device_setup(&sms);
     if (st) return st;
     uint16_t* h = static_cast<uint16_t*>(ws.take(static_cast<size_t>(rows) * I * 2));
-    uint16_t* xp = (mode == PDX_FFN_GEMM || mode == PDX_FFN_GEMV)
+    uint16_t* xp = (is_gemm_mode(mode) || mode == PDX_FFN_GEMV)
                        ? static_cast<uint16_t*>(ws.take(static_cast<size_t>(rows) * H * 2))
                        : nullptr;
     StreamPlan plan{};
@@ -426,6 +489,8 @@ int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* o
         PDX_LAUNCHED();
         return PDX_OK;
     }
+    // prefill sizes launch without programmatic overlap (see launch_pdl)
+    PdlScope pdl_scope(!is_gemm_mode(mode) || PDX_PREFILL_PDL);
     // tcgen05 paths: gather the packed x rows once (and clear the split-K tickets);
     // with tokens == NULL the rows of x are already in packed order.
     const int zero_words = mode == PDX_FFN_GEMV ? static_cast<int>(2 * plan.ticket_bytes / 4) : 0;
@@ -459,7 +524,27 @@ int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* o
         if (plan.nt == 16) return launch_stream_pair<16>(tm_g, tm_u, tm_x, tm_d, tm_h, plan, a1, a2, sms, stream);
         return launch_stream_pair<32>(tm_g, tm_u, tm_x, tm_d, tm_h, plan, a1, a2, sms, stream);
     }
-    // prefill: token-tiled grouped GEMM
+    // prefill: token-tiled grouped GEMM; CTA pairs (256 x 256 tiles) when experts
+    // average enough rows to fill them, single CTAs (128 x 256) otherwise
+    const bool pair = mode == PDX_FFN_GEMM_PAIR || (mode == PDX_FFN_GEMM && rows >= kPairMinRowsPerExpert * E);
+    if (pair) {
+        if ((st = encode_2d(&tm_x, xp, rows, H, 128))) return st;
+        if ((st = encode_2d(&tm_h, h, rows, I, 128))) return st;
+        if ((st = encode_2d(&tm_d, w->down, (w->num_slots - 1) * ds + H, I, 128))) return st;
+        const int64_t pair_tiles_bound = rows / kPairBM + max_active;
+        const int max_pairs = g_pair_clusters[cur_device()];
+        GemmArgs a1{offsets, active, w->slot_of_expert, w->num_slots, gs, us, static_cast<int>(H),
+                    static_cast<int>(I), 1, h, I};
+        const int pairs1 = static_cast<int>(std::min<int64_t>(max_pairs, pair_tiles_bound * (I / (kGemmBN / 2))));
+        PDX_PDL_TRY(launch_pdl(k_grouped_gemm_pair, dim3(2 * pairs1), dim3(kGemmThreads), kGemmPairSmemBytes,
+                               stream, tm_x, tm_g, tm_u, a1));
+        GemmArgs a2{offsets, active, w->slot_of_expert, w->num_slots, ds, ds, static_cast<int>(I),
+                    static_cast<int>(H), 0, static_cast<uint16_t*>(y), H};
+        const int pairs2 = static_cast<int>(std::min<int64_t>(max_pairs, pair_tiles_bound * (H / kGemmBN)));
+        PDX_PDL_TRY(launch_pdl(k_grouped_gemm_pair, dim3(2 * pairs2), dim3(kGemmThreads), kGemmPairSmemBytes,
+                               stream, tm_h, tm_d, tm_d, a2));
+        return PDX_OK;
+    }
     if ((st = encode_2d(&tm_x, xp, rows, H, kGemmBM))) return st;
     if ((st = encode_2d(&tm_h, h, rows, I, kGemmBM))) return st;
     if ((st = encode_2d(&tm_d, w->down, (w->num_slots - 1) * ds + H, I, kGemmBN))) return st;
@@ -523,7 +608,8 @@ uint64_t pdx_launch_count(void) { return g_launches.load(); }
 
 size_t pdx_route_workspace_bytes(int64_t T, int64_t E) {
     T = std::max<int64_t>(T, 1);
-    return align_up(route_ticket_bytes(T)) + align_up(static_cast<size_t>(T) * std::max<int64_t>(E, 0) * 2);
+    return align_up(route_ticket_bytes(T)) + align_up(static_cast<size_t>(T) * std::max<int64_t>(E, 0) * 2) +
+           align_up(route_partial_bytes(T, std::max<int64_t>(E, 0)));
 }
 
 int pdx_route_topk(const void* x, const void* gate, int64_t T, int64_t H, int64_t E, int32_t top_k, int32_t normalize,
@@ -538,6 +624,7 @@ int pdx_route_topk(const void* x, const void* gate, int64_t T, int64_t H, int64_
     RouteBufs b;
     b.tickets = static_cast<unsigned int*>(c.take(route_ticket_bytes(T)));
     b.logits = logits_out ? static_cast<uint16_t*>(logits_out) : static_cast<uint16_t*>(c.take(T * E * 2));
+    b.partials = static_cast<double*>(c.take(route_partial_bytes(T, E)));
     b.selected = selected_out;
     b.weights = static_cast<uint16_t*>(weights_out);
     if (c.overflow) return fail(PDX_ERR_WORKSPACE, "route workspace too small");
@@ -594,7 +681,12 @@ size_t pdx_ffn_workspace_bytes(int64_t rows, int64_t E, int64_t H, int64_t I, in
     rows = std::max<int64_t>(rows, 1);
     E = std::max<int64_t>(E, 1);
     const int m = resolve_mode(mode, rows, H, I);
-    return ffn_ws_bytes(rows, E, H, I, m) + kAlign;
+    size_t b = ffn_ws_bytes(rows, E, H, I, m);
+    // auto mode resolves on the token count T, which may be <= 64 (decode path)
+    // while rows = T*k exceeds 64: cover that path too (T*k <= 64*kMaxTopK)
+    if (mode == PDX_FFN_AUTO && m != PDX_FFN_GEMV && rows <= kGemvMaxTokens * kMaxTopK && stream_shape_ok(H, I))
+        b = std::max(b, ffn_ws_bytes(rows, E, H, I, PDX_FFN_GEMV));
+    return b + kAlign;
 }
 
 int pdx_moe_ffn_grouped(const void* x, int64_t T, const int32_t* tokens, const int32_t* offsets,
@@ -665,6 +757,7 @@ size_t pdx_layer_workspace_bytes(int64_t T, int64_t H, int64_t E, int32_t top_k,
     Carver c{nullptr, SIZE_MAX};
     c.take(route_ticket_bytes(T));  // route tickets
     c.take(T * E * 2);           // logits
+    c.take(route_partial_bytes(T, E));
     c.take(N * 8);               // selected
     c.take(N * 2);               // weights
     carve_pack(c, T, top_k, E, nullptr);
@@ -690,6 +783,7 @@ int pdx_moe_layer(const void* x, const void* gate, int64_t T, int64_t H, int64_t
     RouteBufs rb;
     rb.tickets = static_cast<unsigned int*>(c.take(route_ticket_bytes(T)));
     rb.logits = logits_out ? static_cast<uint16_t*>(logits_out) : static_cast<uint16_t*>(c.take(T * E * 2));
+    rb.partials = static_cast<double*>(c.take(route_partial_bytes(T, E)));
     rb.selected = selected_out ? selected_out : static_cast<int64_t*>(c.take(N * 8));
     rb.weights = weights_out ? static_cast<uint16_t*>(weights_out) : static_cast<uint16_t*>(c.take(N * 2));
     PackBufs pb = carve_pack(c, T, top_k, E, counts_out);

@@ -147,34 +147,48 @@ constexpr int kTileK = 32;
 constexpr int kTileThreads = 128;
 constexpr size_t kTileSmemBytes = 2 * (kTileK * kTileT + kTileK * kTileE) * sizeof(double);
 
+// Work unit = (64-token x 128-expert tile, K range).  With splits == 1 the unit
+// covers all of K and writes the rounded BF16 logits; with splits > 1 it
+// writes its FP64 partial dot products to partials[split][T][E] and
+// k_topk_partials adds the splits in split order before the single rounding.
+// The split count balances the units over the SMs (a 64-token tile is ~1/148
+// of the work at 9.5k tokens, so whole tiles alone leave SMs idle).
 __global__ void __launch_bounds__(kTileThreads, 2) k_router_logits_tiled(const uint16_t* __restrict__ x,
                                                                          const uint16_t* __restrict__ gate, int T,
-                                                                         int H, int E,
-                                                                         uint16_t* __restrict__ logits) {
+                                                                         int H, int E, int splits, int k_per_split,
+                                                                         uint16_t* __restrict__ logits,
+                                                                         double* __restrict__ partials) {
     extern __shared__ __align__(16) double smem_route[];
     double* xs = smem_route;                            // [2][kTileK][kTileT]
     double* gs = smem_route + 2 * kTileK * kTileT;      // [2][kTileK][kTileE]
     const int tid = static_cast<int>(threadIdx.x);
     const int tx = tid % 16, ty = tid / 16;
     const int n_et = (E + kTileE - 1) / kTileE;
-    const int t0 = (static_cast<int>(blockIdx.x) / n_et) * kTileT;
-    const int e0 = (static_cast<int>(blockIdx.x) % n_et) * kTileE;
+    const int split = static_cast<int>(blockIdx.x) % splits;
+    const int tile = static_cast<int>(blockIdx.x) / splits;
+    const int t0 = (tile / n_et) * kTileT;
+    const int e0 = (tile % n_et) * kTileE;
+    const int k_begin = split * k_per_split;
+    const int k_end = min(H, k_begin + k_per_split);
     // global -> register staging: x chunk = 64 rows x 32 bf16 (256 x 16 B, 2 per
-    // thread); gate chunk = 128 rows x 32 bf16 (512 x 16 B, 4 per thread)
+    // thread); gate chunk = 128 rows x 32 bf16 (512 x 16 B, 4 per thread).  A
+    // warp's 32 lanes take 32 consecutive rows of one 8-wide K segment, so the
+    // transposed FP64 stores below fill 32 consecutive doubles per k (no bank
+    // conflicts).
     uint4 xr[2], gr[4];
     auto load_chunk = [&](int k0) {
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-            const int idx = tid + r * kTileThreads;       // 0..255
-            const int row = idx / 4, seg = idx % 4;       // 4 x 16 B per 32-wide row
+            const int idx = tid + r * kTileThreads;           // 0..255
+            const int row = idx % kTileT, seg = idx / kTileT;  // seg 0..3: 8 bf16 (16 B) each
             const int t = t0 + row, k = k0 + seg * 8;
             xr[r] = (t < T && k < H) ? __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * H + k))
                                      : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-            const int idx = tid + r * kTileThreads;       // 0..511
-            const int row = idx / 4, seg = idx % 4;
+            const int idx = tid + r * kTileThreads;           // 0..511
+            const int row = idx % kTileE, seg = idx / kTileE;
             const int e = e0 + row, k = k0 + seg * 8;
             gr[r] = (e < E && k < H) ? __ldg(reinterpret_cast<const uint4*>(gate + static_cast<size_t>(e) * H + k))
                                      : make_uint4(0, 0, 0, 0);
@@ -186,7 +200,7 @@ __global__ void __launch_bounds__(kTileThreads, 2) k_router_logits_tiled(const u
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             const int idx = tid + r * kTileThreads;
-            const int row = idx / 4, seg = idx % 4;
+            const int row = idx % kTileT, seg = idx / kTileT;
             const uint32_t w[4] = {xr[r].x, xr[r].y, xr[r].z, xr[r].w};
 #pragma unroll
             for (int q = 0; q < 8; ++q)
@@ -195,7 +209,7 @@ __global__ void __launch_bounds__(kTileThreads, 2) k_router_logits_tiled(const u
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             const int idx = tid + r * kTileThreads;
-            const int row = idx / 4, seg = idx % 4;
+            const int row = idx % kTileE, seg = idx / kTileE;
             const uint32_t w[4] = {gr[r].x, gr[r].y, gr[r].z, gr[r].w};
 #pragma unroll
             for (int q = 0; q < 8; ++q)
@@ -207,13 +221,15 @@ __global__ void __launch_bounds__(kTileThreads, 2) k_router_logits_tiled(const u
     for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[i][j] = 0.0;
-    const int n_chunks = (H + kTileK - 1) / kTileK;
-    load_chunk(0);
-    store_chunk(0);
+    const int n_chunks = k_end > k_begin ? (k_end - k_begin + kTileK - 1) / kTileK : 0;
+    if (n_chunks > 0) {
+        load_chunk(k_begin);
+        store_chunk(0);
+    }
     __syncthreads();
     for (int c = 0; c < n_chunks; ++c) {
         const int buf = c & 1;
-        if (c + 1 < n_chunks) load_chunk((c + 1) * kTileK);
+        if (c + 1 < n_chunks) load_chunk(k_begin + (c + 1) * kTileK);
         const double* xb = xs + buf * kTileK * kTileT;
         const double* gb = gs + buf * kTileK * kTileE;
 #pragma unroll 4
@@ -238,8 +254,33 @@ __global__ void __launch_bounds__(kTileThreads, 2) k_router_logits_tiled(const u
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int e = e0 + tx + 16 * j;
-            if (e < E) logits[static_cast<size_t>(t) * E + e] = f64_to_bf16_bits(acc[i][j]);
+            if (e >= E) continue;
+            if (splits == 1)
+                logits[static_cast<size_t>(t) * E + e] = f64_to_bf16_bits(acc[i][j]);
+            else
+                partials[(static_cast<size_t>(split) * T + t) * E + e] = acc[i][j];
         }
+    }
+}
+
+// Split-K router tail, one warp per token: logits = RNE_bf16(sum of the FP64
+// partials in split order), written out, then softmax + top-k + renormalise
+// on the row just written.
+__global__ void __launch_bounds__(256) k_topk_partials(const double* __restrict__ partials, int splits, int T, int E,
+                                                       int k, int normalize, uint16_t* __restrict__ logits,
+                                                       int64_t* __restrict__ selected,
+                                                       uint16_t* __restrict__ weights) {
+    const int warps = static_cast<int>(blockDim.x >> 5);
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    for (int t = static_cast<int>(blockIdx.x) * warps + static_cast<int>(threadIdx.x >> 5); t < T;
+         t += static_cast<int>(gridDim.x) * warps) {
+        for (int e = lane; e < E; e += 32) {
+            double sum = 0.0;
+            for (int sp = 0; sp < splits; ++sp) sum += partials[(static_cast<size_t>(sp) * T + t) * E + e];
+            logits[static_cast<size_t>(t) * E + e] = f64_to_bf16_bits(sum);
+        }
+        __syncwarp();  // the row is re-read by every lane of this warp
+        topk_row(logits, t, E, k, normalize != 0, selected, weights);
     }
 }
 

@@ -10,13 +10,15 @@ Per layer on every rank:
   1. route + pack locally (all E experts)                     pdx_route_topk, pdx_pack
   2. dispatch: packed rows for rank d are the contiguous range of experts
      [d*EL, (d+1)*EL); all-to-all of the per-expert counts, then of the rows
-  3. the received rows are laid out as "virtual experts" (source rank, local
-     expert) that reuse the local weight slots; one grouped FFN   pdx_ep_layout,
-                                                                 pdx_moe_ffn_grouped
+  3. the received rows are regrouped by local expert (every source's rows of
+     expert l made contiguous), so each local expert's weights are streamed
+     once per layer however many ranks sent it rows; one grouped FFN; the
+     results are put back in the receive layout      pdx_ep_layout, pdx_ep_regroup,
+                                                      pdx_moe_ffn_grouped, pdx_ep_ungroup
   4. all-to-all of the unweighted rows back, weighted combine in slot order
-                                                                 pdx_ep_combine / pdx_combine
+                                                      pdx_ep_combine
 Two exchange forms:
-  * padded (decode, T <= 64): every (source, destination) block has the fixed
+  * padded (decode, T <= 256 per rank): every (source, destination) block has the fixed
     capacity T*min(k, EL) rows, so sizes never leave the device (no host sync;
     the whole step can be captured in a CUDA graph);
   * exact (prefill): the counts are read back to size an exact all-to-all
@@ -35,7 +37,7 @@ from . import _lib
 from ._lib import check, lib
 from .runtime import ExpertSlab, Packed, _ptr, _stream, pack as _pack
 
-PADDED_MAX_TOKENS = 64
+PADDED_MAX_TOKENS = 256
 
 
 @dataclass

@@ -41,6 +41,12 @@ def test_workspace_queries_are_monotone():
     assert 0 < a < b <= c
     assert lib.pdx_pack_workspace_bytes(4096, 8, 128) >= 8 * 128 * 4
     assert lib.pdx_route_workspace_bytes(64, 128) >= 64 * 128 * 2
+    # prefill sizes also hold the split-K router partials (up to 4 x T x E FP64)
+    assert lib.pdx_route_workspace_bytes(4096, 128) >= 4 * 4096 * 128 * 8
+    # auto FFN workspace for rows = T*k also covers T <= 64 (decode path), e.g. 16 tokens x 8
+    for rows in (128, 512):
+        assert lib.pdx_ffn_workspace_bytes(rows, 128, 2048, 768, 0) >= lib.pdx_ffn_workspace_bytes(rows, 128, 2048,
+                                                                                                      768, 1)
 
 
 def test_validation_errors_without_device():

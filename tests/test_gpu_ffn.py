@@ -65,11 +65,17 @@ def test_expert_forward_vs_torch_on_device(pdx):
         np.testing.assert_allclose(f32(ours), f32(ref), rtol=RTOL, atol=ATOL)
 
 
-def _grouped_case(pdx, tokens, experts, k, hidden, inter, mode, seed, slot_perm=False):
+def _grouped_case(pdx, tokens, experts, k, hidden, inter, mode, seed, slot_perm=False, zipf=False, check=True):
     from tests.gpu_util import to_bits, to_dev
     from pdscope_b200 import _lib
     from pdscope_b200.runtime import ExpertSlab
     x, gate, wg, wu, wd = mo.synthetic_layer(seed, tokens, hidden, experts, inter)
+    if zipf:  # Zipf(1.1) router skew through hidden column 0: a few experts take most rows
+        ranks = np.random.default_rng(seed).permutation(experts) + 1
+        gate = gate.copy()
+        x = x.copy()
+        gate[:, 0] = mo.f32_to_bf16((-0.75 * 1.1 * np.log(ranks)).astype(np.float32))
+        x[:, 0] = mo.f32_to_bf16(np.ones(tokens, np.float32))
     _, sel, w = mo.route(x, gate, k, True)
     packed = mo.compact_expert_groups(sel, w, experts)
     slab = ExpertSlab.from_tensors([dict(gate_proj=to_dev(wg[e]), up_proj=to_dev(wu[e]), down_proj=to_dev(wd[e]))
@@ -97,6 +103,8 @@ def _grouped_case(pdx, tokens, experts, k, hidden, inter, mode, seed, slot_perm=
     torch.cuda.synchronize()
     assert _lib.device_error(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
     got = to_bits(y)
+    if not check:
+        return got
     exp = np.zeros_like(got)
     off = packed["offsets"]
     for e in nz:
@@ -107,13 +115,13 @@ def _grouped_case(pdx, tokens, experts, k, hidden, inter, mode, seed, slot_perm=
     return got
 
 
-@pytest.mark.parametrize("mode", (1, 2, 3))
+@pytest.mark.parametrize("mode", (1, 2, 3, 4, 5))
 @pytest.mark.parametrize("tokens", (1, 5, 64, 300))
 def test_grouped_ffn_small_shape(pdx, mode, tokens):
     _grouped_case(pdx, tokens, 16, 4, 256, 128, mode, 100 + tokens)
 
 
-@pytest.mark.parametrize("mode", (1, 2, 3))
+@pytest.mark.parametrize("mode", (1, 2, 3, 5))
 def test_grouped_ffn_slot_mapping(pdx, mode):
     """Experts located through slot_of_expert (the executor's cache-slot ledger)."""
     a = _grouped_case(pdx, 40, 16, 4, 256, 128, mode, 7, slot_perm=False)
@@ -121,7 +129,8 @@ def test_grouped_ffn_slot_mapping(pdx, mode):
     assert np.array_equal(a, b)
 
 
-@pytest.mark.parametrize("mode,tokens", ((1, 1), (1, 8), (1, 64), (1, 130), (3, 64), (2, 130), (2, 512)))
+@pytest.mark.parametrize("mode,tokens", ((1, 1), (1, 8), (1, 64), (1, 130), (3, 64), (2, 130), (2, 512), (5, 130),
+                                         (5, 512)))
 def test_grouped_ffn_qwen3_shape(pdx, mode, tokens):
     _grouped_case(pdx, tokens, 128, 8, 2048, 768, mode, 200 + tokens)
 
@@ -141,3 +150,20 @@ def test_stream_split_k_deterministic(pdx, tokens):
     a = _grouped_case(pdx, tokens, 64, 8, 1024, 512, 1, 900 + tokens)
     b = _grouped_case(pdx, tokens, 64, 8, 1024, 512, 1, 900 + tokens)
     assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("tokens", (700, 3000))
+def test_pair_tiles_match_single(pdx, tokens):
+    """CTA-pair 256 x 256 tiles (mode 5) against single-CTA 128 x 256 tiles
+    (mode 4) on a Zipf-skewed prefill at the Qwen3-30B-A3B shape: segments of
+    thousands of rows, ragged tails and one-row experts.  Each output element
+    takes the same K-ordered sequence of MMAs on both paths."""
+    a = _grouped_case(pdx, tokens, 128, 8, 2048, 768, 4, 55 + tokens, zipf=True, check=False)
+    b = _grouped_case(pdx, tokens, 128, 8, 2048, 768, 5, 55 + tokens, zipf=True, check=False)
+    np.testing.assert_allclose(mo.bf16_to_f32(a), mo.bf16_to_f32(b), rtol=RTOL, atol=ATOL)
+    assert (a == b).mean() > 0.999
+
+
+def test_pair_tiles_zipf_oracle(pdx):
+    """CTA-pair path against the oracle on a skewed batch (auto mode picks it)."""
+    _grouped_case(pdx, 400, 16, 8, 512, 256, 0, 77, zipf=True)

@@ -1,0 +1,67 @@
+"""Offload mode on the device: experts in pinned host memory, a hot set and a
+small cache ring in HBM.  The output of every step must equal the all-resident
+stack's output bit for bit (same kernels, same split-K plan; only the expert
+slot table differs), through prefill and decode steps that force demand
+chunks, prefetch hits and evictions."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+L, E, H, I, K = 4, 16, 256, 128, 4
+
+
+@pytest.fixture(scope="module")
+def stacks():
+    from pdscope_b200.offload import OffloadMoEStack, zipf_hot_sets
+    from pdscope_b200.stack import build_stack
+    res = build_stack(L, H, E, I, top_k=K, seed=5, zipf=True)
+    host = torch.stack([s.storage.view(E, -1).cpu() for s in res.slabs]).pin_memory()
+    hot = zipf_hot_sets(res.gates, 4)
+    off = OffloadMoEStack(res.gates, host, hot, hidden=H, inter=I, cache_slots=14, top_k=K, chunk=3)
+    return res, off
+
+
+def _resident(res, x):
+    t = x.shape[0]
+    res.input(t).copy_(x)
+    res.step(t, graph=False)
+    return res.output(t).clone()
+
+
+@pytest.mark.parametrize("t_count", [1, 7, 96])
+def test_offload_matches_resident(stacks, t_count):
+    from pdscope_b200.stack import activations
+    res, off = stacks
+    for step in range(3):
+        x = activations(t_count, H, seed=300 + 10 * t_count + step, zipf=True)
+        want = _resident(res, x)
+        got = off.forward(x).clone()
+        torch.cuda.synchronize()
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16)), (t_count, step)
+    from pdscope_b200.runtime import raise_device_error
+    raise_device_error()
+
+
+def test_offload_ledger(stacks):
+    from pdscope_b200.stack import activations
+    _, off = stacks
+    before = off.stats.as_dict()
+    for step in range(6):
+        off.forward(activations(1, H, seed=900 + step, zipf=True))
+    torch.cuda.synchronize()
+    s = off.stats.as_dict()
+    d = {k: s[k] - before[k] for k in s}
+    assert d["layers"] == 6 * L
+    # every non-hot expert use is either a ring hit or a demand copy
+    assert d["expert_uses"] == d["hot_hits"] + d["cache_hits"] + d["demand_copies"]
+    assert d["h2d_bytes"] == (d["demand_copies"] + d["prefetch_copies"]) * 3 * H * I * 2
+    assert d["prefetch_copies"] > 0
+
+
+def test_offload_rejects_pageable_host():
+    from pdscope_b200.offload import OffloadMoEStack
+    g = [torch.zeros(E, H, dtype=torch.bfloat16, device="cuda")]
+    with pytest.raises(ValueError, match="pinned"):
+        OffloadMoEStack(g, torch.zeros(1, E, 3 * H * I, dtype=torch.bfloat16), [[0]], hidden=H, inter=I,
+                        cache_slots=4, top_k=K)

@@ -7,7 +7,8 @@ from oracle import moe_oracle as mo
 
 pytestmark = pytest.mark.gpu
 
-ROUTE_T = (1, 3, 16, 17, 64, 65, 256, 1000, 1024, 4096)
+# 65..4096 and 12450: split-K tiled router (2-4 K splits); 18944 = 296 whole tiles: one split
+ROUTE_T = (1, 3, 16, 17, 64, 65, 256, 1000, 1024, 4096, 12450, 18944)
 
 
 @pytest.fixture(scope="module")
@@ -105,7 +106,8 @@ def test_route_golden_reference_rows(pdx, golden):
 def test_route_other_shapes(pdx):
     """E, k, H away from the Qwen3 defaults (E not a multiple of 8, k=1, odd T)."""
     from tests.gpu_util import to_bits, to_dev
-    for (tokens, hidden, experts, k) in ((5, 64, 20, 3), (33, 256, 16, 4), (9, 512, 200, 1), (7, 2048, 64, 8)):
+    for (tokens, hidden, experts, k) in ((5, 64, 20, 3), (33, 256, 16, 4), (9, 512, 200, 1), (7, 2048, 64, 8),
+                                         (300, 512, 200, 4), (130, 256, 16, 4), (97, 1024, 130, 8)):
         x, gate = mo.synthetic_router(5000 + tokens, tokens, hidden, experts)
         for normalize in (True, False):
             r = pdx.route(to_dev(x), to_dev(gate), k, normalize)
