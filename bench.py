@@ -316,11 +316,12 @@ def main():
     per_launch_s = ffn_ms / 1e3 / (K * L)
     achieved = bytes_per_launch / per_launch_s / 1e9
     traffic = None
-    tj = ROOT / "profiles" / "traffic.json"
-    if tj.exists():
-        d = json.loads(tj.read_text()).get("decode_ffn")
-        if d:
-            traffic = d["dram_bytes_per_active_expert"] * statistics.mean(act)
+    tt = ROOT / "profiles" / "traffic.txt"   # figure from an ncu capture (see the file's header)
+    if tt.exists():
+        for line in tt.read_text().splitlines():
+            f = line.split()
+            if len(f) == 2 and f[0] == "decode_ffn_dram_bytes_per_active_expert":
+                traffic = float(f[1]) * statistics.mean(act)
     roofline = dict(bound="hbm", kernel="pdx_moe_ffn_grouped decode path (k_gather_rows + 2x k_stream_gemm: TMA weight stream, tcgen05 swap-AB)",
                     achieved=achieved, peak=pk["hbm_gbs"], unit="GB/s", frac=achieved / pk["hbm_gbs"],
                     peak_source=pk["source"], frac_of_8000_nominal=achieved / 8000.0, traffic=traffic,
@@ -345,7 +346,9 @@ def main():
         stack.release_graphs()
         pstack.step(tp)
         pk_steps = max(1, args.prefill_steps)
-        ms = timed(lambda: pstack.step(tp), pk_steps, 1)
+        with ClockSampler(local_rank) as psampler:
+            ms = timed(lambda: pstack.step(tp), pk_steps, 1)
+        prefill_clocks = psampler.summary()
         b = pstack.buffers(tp)
         c0 = b["stages"][0].counts.float()
         top16 = float(torch.topk(c0, 16).values.sum() / c0.sum())
@@ -358,7 +361,7 @@ def main():
         tflops = flops_launch / per_launch_p / 1e12
         prefill = dict(tokens=tp, lengths=lengths, ms_per_step=ms / pk_steps,
                        tok_s=sum_over_ranks(tp) * pk_steps / (ms / 1e3), top16_share_layer0=top16,
-                       stage_us_per_layer=stages_p,
+                       stage_us_per_layer=stages_p, clocks=prefill_clocks,
                        zipf=dict(s=ZIPF_S, alpha=ZIPF_ALPHA),
                        roofline=dict(bound="tensor", kernel="pdx_moe_ffn_grouped tcgen05 (gather + 2x k_grouped_gemm)",
                                      achieved=tflops, unit="TFLOP/s", peak=pk["bf16_tflops_sustained"],
@@ -367,6 +370,30 @@ def main():
                                      flops_per_launch=flops_launch, us_per_launch=per_launch_p * 1e6))
         pstack.release_graphs()
         del pstack
+
+    # ---- config 1: one layer (pdx_moe_layer, one C-ABI call) at T = 1 and 512 ----------
+    from pdscope_b200.runtime import LayerOutputs, ResidentMoELayer
+    layer0 = ResidentMoELayer(stack.gates[0], stack.slabs[0])
+    config1 = {}
+    for t_count, reps in ((1, 200), (512, 50)):
+        x1 = activations(t_count, CFG["hidden"], device=dev, seed=300 + t_count)
+        outs = layer0.forward(x1)
+        ms1 = timed(lambda: layer0.forward(x1, outputs=outs), reps, W) / reps
+        u = int((outs.counts > 0).sum().item())
+        layer_bytes = u * EXPERT_BYTES + CFG["experts"] * CFG["hidden"] * 2 + 2 * t_count * CFG["hidden"] * 2
+        config1[str(t_count)] = dict(us_per_layer=ms1 * 1e3, active_experts=u,
+                                     hbm_gbs=layer_bytes / (ms1 / 1e3) / 1e9,
+                                     hbm_frac=layer_bytes / (ms1 / 1e3) / 1e9 / pk["hbm_gbs"],
+                                     tflops=t_count * CFG["top_k"] * FLOPS_PER_ROW / (ms1 / 1e3) / 1e12)
+    if world == 1 and not args.no_cpu:
+        from oracle import cpu_path
+        cores = args.cpu_threads or usable_cores()
+        sample = [cpu_path.make_layer(CFG["hidden"], CFG["experts"], CFG["inter"], seed=100)]
+        for t_count in (1, 512):
+            per_layer, _ = cpu_path.time_layers(sample, t_count, CFG["hidden"], cores, repeats=1)
+            config1[str(t_count)]["cpu_reference_us_per_layer"] = per_layer * 1e6
+            config1[str(t_count)]["cpu_cores"] = cores
+    del layer0
 
     # ---- e2e: public API with host buffers (pinned H2D in, D2H out) --------------------
     t_count = headline_t
@@ -406,7 +433,7 @@ def main():
                     roofline=roofline, cpu_baseline=cpu, e2e=e2e, clocks=d["clocks"],
                     gpu_launches=d["launches_per_step"] * K,
                     decode={str(t): {k: v for k, v in r.items() if k != "clocks"} for t, r in decode.items()},
-                    prefill=prefill)
+                    prefill=prefill, config1_layer=config1)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -150,11 +150,11 @@ int pdx_gather_rows(const void *x, const int32_t *tokens, int64_t rows, int64_t 
  * the product).  `x` is the [T,H] token matrix; rows are gathered through
  * `tokens` (tokens == NULL: x already holds the `rows` rows in packed order).  mode: 0 = auto; 1 = decode path (weights streamed by TMA as the
  * tcgen05 M operand, tokens as N, split-K for few experts); 2 = prefill path
- * (tcgen05 grouped GEMM tiled over tokens; 256-row tiles on CTA pairs when
- * experts average >= 192 rows, else 128-row tiles on single CTAs); 3 = SIMT
- * weight-streaming GEMV (an independent implementation kept for cross-checks
- * and for shapes the tcgen05 paths do not tile); 4 / 5 = the prefill path
- * forced to single-CTA 128 x 256 tiles / CTA-pair 256 x 256 tiles.
+ * (tcgen05 grouped GEMM tiled over tokens, 128 x 256 tiles on single CTAs);
+ * 3 = SIMT weight-streaming GEMV (an independent implementation kept for
+ * cross-checks and for shapes the tcgen05 paths do not tile); 4 = the prefill
+ * path (same as 2); 5 = the prefill path on CTA pairs (tcgen05 cta_group::2,
+ * 256 x 256 tiles).
  */
 #define PDX_FFN_AUTO 0
 #define PDX_FFN_GEMV 1

@@ -114,7 +114,6 @@ struct Carver {
 constexpr int kMaxDevices = 64;
 int g_num_sms[kMaxDevices] = {0};
 int g_pair_clusters[kMaxDevices] = {0};
-constexpr int64_t kPairMinRowsPerExpert = 192;  // auto: CTA-pair tiles when rows >= this x E
 
 int cur_device() {
     int dev = 0;
@@ -137,8 +136,8 @@ int device_setup(int* sms_out) {
         if (major != 10) return fail(PDX_ERR_UNSUPPORTED, "pdx_moe is built for sm_100a; device %d is sm_%d", dev, major);
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_grouped_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           static_cast<int>(kGemmSmemBytes)));
-        PDX_CUDA_TRY(cudaFuncSetAttribute(k_router_logits_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          static_cast<int>(kTileSmemBytes)));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_router_logits_dmma, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(kDmmaSmemBytes)));
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_grouped_gemm_pair, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           static_cast<int>(kGemmPairSmemBytes)));
         {   // CTA pairs that can be resident at once (one CTA per SM)
@@ -297,7 +296,7 @@ int router_splits(int64_t tiles, int64_t H, int slots) {
     int best = 1;
     double best_t = 1e30;
     for (int s = 1; s <= kMaxRouterSplits; ++s) {
-        if (s > 1 && H / s < 8 * kTileK) break;
+        if (s > 1 && H / s < 8 * kDmK) break;
         const int64_t units = tiles * s;
         const double t = static_cast<double>((units + slots - 1) / slots) / s;
         if (t < best_t - 1e-9) { best_t = t; best = s; }
@@ -315,10 +314,10 @@ int launch_route(const void* x, const void* gate, int64_t T, int64_t H, int64_t 
         int sms = 0;
         int st = device_setup(&sms);
         if (st) return st;
-        const int64_t tiles = ((T + kTileT - 1) / kTileT) * ((E + kTileE - 1) / kTileE);
+        const int64_t tiles = ((T + kDmT - 1) / kDmT) * ((E + kDmE - 1) / kDmE);
         const int splits = router_splits(tiles, H, 2 * sms);
-        const int k_per_split = static_cast<int>(((H + splits - 1) / splits + kTileK - 1) / kTileK * kTileK);
-        k_router_logits_tiled<<<static_cast<unsigned>(tiles * splits), kTileThreads, kTileSmemBytes, stream>>>(
+        const int k_per_split = static_cast<int>(((H + splits - 1) / splits + kDmK - 1) / kDmK * kDmK);
+        k_router_logits_dmma<<<static_cast<unsigned>(tiles * splits), kDmThreads, kDmmaSmemBytes, stream>>>(
             static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gate), static_cast<int>(T),
             static_cast<int>(H), static_cast<int>(E), splits, k_per_split, b.logits, b.partials);
         PDX_LAUNCHED();
@@ -524,9 +523,12 @@ int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* o
         if (plan.nt == 16) return launch_stream_pair<16>(tm_g, tm_u, tm_x, tm_d, tm_h, plan, a1, a2, sms, stream);
         return launch_stream_pair<32>(tm_g, tm_u, tm_x, tm_d, tm_h, plan, a1, a2, sms, stream);
     }
-    // prefill: token-tiled grouped GEMM; CTA pairs (256 x 256 tiles) when experts
-    // average enough rows to fill them, single CTAs (128 x 256) otherwise
-    const bool pair = mode == PDX_FFN_GEMM_PAIR || (mode == PDX_FFN_GEMM && rows >= kPairMinRowsPerExpert * E);
+    // prefill: token-tiled grouped GEMM on single CTAs (128 x 256 tiles); CTA-pair
+    // 256 x 256 tiles on request (mode PDX_FFN_GEMM_PAIR).  The pair form moves a
+    // third less L2->SM data per FLOP but measured slower on a 12,450-token Zipf
+    // prefill (1172 vs 1031 us per layer): the GEMM is bound by the power-capped
+    // tensor clock, not by L2 bandwidth.
+    const bool pair = mode == PDX_FFN_GEMM_PAIR;
     if (pair) {
         if ((st = encode_2d(&tm_x, xp, rows, H, 128))) return st;
         if ((st = encode_2d(&tm_h, h, rows, I, 128))) return st;

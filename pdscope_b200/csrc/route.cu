@@ -132,96 +132,102 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_router_logits(const uint16
     block_pack_all(tail.selected, tail.weights, T, tail.k, E, hist, excl, warp_hist, tail.pack);
 }
 
-// Prefill-size logits: a shared-memory-tiled FP64 GEMM.  A CTA of 128 threads
-// owns 64 tokens x 128 experts; K advances in chunks of 32 staged in shared
-// memory as FP64 (each BF16 operand converted once per CTA, transposed so a
-// thread's operands are one LDS.64 each).  Thread (tx, ty) accumulates tokens
-// ty + 8i and experts tx + 16j (i, j < 8): the strided ownership makes the
-// expert reads of a warp 16 consecutive doubles (conflict-free) and the token
-// reads broadcasts.  The next chunk is loaded from global memory into
-// registers while the current one is multiplied.  Same exact-sum contract as
-// k_router_logits (FP64 accumulation of exact BF16 products, one rounding).
-constexpr int kTileT = 64;
-constexpr int kTileE = 128;
-constexpr int kTileK = 32;
-constexpr int kTileThreads = 128;
-constexpr size_t kTileSmemBytes = 2 * (kTileK * kTileT + kTileK * kTileE) * sizeof(double);
+// Prefill-size router on the FP64 tensor path (mma.sync m8n8k4 .f64; tcgen05
+// has no FP64 kind): exact BF16 products summed in FP64, as k_router_logits,
+// with each warp instruction doing 256 FMAs (8x8x4) from register fragments.  The FP64
+// tensor path has the FP64 pipe's peak (64 FMA/clk/SM) but needs an eighth of
+// the issue slots and, with a 32x64 warp tile, 1/4 of the shared-memory loads
+// per FMA.  Tile: 64 tokens x 128 experts per 128-thread CTA, K chunks of 32
+// in double-buffered FP64 shared memory, row stride 36 doubles so the
+// fragment loads (8 rows x 4 k per warp) touch every 8-byte bank twice.
+// Work unit = (tile, K range).  With splits == 1 the unit covers all of K and
+// writes the rounded BF16 logits; with splits > 1 it writes its FP64 partial
+// dot products to partials[split][T][E] and k_topk_partials adds the splits in
+// split order before the single rounding.  The split count balances the units
+// over the SMs (a 64-token tile is ~1/148 of the work at 9.5k tokens, so whole
+// tiles alone leave SMs idle).
+constexpr int kDmT = 64;
+constexpr int kDmE = 128;
+constexpr int kDmK = 32;
+constexpr int kDmS = 36;  // shared-memory row stride (doubles)
+constexpr int kDmThreads = 128;
+constexpr size_t kDmmaSmemBytes = 2 * (kDmT + kDmE) * kDmS * sizeof(double);
 
-// Work unit = (64-token x 128-expert tile, K range).  With splits == 1 the unit
-// covers all of K and writes the rounded BF16 logits; with splits > 1 it
-// writes its FP64 partial dot products to partials[split][T][E] and
-// k_topk_partials adds the splits in split order before the single rounding.
-// The split count balances the units over the SMs (a 64-token tile is ~1/148
-// of the work at 9.5k tokens, so whole tiles alone leave SMs idle).
-__global__ void __launch_bounds__(kTileThreads, 2) k_router_logits_tiled(const uint16_t* __restrict__ x,
-                                                                         const uint16_t* __restrict__ gate, int T,
-                                                                         int H, int E, int splits, int k_per_split,
-                                                                         uint16_t* __restrict__ logits,
-                                                                         double* __restrict__ partials) {
-    extern __shared__ __align__(16) double smem_route[];
-    double* xs = smem_route;                            // [2][kTileK][kTileT]
-    double* gs = smem_route + 2 * kTileK * kTileT;      // [2][kTileK][kTileE]
+__device__ __forceinline__ void dmma_884(double (&d)[2], double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
+                 : "+d"(d[0]), "+d"(d[1])
+                 : "d"(a), "d"(b));
+}
+
+__global__ void __launch_bounds__(kDmThreads, 2) k_router_logits_dmma(const uint16_t* __restrict__ x,
+                                                                     const uint16_t* __restrict__ gate, int T, int H,
+                                                                     int E, int splits, int k_per_split,
+                                                                     uint16_t* __restrict__ logits,
+                                                                     double* __restrict__ partials) {
+    extern __shared__ __align__(16) double smem_dmma[];
+    double* xs = smem_dmma;                    // [2][kDmT][kDmS]
+    double* gs = smem_dmma + 2 * kDmT * kDmS;  // [2][kDmE][kDmS]
     const int tid = static_cast<int>(threadIdx.x);
-    const int tx = tid % 16, ty = tid / 16;
-    const int n_et = (E + kTileE - 1) / kTileE;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int n_et = (E + kDmE - 1) / kDmE;
     const int split = static_cast<int>(blockIdx.x) % splits;
     const int tile = static_cast<int>(blockIdx.x) / splits;
-    const int t0 = (tile / n_et) * kTileT;
-    const int e0 = (tile % n_et) * kTileE;
+    const int t0 = (tile / n_et) * kDmT;
+    const int e0 = (tile % n_et) * kDmE;
     const int k_begin = split * k_per_split;
     const int k_end = min(H, k_begin + k_per_split);
-    // global -> register staging: x chunk = 64 rows x 32 bf16 (256 x 16 B, 2 per
-    // thread); gate chunk = 128 rows x 32 bf16 (512 x 16 B, 4 per thread).  A
-    // warp's 32 lanes take 32 consecutive rows of one 8-wide K segment, so the
-    // transposed FP64 stores below fill 32 consecutive doubles per k (no bank
-    // conflicts).
+    const int wm = (warp >> 1) * 32;  // warp tile: 32 tokens x 64 experts
+    const int wn = (warp & 1) * 64;
+    const int fr = lane >> 2, fk = lane & 3;  // fragment row (token / expert) and k of this lane
+
+    // global -> registers: 4 lanes per 64-byte row segment (coalesced)
     uint4 xr[2], gr[4];
     auto load_chunk = [&](int k0) {
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-            const int idx = tid + r * kTileThreads;           // 0..255
-            const int row = idx % kTileT, seg = idx / kTileT;  // seg 0..3: 8 bf16 (16 B) each
+            const int idx = tid + r * kDmThreads;  // 0..255 = 64 rows x 4 segments
+            const int row = idx >> 2, seg = idx & 3;
             const int t = t0 + row, k = k0 + seg * 8;
             xr[r] = (t < T && k < H) ? __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * H + k))
                                      : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-            const int idx = tid + r * kTileThreads;           // 0..511
-            const int row = idx % kTileE, seg = idx / kTileE;
+            const int idx = tid + r * kDmThreads;  // 0..511 = 128 rows x 4 segments
+            const int row = idx >> 2, seg = idx & 3;
             const int e = e0 + row, k = k0 + seg * 8;
             gr[r] = (e < E && k < H) ? __ldg(reinterpret_cast<const uint4*>(gate + static_cast<size_t>(e) * H + k))
                                      : make_uint4(0, 0, 0, 0);
         }
     };
+    auto store8 = [&](double* dst, const uint4& v) {  // 8 BF16 -> 8 doubles, 16-byte stores
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            reinterpret_cast<double2*>(dst)[q] = make_double2(bits_to_f64(w[q] & 0xFFFFu), bits_to_f64(w[q] >> 16));
+    };
     auto store_chunk = [&](int buf) {
-        double* xb = xs + buf * kTileK * kTileT;
-        double* gb = gs + buf * kTileK * kTileE;
+        double* xb = xs + buf * kDmT * kDmS;
+        double* gb = gs + buf * kDmE * kDmS;
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-            const int idx = tid + r * kTileThreads;
-            const int row = idx % kTileT, seg = idx / kTileT;
-            const uint32_t w[4] = {xr[r].x, xr[r].y, xr[r].z, xr[r].w};
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-                xb[(seg * 8 + q) * kTileT + row] = bits_to_f64((q & 1) ? (w[q >> 1] >> 16) : (w[q >> 1] & 0xFFFFu));
+            const int idx = tid + r * kDmThreads;
+            store8(xb + (idx >> 2) * kDmS + (idx & 3) * 8, xr[r]);
         }
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-            const int idx = tid + r * kTileThreads;
-            const int row = idx % kTileE, seg = idx / kTileE;
-            const uint32_t w[4] = {gr[r].x, gr[r].y, gr[r].z, gr[r].w};
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-                gb[(seg * 8 + q) * kTileE + row] = bits_to_f64((q & 1) ? (w[q >> 1] >> 16) : (w[q >> 1] & 0xFFFFu));
+            const int idx = tid + r * kDmThreads;
+            store8(gb + (idx >> 2) * kDmS + (idx & 3) * 8, gr[r]);
         }
     };
-    double acc[8][8];
+
+    double acc[4][8][2];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0;
-    const int n_chunks = k_end > k_begin ? (k_end - k_begin + kTileK - 1) / kTileK : 0;
+        for (int ni = 0; ni < 8; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
+
+    const int n_chunks = k_end > k_begin ? (k_end - k_begin + kDmK - 1) / kDmK : 0;
     if (n_chunks > 0) {
         load_chunk(k_begin);
         store_chunk(0);
@@ -229,58 +235,93 @@ __global__ void __launch_bounds__(kTileThreads, 2) k_router_logits_tiled(const u
     __syncthreads();
     for (int c = 0; c < n_chunks; ++c) {
         const int buf = c & 1;
-        if (c + 1 < n_chunks) load_chunk(k_begin + (c + 1) * kTileK);
-        const double* xb = xs + buf * kTileK * kTileT;
-        const double* gb = gs + buf * kTileK * kTileE;
-#pragma unroll 4
-        for (int kk = 0; kk < kTileK; ++kk) {
-            double xv[8], gv[8];
+        if (c + 1 < n_chunks) load_chunk(k_begin + (c + 1) * kDmK);
+        const double* xb = xs + buf * kDmT * kDmS + (wm + fr) * kDmS + fk;
+        const double* gb = gs + buf * kDmE * kDmS + (wn + fr) * kDmS + fk;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) xv[i] = xb[kk * kTileT + ty + 8 * i];
+        for (int kq = 0; kq < kDmK / 4; ++kq) {
+            double a[4], b[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) gv[j] = gb[kk * kTileE + tx + 16 * j];
+            for (int mi = 0; mi < 4; ++mi) a[mi] = xb[mi * 8 * kDmS + kq * 4];
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
+            for (int ni = 0; ni < 8; ++ni) b[ni] = gb[ni * 8 * kDmS + kq * 4];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) acc[i][j] = fma(xv[i], gv[j], acc[i][j]);
+            for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+                for (int ni = 0; ni < 8; ++ni) dmma_884(acc[mi][ni], a[mi], b[ni]);
         }
         if (c + 1 < n_chunks) store_chunk(buf ^ 1);
         __syncthreads();
     }
+    // accumulator fragment: row fr (token), columns 2*fk + {0, 1} (experts)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int t = t0 + ty + 8 * i;
+    for (int mi = 0; mi < 4; ++mi) {
+        const int t = t0 + wm + mi * 8 + fr;
         if (t >= T) continue;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int e = e0 + tx + 16 * j;
-            if (e >= E) continue;
-            if (splits == 1)
-                logits[static_cast<size_t>(t) * E + e] = f64_to_bf16_bits(acc[i][j]);
-            else
-                partials[(static_cast<size_t>(split) * T + t) * E + e] = acc[i][j];
+        for (int ni = 0; ni < 8; ++ni) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int e = e0 + wn + ni * 8 + 2 * fk + j;
+                if (e >= E) continue;
+                if (splits == 1)
+                    logits[static_cast<size_t>(t) * E + e] = f64_to_bf16_bits(acc[mi][ni][j]);
+                else
+                    partials[(static_cast<size_t>(split) * T + t) * E + e] = acc[mi][ni][j];
+            }
         }
     }
 }
 
 // Split-K router tail, one warp per token: logits = RNE_bf16(sum of the FP64
-// partials in split order), written out, then softmax + top-k + renormalise
-// on the row just written.
+// partials in split order), written out and kept in registers for the
+// softmax + top-k + renormalisation of the row.
+template <int EPL>
+__device__ __forceinline__ void topk_partials_row(const double* __restrict__ partials, int splits, int T, int E,
+                                                  int t, int k, bool normalize, uint16_t* __restrict__ logits,
+                                                  int64_t* __restrict__ selected, uint16_t* __restrict__ weights) {
+    const int lane = static_cast<int>(lane_id());
+    double acc[EPL];
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) acc[i] = 0.0;
+    for (int sp = 0; sp < splits; ++sp) {
+        const double* row = partials + (static_cast<size_t>(sp) * T + t) * E;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+            const int idx = lane + 32 * i;
+            if (idx < E) acc[i] += __ldg(row + idx);
+        }
+    }
+    float v[EPL];
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+        const int idx = lane + 32 * i;
+        if (idx < E) {
+            const uint16_t b = f64_to_bf16_bits(acc[i]);
+            logits[static_cast<size_t>(t) * E + idx] = b;
+            v[i] = bits2f(b);
+        } else {
+            v[i] = -INFINITY;
+        }
+    }
+    warp_softmax_topk_vals<EPL>(v, E, k, normalize, selected + static_cast<size_t>(t) * k,
+                                weights + static_cast<size_t>(t) * k);
+}
+
 __global__ void __launch_bounds__(256) k_topk_partials(const double* __restrict__ partials, int splits, int T, int E,
                                                        int k, int normalize, uint16_t* __restrict__ logits,
                                                        int64_t* __restrict__ selected,
                                                        uint16_t* __restrict__ weights) {
     const int warps = static_cast<int>(blockDim.x >> 5);
-    const int lane = static_cast<int>(threadIdx.x & 31);
+    const bool nrm = normalize != 0;
     for (int t = static_cast<int>(blockIdx.x) * warps + static_cast<int>(threadIdx.x >> 5); t < T;
          t += static_cast<int>(gridDim.x) * warps) {
-        for (int e = lane; e < E; e += 32) {
-            double sum = 0.0;
-            for (int sp = 0; sp < splits; ++sp) sum += partials[(static_cast<size_t>(sp) * T + t) * E + e];
-            logits[static_cast<size_t>(t) * E + e] = f64_to_bf16_bits(sum);
-        }
-        __syncwarp();  // the row is re-read by every lane of this warp
-        topk_row(logits, t, E, k, normalize != 0, selected, weights);
+        if (E <= 32) topk_partials_row<1>(partials, splits, T, E, t, k, nrm, logits, selected, weights);
+        else if (E <= 64) topk_partials_row<2>(partials, splits, T, E, t, k, nrm, logits, selected, weights);
+        else if (E <= 128) topk_partials_row<4>(partials, splits, T, E, t, k, nrm, logits, selected, weights);
+        else if (E <= 256) topk_partials_row<8>(partials, splits, T, E, t, k, nrm, logits, selected, weights);
+        else if (E <= 512) topk_partials_row<16>(partials, splits, T, E, t, k, nrm, logits, selected, weights);
+        else topk_partials_row<32>(partials, splits, T, E, t, k, nrm, logits, selected, weights);
     }
 }
 

@@ -26,17 +26,11 @@ namespace pdx {
 //    1, 2, 4, ...; lane 0's total divides every weight; result RNE to BF16.
 // EPL = elements per lane = max(1, next_pow2(E) / 32).
 // ---------------------------------------------------------------------------
+// Values form: v[i] = logit of expert lane + 32*i (-inf past E), already in registers.
 template <int EPL>
-__device__ __forceinline__ void warp_softmax_topk(const uint16_t* __restrict__ logits_row, int E, int k,
-                                                  bool normalize, int64_t* __restrict__ sel_out,
-                                                  uint16_t* __restrict__ w_out) {
+__device__ __forceinline__ void warp_softmax_topk_vals(float (&v)[EPL], int E, int k, bool normalize,
+                                                       int64_t* __restrict__ sel_out, uint16_t* __restrict__ w_out) {
     const uint32_t lane = lane_id();
-    float v[EPL];
-#pragma unroll
-    for (int i = 0; i < EPL; ++i) {
-        const int idx = static_cast<int>(lane) + 32 * i;
-        v[i] = idx < E ? bits2f(logits_row[idx]) : -INFINITY;
-    }
     float m = v[0];
 #pragma unroll
     for (int i = 1; i < EPL; ++i) m = fmaxf(m, v[i]);
@@ -146,6 +140,21 @@ __device__ __forceinline__ void warp_softmax_topk(const uint16_t* __restrict__ l
         sel_out[lane] = val;
         w_out[lane] = f2bits(normalize ? __fdiv_rn(key, denom) : key);
     }
+}
+
+
+template <int EPL>
+__device__ __forceinline__ void warp_softmax_topk(const uint16_t* __restrict__ logits_row, int E, int k,
+                                                  bool normalize, int64_t* __restrict__ sel_out,
+                                                  uint16_t* __restrict__ w_out) {
+    const uint32_t lane = lane_id();
+    float v[EPL];
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+        const int idx = static_cast<int>(lane) + 32 * i;
+        v[i] = idx < E ? bits2f(logits_row[idx]) : -INFINITY;
+    }
+    warp_softmax_topk_vals<EPL>(v, E, k, normalize, sel_out, w_out);
 }
 
 template <int EPL>

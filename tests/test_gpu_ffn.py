@@ -165,5 +165,5 @@ def test_pair_tiles_match_single(pdx, tokens):
 
 
 def test_pair_tiles_zipf_oracle(pdx):
-    """CTA-pair path against the oracle on a skewed batch (auto mode picks it)."""
-    _grouped_case(pdx, 400, 16, 8, 512, 256, 0, 77, zipf=True)
+    """CTA-pair path against the oracle on a skewed batch."""
+    _grouped_case(pdx, 400, 16, 8, 512, 256, 5, 77, zipf=True)
