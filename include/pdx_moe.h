@@ -190,6 +190,16 @@ int pdx_combine(const void *y, const void *weights, const int32_t *inverse, int6
                 int32_t top_k, int64_t H, const void *residual, void *out,
                 pdx_stream_t stream);
 
+/* Next-layer activation of a multi-layer stack, as the reference's two-layer
+ * protocol forms it (benchmarks/pdscope_compare.py:609-705, `x =
+ * F.layer_norm(out.float() + x.float(), (H,)).to(bf16)`): out[t] =
+ * bf16(layer_norm(float(y[t]) + float(residual[t]))) -- no affine, population
+ * variance, FP32 statistics.  y, residual, out: [T,H] BF16; H a multiple of 8,
+ * <= 8192; out may alias y or residual.  Not part of the reference's MoE path;
+ * it keeps a synthetic stack's activations at unit scale. */
+int pdx_residual_layernorm(const void *y, const void *residual, int64_t T, int64_t H, float eps, void *out,
+                           pdx_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * Whole layer: route -> pack -> grouped FFN -> combine, all on `stream`, no
  * host synchronisation (PDScopeCudaRuntime.forward's GPU work,

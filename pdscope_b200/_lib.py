@@ -63,6 +63,7 @@ SIGNATURES = {
     "pdx_expert_ffn_workspace_bytes": (c_sz, [c_i64, c_i64, c_i64]),
     "pdx_expert_ffn": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_sz, c_vp]),
     "pdx_combine": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, c_i32, c_i64, c_vp, c_vp, c_vp]),
+    "pdx_residual_layernorm": (ctypes.c_int, [c_vp, c_vp, c_i64, c_i64, ctypes.c_float, c_vp, c_vp]),
     "pdx_layer_workspace_bytes": (c_sz, [c_i64, c_i64, c_i64, c_i32, c_i64, c_i32]),
     "pdx_moe_layer": (ctypes.c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_i32,
                                      ctypes.POINTER(ExpertWeights), c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,

@@ -113,4 +113,76 @@ __global__ void k_zero_words(unsigned int* __restrict__ p, int n) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = 0u;
 }
 
+// Next-layer activation of a synthetic multi-layer stack, as the reference's
+// two-layer protocol forms it (benchmarks/pdscope_compare.py:609-705):
+//   out[t] = bf16( layer_norm( float(y[t]) + float(residual[t]) ) )
+// (no affine, population variance, eps; FP32 statistics).  y is the MoE layer
+// output (BF16).  One CTA per token; up to kLnMaxPerThread values per thread
+// stay in registers between the two reductions.
+constexpr int kLnThreads = 256;
+constexpr int kLnMaxPerThread = 32;  // H <= 8192
+
+__device__ __forceinline__ float block_sum_ln(float v, float* red) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
+    __syncthreads();  // red[] free from a previous reduction
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float tot = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) tot += red[w];  // fixed order
+    return tot;
+}
+
+// out may alias y or residual: a CTA reads its whole row before writing it.
+__global__ void __launch_bounds__(kLnThreads) k_residual_layernorm(const uint16_t* y, const uint16_t* residual,
+                                                                   int T, int H, float eps, uint16_t* out) {
+    griddep_wait();
+    griddep_launch();
+    const int t = static_cast<int>(blockIdx.x);
+    if (t >= T) return;
+    __shared__ float red[32];
+    float v[kLnMaxPerThread];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < kLnMaxPerThread / 8; ++j) {
+        const int c = (static_cast<int>(threadIdx.x) + j * kLnThreads) * 8;
+        if (c < H) {
+            float a[8], b[8];
+            unpack8(*reinterpret_cast<const uint4*>(y + static_cast<size_t>(t) * H + c), a);
+            unpack8(*reinterpret_cast<const uint4*>(residual + static_cast<size_t>(t) * H + c), b);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                v[j * 8 + i] = a[i] + b[i];
+                s += v[j * 8 + i];
+            }
+        }
+    }
+    const float mean = block_sum_ln(s, red) / static_cast<float>(H);
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < kLnMaxPerThread / 8; ++j) {
+        const int c = (static_cast<int>(threadIdx.x) + j * kLnThreads) * 8;
+        if (c < H) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float d = v[j * 8 + i] - mean;
+                q += d * d;
+            }
+        }
+    }
+    const float var = block_sum_ln(q, red) / static_cast<float>(H);
+    const float inv = 1.0f / sqrtf(var + eps);
+#pragma unroll
+    for (int j = 0; j < kLnMaxPerThread / 8; ++j) {
+        const int c = (static_cast<int>(threadIdx.x) + j * kLnThreads) * 8;
+        if (c < H) {
+            float o[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = (v[j * 8 + i] - mean) * inv;
+            *reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H + c) = pack8(o);
+        }
+    }
+}
+
 }  // namespace pdx

@@ -751,6 +751,20 @@ int pdx_combine(const void* y, const void* weights, const int32_t* inverse, int6
     return ok();
 }
 
+int pdx_residual_layernorm(const void* y, const void* residual, int64_t T, int64_t H, float eps, void* out,
+                           pdx_stream_t stream) {
+    if (!y || !residual || !out) return fail(PDX_ERR_INVALID, "null layer-norm argument");
+    if (T < 1) return fail(PDX_ERR_INVALID, "empty layer-norm batch");
+    if (H < 8 || H % 8 || H > 8 * kLnThreads * (kLnMaxPerThread / 8))
+        return fail(PDX_ERR_UNSUPPORTED, "layer norm needs H a multiple of 8 and <= %d",
+                    8 * kLnThreads * (kLnMaxPerThread / 8));
+    if (!(eps > 0.f)) return fail(PDX_ERR_INVALID, "eps must be positive");
+    PDX_PDL_TRY(launch_pdl(k_residual_layernorm, dim3(static_cast<unsigned>(T)), dim3(kLnThreads), 0, stream,
+                           static_cast<const uint16_t*>(y), static_cast<const uint16_t*>(residual),
+                           static_cast<int>(T), static_cast<int>(H), eps, static_cast<uint16_t*>(out)));
+    return ok();
+}
+
 size_t pdx_layer_workspace_bytes(int64_t T, int64_t H, int64_t E, int32_t top_k, int64_t I, int32_t mode) {
     T = std::max<int64_t>(T, 1);
     E = std::max<int64_t>(E, 1);

@@ -35,7 +35,7 @@ import torch
 
 from . import _lib
 from ._lib import check, lib
-from .runtime import ExpertSlab, Packed, _ptr, _stream, pack as _pack
+from .runtime import ExpertSlab, Packed, _ptr, _stream, pack as _pack, residual_layernorm
 
 PADDED_MAX_TOKENS = 256
 
@@ -236,8 +236,8 @@ def local_slab_of(full_slab, rank, world):
 class ExpertParallelStack:
     """``layers`` expert-parallel MoE layers driven as one step on every rank.
 
-    Layer l+1's input is ``x_l + MoE_l(x_l)`` (residual fused into the
-    combine).  ``step`` replays one CUDA graph per batch size holding every
+    Layer l+1's input is ``layer_norm(MoE_l(x_l) + x_l)`` (the resident
+    stack's next-layer activation).  ``step`` replays one CUDA graph per batch size holding every
     layer's kernels and NCCL exchanges (padded exchange only: all ranks must
     use the same batch size).
     """
@@ -259,7 +259,8 @@ class ExpertParallelStack:
         x, out = self.io(t_count)
         h = x
         for layer in self.layers:
-            h = layer.forward(h, residual=h, mode=mode)
+            y = layer.forward(h, residual=None, mode=mode)
+            h = residual_layernorm(y, h, out=y)
         out.copy_(h)
 
     def step(self, t_count, *, graph=True):

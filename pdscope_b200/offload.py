@@ -46,7 +46,7 @@ import torch
 
 from . import _lib
 from ._lib import ExpertWeights, check, lib
-from .runtime import _ptr, _stream
+from .runtime import _ptr, _stream, residual_layernorm
 
 
 @dataclass
@@ -226,7 +226,7 @@ class OffloadMoEStack:
         ws = max(lib.pdx_route_workspace_bytes(t, E), lib.pdx_pack_workspace_bytes(t, k, E),
                  lib.pdx_ffn_workspace_bytes(n, E, H, self.I, _lib.FFN_AUTO))
         b = dict(cur=routing(), nxt=routing(), counts=counts, rows=torch.empty((n, H), **bf),
-                 acts=[torch.empty((t, H), **bf) for _ in range(2)],
+                 acts=[torch.empty((t, H), **bf) for _ in range(2)], moe=torch.empty((t, H), **bf),
                  ws=torch.empty(ws, dtype=torch.uint8, device=dev))
         self._bufs[t] = b
         return b
@@ -365,14 +365,16 @@ class OffloadMoEStack:
         return out
 
     def forward(self, x):
-        """Every layer on ``x`` [T, H]; layer l+1's input is x_l + MoE_l(x_l).
-        Returns a buffer owned by the stack (valid until the next call with the
-        same token count)."""
+        """Every layer on ``x`` [T, H]; layer l+1's input is
+        layer_norm(MoE_l(x_l) + x_l) (the next-layer activation of the resident
+        stack).  Returns a buffer owned by the stack (valid until the next call
+        with the same token count)."""
         b = self._buffers(x.shape[0])
         h = x
         for l in range(self.L):
             out = b["acts"][l % 2]
-            self.forward_layer(l, h, out, residual=h)
+            self.forward_layer(l, h, b["moe"], residual=None)
+            residual_layernorm(b["moe"], h, out=out)
             h = out
         return h
 

@@ -283,6 +283,26 @@ def combine(rows, weights, inverse, residual=None):
     return out
 
 
+LN_EPS = 1e-5
+
+
+def residual_layernorm(y, residual, eps=LN_EPS, out=None):
+    """Next-layer activation of a multi-layer stack as the reference's
+    two-layer protocol forms it (benchmarks/pdscope_compare.py:609-705):
+    ``layer_norm(y.float() + residual.float(), (H,)).to(bf16)``.  ``out`` may
+    be ``y`` or ``residual``."""
+    _require_cuda_bf16("y", y, 2)
+    _require_cuda_bf16("residual", residual, 2)
+    if y.shape != residual.shape:
+        raise ValueError("y and residual shapes differ")
+    t_count, hidden = y.shape
+    if out is None:
+        out = torch.empty_like(y)
+    check(lib.pdx_residual_layernorm(_ptr(y), _ptr(residual), t_count, hidden, ctypes.c_float(eps), _ptr(out),
+                                     _stream()))
+    return out
+
+
 # ---------------------------------------------------------------------------
 # Weight placement
 # ---------------------------------------------------------------------------
