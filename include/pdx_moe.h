@@ -148,7 +148,9 @@ int pdx_gather_rows(const void *x, const int32_t *tokens, int64_t rows, int64_t 
  * for every packed row p of every active expert, UNWEIGHTED, in packed order,
  * with the reference's BF16 roundings (after each linear, after silu, after
  * the product).  `x` is the [T,H] token matrix; rows are gathered through
- * `tokens` (tokens == NULL: x already holds the `rows` rows in packed order).  mode: 0 = auto; 1 = decode path (weights streamed by TMA as the
+ * `tokens` (tokens == NULL: x already holds the `rows` rows in packed order).
+ * mode: 0 = auto (the decode path up to 16 rows per expert on average, else
+ * the prefill path); 1 = decode path (weights streamed by TMA as the
  * tcgen05 M operand, tokens as N, split-K for few experts); 2 = prefill path
  * (tcgen05 grouped GEMM tiled over tokens, 128 x 256 tiles on single CTAs);
  * 3 = SIMT weight-streaming GEMV (an independent implementation kept for
@@ -199,6 +201,18 @@ int pdx_combine(const void *y, const void *weights, const int32_t *inverse, int6
  * it keeps a synthetic stack's activations at unit scale. */
 int pdx_residual_layernorm(const void *y, const void *residual, int64_t T, int64_t H, float eps, void *out,
                            pdx_stream_t stream);
+
+/* Combine and next-layer norm in one pass (bit-identical to pdx_combine with
+ * residual = NULL followed by pdx_residual_layernorm): out[t] =
+ * bf16(layer_norm(bf16(sum_s bf16(y_s * w_s)) + residual[t])).  residual must
+ * not alias y; it may alias out. */
+int pdx_combine_layernorm(const void *y, const void *weights, const int32_t *inverse, int64_t T, int32_t top_k,
+                          int64_t H, const void *residual, float eps, void *out, pdx_stream_t stream);
+
+/* OR into pdx_moe_layer's mode: out = layer_norm(MoE(x) + residual) with
+ * eps PDX_LAYER_NORM_EPS (the fused combine above); residual is required. */
+#define PDX_LAYER_OUT_NORM 0x100
+#define PDX_LAYER_NORM_EPS 1e-5f
 
 /* ---------------------------------------------------------------------------
  * Whole layer: route -> pack -> grouped FFN -> combine, all on `stream`, no

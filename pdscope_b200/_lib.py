@@ -25,6 +25,7 @@ PDX_DEVERR_BAD_EXPERT = 2
 PDX_DEVERR_BAD_SLOT = 3
 
 FFN_AUTO, FFN_GEMV, FFN_GEMM, FFN_SIMT, FFN_GEMM_1CTA, FFN_GEMM_PAIR = 0, 1, 2, 3, 4, 5
+LAYER_OUT_NORM = 0x100   # OR into pdx_moe_layer's mode: out = layer_norm(MoE(x) + residual)
 
 ABI_VERSION = 1
 
@@ -64,6 +65,8 @@ SIGNATURES = {
     "pdx_expert_ffn": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_sz, c_vp]),
     "pdx_combine": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, c_i32, c_i64, c_vp, c_vp, c_vp]),
     "pdx_residual_layernorm": (ctypes.c_int, [c_vp, c_vp, c_i64, c_i64, ctypes.c_float, c_vp, c_vp]),
+    "pdx_combine_layernorm": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, c_i32, c_i64, c_vp, ctypes.c_float, c_vp,
+                                             c_vp]),
     "pdx_layer_workspace_bytes": (c_sz, [c_i64, c_i64, c_i64, c_i32, c_i64, c_i32]),
     "pdx_moe_layer": (ctypes.c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_i32,
                                      ctypes.POINTER(ExpertWeights), c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,

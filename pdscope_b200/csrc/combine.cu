@@ -30,6 +30,48 @@ __device__ __forceinline__ uint4 pack8(const float* f) {
     return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// Combine setup: the k (row, weight) pairs of token t into shared memory.
+// Entries outside [0, y_rows) are flagged and contribute nothing.
+__device__ __forceinline__ void combine_slots(const uint16_t* __restrict__ weights,
+                                              const int32_t* __restrict__ inverse, int t, int k, int y_rows,
+                                              int* s_row, float* s_w) {
+    if (threadIdx.x < static_cast<unsigned>(k)) {
+        int row = inverse[static_cast<size_t>(t) * k + threadIdx.x];
+        float w = bits2f(weights[static_cast<size_t>(t) * k + threadIdx.x]);
+        if (row < 0 || row >= y_rows) {
+            raise_error(PDX_DEVERR_BAD_EXPERT);
+            row = 0;
+            w = 0.f;
+        }
+        s_row[threadIdx.x] = row;
+        s_w[threadIdx.x] = w;
+    }
+    __syncthreads();
+}
+
+// acc[0..8) += sum_{s<k} bf16(y[row_s][c..c+8) * w_s), FP32, in slot order
+// (the loads of up to 8 expert rows are issued before accumulating).
+__device__ __forceinline__ void combine_chunk(const uint16_t* __restrict__ y, const int* s_row, const float* s_w,
+                                              int k, int H, int c, float* acc) {
+    for (int s0 = 0; s0 < k; s0 += 8) {
+        uint4 rv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (s0 + j < k)
+                rv[j] = __ldg(reinterpret_cast<const uint4*>(y + static_cast<size_t>(s_row[s0 + j]) * H + c));
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (s0 + j < k) {
+                float v[8];
+                unpack8(rv[j], v);
+                const float w = s_w[s0 + j];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[i] += round_bf16(v[i] * w);
+            }
+        }
+    }
+}
+
 // out[t] = bf16( residual[t] + sum_{s<k} bf16(y[inverse[t*k+s]] * w[t*k+s]) )
 // y has y_rows rows; inverse entries outside [0, y_rows) are flagged and skipped.
 __global__ void __launch_bounds__(kCombineThreads) k_combine(const uint16_t* __restrict__ y,
@@ -43,18 +85,7 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(const uint16_t* __r
     if (t >= T) return;
     __shared__ int s_row[32];
     __shared__ float s_w[32];
-    if (threadIdx.x < static_cast<unsigned>(k)) {
-        int row = inverse[static_cast<size_t>(t) * k + threadIdx.x];
-        float w = bits2f(weights[static_cast<size_t>(t) * k + threadIdx.x]);
-        if (row < 0 || row >= y_rows) {  // not a valid row of y: flag, contribute nothing
-            raise_error(PDX_DEVERR_BAD_EXPERT);
-            row = 0;
-            w = 0.f;
-        }
-        s_row[threadIdx.x] = row;
-        s_w[threadIdx.x] = w;
-    }
-    __syncthreads();
+    combine_slots(weights, inverse, t, k, y_rows, s_row, s_w);
     for (int c = static_cast<int>(threadIdx.x) * 8; c < H; c += blockDim.x * 8) {
         float acc[8];
         if (residual) {
@@ -63,24 +94,7 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(const uint16_t* __r
 #pragma unroll
             for (int i = 0; i < 8; ++i) acc[i] = 0.f;
         }
-        // issue the loads of up to 8 expert rows before accumulating (slot order)
-        for (int s0 = 0; s0 < k; s0 += 8) {
-            uint4 rv[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                if (s0 + j < k)
-                    rv[j] = __ldg(reinterpret_cast<const uint4*>(y + static_cast<size_t>(s_row[s0 + j]) * H + c));
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                if (s0 + j < k) {
-                    float v[8];
-                    unpack8(rv[j], v);
-                    const float w = s_w[s0 + j];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) acc[i] += round_bf16(v[i] * w);
-                }
-            }
-        }
+        combine_chunk(y, s_row, s_w, k, H, c, acc);
         *reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H + c) = pack8(acc);
     }
 }
@@ -134,6 +148,37 @@ __device__ __forceinline__ float block_sum_ln(float v, float* red) {
     return tot;
 }
 
+// Normalise the row held in v (this thread's chunks c = (tid + 256 j) * 8)
+// and store it: population variance, FP32 statistics in a fixed order.
+__device__ __forceinline__ void layernorm_store(float (&v)[kLnMaxPerThread], float sum, int H, float eps,
+                                                uint16_t* out_row, float* red) {
+    const float mean = block_sum_ln(sum, red) / static_cast<float>(H);
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < kLnMaxPerThread / 8; ++j) {
+        const int c = (static_cast<int>(threadIdx.x) + j * kLnThreads) * 8;
+        if (c < H) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float d = v[j * 8 + i] - mean;
+                q += d * d;
+            }
+        }
+    }
+    const float var = block_sum_ln(q, red) / static_cast<float>(H);
+    const float inv = 1.0f / sqrtf(var + eps);
+#pragma unroll
+    for (int j = 0; j < kLnMaxPerThread / 8; ++j) {
+        const int c = (static_cast<int>(threadIdx.x) + j * kLnThreads) * 8;
+        if (c < H) {
+            float o[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = (v[j * 8 + i] - mean) * inv;
+            *reinterpret_cast<uint4*>(out_row + c) = pack8(o);
+        }
+    }
+}
+
 // out may alias y or residual: a CTA reads its whole row before writing it.
 __global__ void __launch_bounds__(kLnThreads) k_residual_layernorm(const uint16_t* y, const uint16_t* residual,
                                                                    int T, int H, float eps, uint16_t* out) {
@@ -158,31 +203,44 @@ __global__ void __launch_bounds__(kLnThreads) k_residual_layernorm(const uint16_
             }
         }
     }
-    const float mean = block_sum_ln(s, red) / static_cast<float>(H);
-    float q = 0.f;
+    layernorm_store(v, s, H, eps, out + static_cast<size_t>(t) * H, red);
+}
+
+// Combine and next-layer norm in one pass, bit-identical to k_combine (no
+// residual) followed by k_residual_layernorm:
+//   out[t] = bf16( layer_norm( bf16(sum_s bf16(y_s * w_s)) + residual[t] ) )
+// residual must not alias y (the expert rows of other tokens); it may alias out.
+__global__ void __launch_bounds__(kCombineThreads) k_combine_norm(const uint16_t* __restrict__ y,
+                                                                  const uint16_t* __restrict__ weights,
+                                                                  const int32_t* __restrict__ inverse, int T, int k,
+                                                                  int H, int y_rows, const uint16_t* residual,
+                                                                  float eps, uint16_t* out) {
+    griddep_wait();
+    griddep_launch();
+    const int t = static_cast<int>(blockIdx.x);
+    if (t >= T) return;
+    __shared__ int s_row[32];
+    __shared__ float s_w[32];
+    __shared__ float red[32];
+    combine_slots(weights, inverse, t, k, y_rows, s_row, s_w);
+    float v[kLnMaxPerThread];
+    float sum = 0.f;
 #pragma unroll
     for (int j = 0; j < kLnMaxPerThread / 8; ++j) {
         const int c = (static_cast<int>(threadIdx.x) + j * kLnThreads) * 8;
         if (c < H) {
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            combine_chunk(y, s_row, s_w, k, H, c, acc);
+            float r[8];
+            unpack8(*reinterpret_cast<const uint4*>(residual + static_cast<size_t>(t) * H + c), r);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const float d = v[j * 8 + i] - mean;
-                q += d * d;
+                v[j * 8 + i] = round_bf16(acc[i]) + r[i];
+                sum += v[j * 8 + i];
             }
         }
     }
-    const float var = block_sum_ln(q, red) / static_cast<float>(H);
-    const float inv = 1.0f / sqrtf(var + eps);
-#pragma unroll
-    for (int j = 0; j < kLnMaxPerThread / 8; ++j) {
-        const int c = (static_cast<int>(threadIdx.x) + j * kLnThreads) * 8;
-        if (c < H) {
-            float o[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = (v[j * 8 + i] - mean) * inv;
-            *reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H + c) = pack8(o);
-        }
-    }
+    layernorm_store(v, sum, H, eps, out + static_cast<size_t>(t) * H, red);
 }
 
 }  // namespace pdx

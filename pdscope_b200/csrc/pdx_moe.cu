@@ -200,7 +200,7 @@ constexpr int kMaxTopK = 32;
 constexpr int kMaxExperts = 1024;
 constexpr int64_t kTailMaxTokens = 64;     // fused route tail up to this many tokens
 constexpr int64_t kPackSingleMax = 8192;   // single-CTA pack up to this many assignments
-constexpr int64_t kGemvMaxTokens = 64;     // auto mode: GEMV for T <= this
+constexpr int64_t kStreamMaxRowsPerExpert = 16;  // auto mode: weight streaming up to this average
 
 int check_route_shape(int64_t T, int64_t H, int64_t E, int32_t k) {
     if (T < 1) return fail(PDX_ERR_INVALID, "empty expert routing (T=%lld)", static_cast<long long>(T));
@@ -219,10 +219,17 @@ bool gemm_shape_ok(int64_t H, int64_t I) { return H % 256 == 0 && I % 128 == 0 &
 bool is_gemm_mode(int mode) { return mode == PDX_FFN_GEMM || mode == PDX_FFN_GEMM_1CTA || mode == PDX_FFN_GEMM_PAIR; }
 bool stream_shape_ok(int64_t H, int64_t I) { return H % 128 == 0 && I % 128 == 0 && H >= 128 && I >= 128; }
 
-int resolve_mode(int32_t mode, int64_t T, int64_t H, int64_t I) {
+// Auto mode picks the path from the average rows per expert: the
+// weight-streaming path reads each active expert's weights once per 16/32-row
+// token tile, the token-tiled GEMM once per 128-row tile at full tensor-core
+// tile efficiency.  Measured on one Qwen3-30B-A3B layer (E=128, k=8): streaming
+// is ahead up to T = 256 (16 rows per expert), the GEMM from T = 384 on.
+int resolve_mode(int32_t mode, int64_t rows, int64_t E, int64_t H, int64_t I) {
     if (mode != PDX_FFN_AUTO) return mode;
-    if (T > kGemvMaxTokens && gemm_shape_ok(H, I)) return PDX_FFN_GEMM;
+    const bool few_rows = rows <= kStreamMaxRowsPerExpert * std::max<int64_t>(E, 1);
+    if (!few_rows && gemm_shape_ok(H, I)) return PDX_FFN_GEMM;
     if (stream_shape_ok(H, I)) return PDX_FFN_GEMV;
+    if (gemm_shape_ok(H, I)) return PDX_FFN_GEMM;
     return PDX_FFN_SIMT;
 }
 
@@ -600,6 +607,13 @@ PackBufs carve_pack(Carver& c, int64_t T, int32_t k, int64_t E, int32_t* counts_
 
 using namespace pdx;
 
+int check_norm_shape(int64_t H) {
+    if (H < 8 || H % 8 || H > 8 * kLnThreads * (kLnMaxPerThread / 8))
+        return fail(PDX_ERR_UNSUPPORTED, "layer norm needs H a multiple of 8 and <= %d",
+                    8 * kLnThreads * (kLnMaxPerThread / 8));
+    return PDX_OK;
+}
+
 extern "C" {
 
 const char* pdx_last_error(void) { return t_last_error.c_str(); }
@@ -682,13 +696,8 @@ int pdx_gather_rows(const void* x, const int32_t* tokens, int64_t rows, int64_t 
 size_t pdx_ffn_workspace_bytes(int64_t rows, int64_t E, int64_t H, int64_t I, int32_t mode) {
     rows = std::max<int64_t>(rows, 1);
     E = std::max<int64_t>(E, 1);
-    const int m = resolve_mode(mode, rows, H, I);
-    size_t b = ffn_ws_bytes(rows, E, H, I, m);
-    // auto mode resolves on the token count T, which may be <= 64 (decode path)
-    // while rows = T*k exceeds 64: cover that path too (T*k <= 64*kMaxTopK)
-    if (mode == PDX_FFN_AUTO && m != PDX_FFN_GEMV && rows <= kGemvMaxTokens * kMaxTopK && stream_shape_ok(H, I))
-        b = std::max(b, ffn_ws_bytes(rows, E, H, I, PDX_FFN_GEMV));
-    return b + kAlign;
+    const int m = resolve_mode(mode, rows, E, H, I);
+    return ffn_ws_bytes(rows, E, H, I, m) + kAlign;
 }
 
 int pdx_moe_ffn_grouped(const void* x, int64_t T, const int32_t* tokens, const int32_t* offsets,
@@ -697,7 +706,7 @@ int pdx_moe_ffn_grouped(const void* x, int64_t T, const int32_t* tokens, const i
                         pdx_stream_t stream) {
     if (!x || !offsets || !active || !y_out) return fail(PDX_ERR_INVALID, "null FFN argument");
     if (T < 1 || rows < 1 || E < 1) return fail(PDX_ERR_INVALID, "empty FFN batch");
-    const int m = resolve_mode(mode, T, H, I);
+    const int m = resolve_mode(mode, rows, E, H, I);
     int st = check_ffn_shape(H, I, m);
     if (st) return st;
     if ((st = check_weights(weights, H, I))) return st;
@@ -710,7 +719,7 @@ int pdx_moe_ffn_grouped(const void* x, int64_t T, const int32_t* tokens, const i
 
 size_t pdx_expert_ffn_workspace_bytes(int64_t n, int64_t H, int64_t I) {
     const int64_t nn = std::max<int64_t>(n, 1);
-    const int m = resolve_mode(PDX_FFN_AUTO, nn, H, I);
+    const int m = resolve_mode(PDX_FFN_AUTO, nn, 1, H, I);
     return align_up(8) * 2 + align_up(nn * 4) + ffn_ws_bytes(nn, 1, H, I, m) + kAlign;
 }
 
@@ -718,7 +727,7 @@ int pdx_expert_ffn(const void* x, int64_t n, const void* gate, const void* up, c
                    void* y_out, void* workspace, size_t workspace_bytes, pdx_stream_t stream) {
     if (!x || !gate || !up || !down || !y_out) return fail(PDX_ERR_INVALID, "null expert argument");
     if (n < 1) return fail(PDX_ERR_INVALID, "expert input must have at least one row");
-    const int m = resolve_mode(PDX_FFN_AUTO, n, H, I);
+    const int m = resolve_mode(PDX_FFN_AUTO, n, 1, H, I);
     int st = check_ffn_shape(H, I, m);
     if (st) return st;
     if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1)) ||
@@ -735,6 +744,22 @@ int pdx_expert_ffn(const void* x, int64_t n, const void* gate, const void* up, c
     PDX_LAUNCHED();
     st = launch_ffn(x, n, tokens, offsets, active, 1, n, &w, H, I, y_out, m, c, stream);
     return st ? st : ok();
+}
+
+int pdx_combine_layernorm(const void* y, const void* weights, const int32_t* inverse, int64_t T, int32_t top_k,
+                          int64_t H, const void* residual, float eps, void* out, pdx_stream_t stream) {
+    if (!y || !weights || !inverse || !residual || !out) return fail(PDX_ERR_INVALID, "null combine argument");
+    if (T < 1 || top_k < 1) return fail(PDX_ERR_INVALID, "empty combine");
+    if (top_k > kMaxTopK) return fail(PDX_ERR_UNSUPPORTED, "top_k > %d", kMaxTopK);
+    int st = check_norm_shape(H);
+    if (st) return st;
+    if (!(eps > 0.f)) return fail(PDX_ERR_INVALID, "eps must be positive");
+    PDX_PDL_TRY(launch_pdl(k_combine_norm, dim3(static_cast<unsigned>(T)), dim3(kCombineThreads), 0, stream,
+                           static_cast<const uint16_t*>(y), static_cast<const uint16_t*>(weights), inverse,
+                           static_cast<int>(T), static_cast<int>(top_k), static_cast<int>(H),
+                           static_cast<int>(T * top_k), static_cast<const uint16_t*>(residual), eps,
+                           static_cast<uint16_t*>(out)));
+    return ok();
 }
 
 int pdx_combine(const void* y, const void* weights, const int32_t* inverse, int64_t T, int32_t top_k, int64_t H,
@@ -755,9 +780,8 @@ int pdx_residual_layernorm(const void* y, const void* residual, int64_t T, int64
                            pdx_stream_t stream) {
     if (!y || !residual || !out) return fail(PDX_ERR_INVALID, "null layer-norm argument");
     if (T < 1) return fail(PDX_ERR_INVALID, "empty layer-norm batch");
-    if (H < 8 || H % 8 || H > 8 * kLnThreads * (kLnMaxPerThread / 8))
-        return fail(PDX_ERR_UNSUPPORTED, "layer norm needs H a multiple of 8 and <= %d",
-                    8 * kLnThreads * (kLnMaxPerThread / 8));
+    int st = check_norm_shape(H);
+    if (st) return st;
     if (!(eps > 0.f)) return fail(PDX_ERR_INVALID, "eps must be positive");
     PDX_PDL_TRY(launch_pdl(k_residual_layernorm, dim3(static_cast<unsigned>(T)), dim3(kLnThreads), 0, stream,
                            static_cast<const uint16_t*>(y), static_cast<const uint16_t*>(residual),
@@ -766,6 +790,7 @@ int pdx_residual_layernorm(const void* y, const void* residual, int64_t T, int64
 }
 
 size_t pdx_layer_workspace_bytes(int64_t T, int64_t H, int64_t E, int32_t top_k, int64_t I, int32_t mode) {
+    mode &= ~PDX_LAYER_OUT_NORM;
     T = std::max<int64_t>(T, 1);
     E = std::max<int64_t>(E, 1);
     top_k = std::max<int32_t>(top_k, 1);
@@ -778,7 +803,7 @@ size_t pdx_layer_workspace_bytes(int64_t T, int64_t H, int64_t E, int32_t top_k,
     c.take(N * 2);               // weights
     carve_pack(c, T, top_k, E, nullptr);
     c.take(N * H * 2);           // y
-    const int m = resolve_mode(mode, T, H, I);
+    const int m = resolve_mode(mode, T * top_k, E, H, I);
     return c.used + ffn_ws_bytes(N, E, H, I, m) + kAlign;
 }
 
@@ -789,7 +814,13 @@ int pdx_moe_layer(const void* x, const void* gate, int64_t T, int64_t H, int64_t
     int st = check_route_shape(T, H, E, top_k);
     if (st) return st;
     if (!x || !gate || !out) return fail(PDX_ERR_INVALID, "null layer argument");
-    const int m = resolve_mode(mode, T, H, I);
+    const bool out_norm = (mode & PDX_LAYER_OUT_NORM) != 0;
+    mode &= ~PDX_LAYER_OUT_NORM;
+    if (out_norm) {
+        if (!residual) return fail(PDX_ERR_INVALID, "PDX_LAYER_OUT_NORM needs a residual");
+        if ((st = check_norm_shape(H))) return st;
+    }
+    const int m = resolve_mode(mode, T * top_k, E, H, I);
     if ((st = check_ffn_shape(H, I, m))) return st;
     if ((st = check_weights(weights, H, I))) return st;
     if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1)))
@@ -810,11 +841,19 @@ int pdx_moe_layer(const void* x, const void* gate, int64_t T, int64_t H, int64_t
     if (!fused && (st = launch_pack(rb.selected, rb.weights, T, top_k, E, pb.o, pb.chunk_hist, stream))) return st;
     if ((st = launch_ffn(x, T, pb.o.tokens, pb.o.offsets, pb.o.active, E, N, weights, H, I, y, m, c, stream)))
         return st;
-    PDX_PDL_TRY(launch_pdl(k_combine, dim3(static_cast<unsigned>(T)), dim3(kCombineThreads), 0, stream,
-                           static_cast<const uint16_t*>(y), static_cast<const uint16_t*>(rb.weights),
-                           static_cast<const int32_t*>(pb.o.inverse), static_cast<int>(T), static_cast<int>(top_k),
-                           static_cast<int>(H), static_cast<int>(N), static_cast<const uint16_t*>(residual),
-                           static_cast<uint16_t*>(out)));
+    if (out_norm)
+        PDX_PDL_TRY(launch_pdl(k_combine_norm, dim3(static_cast<unsigned>(T)), dim3(kCombineThreads), 0, stream,
+                               static_cast<const uint16_t*>(y), static_cast<const uint16_t*>(rb.weights),
+                               static_cast<const int32_t*>(pb.o.inverse), static_cast<int>(T),
+                               static_cast<int>(top_k), static_cast<int>(H), static_cast<int>(N),
+                               static_cast<const uint16_t*>(residual), PDX_LAYER_NORM_EPS,
+                               static_cast<uint16_t*>(out)));
+    else
+        PDX_PDL_TRY(launch_pdl(k_combine, dim3(static_cast<unsigned>(T)), dim3(kCombineThreads), 0, stream,
+                               static_cast<const uint16_t*>(y), static_cast<const uint16_t*>(rb.weights),
+                               static_cast<const int32_t*>(pb.o.inverse), static_cast<int>(T),
+                               static_cast<int>(top_k), static_cast<int>(H), static_cast<int>(N),
+                               static_cast<const uint16_t*>(residual), static_cast<uint16_t*>(out)));
     return ok();
 }
 

@@ -76,7 +76,9 @@ class DeviceOps:
 
     def dispatch(self, x, p, top_k, experts, ranks, capacity):
         t_count, hidden = x.shape
-        send = torch.zeros((ranks * capacity, hidden), dtype=x.dtype, device=x.device)
+        # rows past a block's count are sent but never read (the receiver's layout
+        # comes from the counts), so the buffer needs no clearing
+        send = torch.empty((ranks * capacity, hidden), dtype=x.dtype, device=x.device)
         inv_ep = torch.empty(t_count * top_k, dtype=torch.int32, device=x.device)
         check(lib.pdx_ep_dispatch(_ptr(x), _ptr(p.tokens), _ptr(p.positions), _ptr(p.offsets), t_count, top_k,
                                   hidden, experts, ranks, capacity, _ptr(send), _ptr(inv_ep), _stream()))

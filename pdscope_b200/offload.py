@@ -46,7 +46,7 @@ import torch
 
 from . import _lib
 from ._lib import ExpertWeights, check, lib
-from .runtime import _ptr, _stream, residual_layernorm
+from .runtime import LN_EPS, _ptr, _stream
 
 
 @dataclass
@@ -226,7 +226,7 @@ class OffloadMoEStack:
         ws = max(lib.pdx_route_workspace_bytes(t, E), lib.pdx_pack_workspace_bytes(t, k, E),
                  lib.pdx_ffn_workspace_bytes(n, E, H, self.I, _lib.FFN_AUTO))
         b = dict(cur=routing(), nxt=routing(), counts=counts, rows=torch.empty((n, H), **bf),
-                 acts=[torch.empty((t, H), **bf) for _ in range(2)], moe=torch.empty((t, H), **bf),
+                 acts=[torch.empty((t, H), **bf) for _ in range(2)],
                  ws=torch.empty(ws, dtype=torch.uint8, device=dev))
         self._bufs[t] = b
         return b
@@ -277,8 +277,9 @@ class OffloadMoEStack:
         return ev
 
     # ---- one layer --------------------------------------------------------------------
-    def forward_layer(self, l, x, out, residual=None):
-        """out = residual + MoE_l(x) (residual may be None)."""
+    def forward_layer(self, l, x, out, residual=None, norm=False):
+        """out = residual + MoE_l(x) (residual may be None), or with ``norm``
+        layer_norm(MoE_l(x) + residual), the stack's next-layer activation."""
         t = x.shape[0]
         b = self._buffers(t)
         comp = torch.cuda.current_stream(self.dev)
@@ -356,8 +357,12 @@ class OffloadMoEStack:
         for c, (_, ev) in enumerate(chunks):
             comp.wait_event(ev)
             self._ffn(l, x, cur, 1 + c, rows, ws)
-        check(lib.pdx_combine(_ptr(rows), _ptr(cur["w"]), _ptr(cur["inverse"]), t, self.k, self.H, _ptr(residual),
-                              _ptr(out), _stream()))
+        if norm:
+            check(lib.pdx_combine_layernorm(_ptr(rows), _ptr(cur["w"]), _ptr(cur["inverse"]), t, self.k, self.H,
+                                            _ptr(residual), ctypes.c_float(LN_EPS), _ptr(out), _stream()))
+        else:
+            check(lib.pdx_combine(_ptr(rows), _ptr(cur["w"]), _ptr(cur["inverse"]), t, self.k, self.H,
+                                  _ptr(residual), _ptr(out), _stream()))
         done = torch.cuda.Event()
         done.record(comp)
         for idx in pinned:
@@ -373,8 +378,7 @@ class OffloadMoEStack:
         h = x
         for l in range(self.L):
             out = b["acts"][l % 2]
-            self.forward_layer(l, h, b["moe"], residual=None)
-            residual_layernorm(b["moe"], h, out=out)
+            self.forward_layer(l, h, out, residual=h, norm=True)
             h = out
         return h
 

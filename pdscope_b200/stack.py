@@ -6,7 +6,8 @@ per-layer host work of the reference (``.tolist()`` syncs in grouping,
 pdscope_runtime.py:26, qwen.py:162,171, and one Python call chain per expert)
 disappears from the step.  The activation of layer l+1 is
 ``layer_norm(MoE_l(x_l) + x_l)``, the reference's two-layer protocol
-(pdscope_compare.py:609-705): it keeps every layer's input at unit scale, as
+(pdscope_compare.py:609-705), fused into the combine kernel
+(PDX_LAYER_OUT_NORM): it keeps every layer's input at unit scale, as
 the synthetic configs specify (without it the random residual stream grows
 layer by layer until the last layers compute on inf/NaN).
 
@@ -78,12 +79,11 @@ class ResidentMoEStack:
                                inverse=torch.empty(n, **i32), active=torch.empty(E + 1, **i32))
                   for _ in range(L)]
         rows = torch.empty((n, H), **bf)  # expert outputs of the current layer (staged path)
-        moe = torch.empty((t_count, H), **bf)  # MoE output of the current layer (before the norm)
         ws_layer = lib.pdx_layer_workspace_bytes(t_count, H, E, k, self.inter, mode)
         ws_stage = max(lib.pdx_route_workspace_bytes(t_count, E), lib.pdx_pack_workspace_bytes(t_count, k, E),
                        lib.pdx_ffn_workspace_bytes(n, E, H, self.inter, mode))
         ws = torch.empty(max(ws_layer, ws_stage), dtype=torch.uint8, device=dev)
-        b = dict(acts=acts, stages=stages, ws=ws, rows=rows, moe=moe)
+        b = dict(acts=acts, stages=stages, ws=ws, rows=rows)
         self._bufs[key] = b
         return b
 
@@ -98,17 +98,16 @@ class ResidentMoEStack:
     # -- fused path: one C-ABI call per layer -------------------------------------
     def _step_fused(self, t_count, mode):
         b = self.buffers(t_count, mode)
-        acts, stages, ws, moe = b["acts"], b["stages"], b["ws"], b["moe"]
+        acts, stages, ws = b["acts"], b["stages"], b["ws"]
         s = _stream()
         for l in range(self.num_layers):
             st = stages[l]
             x_in, x_out = self._act_in(acts, l), self._act_out(acts, l)
             check(lib.pdx_moe_layer(_ptr(x_in), _ptr(self.gates[l]), t_count, self.hidden, self.experts,
                                     self.top_k, int(self.normalize), ctypes.byref(self.slabs[l].struct), self.inter,
-                                    None, _ptr(moe), _ptr(st.logits), _ptr(st.selected),
-                                    _ptr(st.weights), _ptr(st.counts), mode, _ptr(ws), ws.numel(), s))
-            check(lib.pdx_residual_layernorm(_ptr(moe), _ptr(x_in), t_count, self.hidden, ctypes.c_float(LN_EPS),
-                                             _ptr(x_out), s))
+                                    _ptr(x_in), _ptr(x_out), _ptr(st.logits), _ptr(st.selected),
+                                    _ptr(st.weights), _ptr(st.counts), mode | _lib.LAYER_OUT_NORM, _ptr(ws),
+                                    ws.numel(), s))
 
     # -- staged path: route, pack, FFN, combine as separate calls --------------------
     def route_and_pack(self, l, t_count, mode=_lib.FFN_AUTO):
@@ -132,23 +131,18 @@ class ResidentMoEStack:
                                       mode, _ptr(ws), ws.numel(), _stream()))
 
     def combine(self, l, t_count, mode=_lib.FFN_AUTO):
+        """Weighted combine fused with the next-layer norm."""
         b = self.buffers(t_count, mode)
         st = b["stages"][l]
-        check(lib.pdx_combine(_ptr(b["rows"]), _ptr(st.weights), _ptr(st.inverse), t_count, self.top_k,
-                              self.hidden, None, _ptr(b["moe"]), _stream()))
-
-    def norm(self, l, t_count, mode=_lib.FFN_AUTO):
-        b = self.buffers(t_count, mode)
         x_in, x_out = self._act_in(b["acts"], l), self._act_out(b["acts"], l)
-        check(lib.pdx_residual_layernorm(_ptr(b["moe"]), _ptr(x_in), t_count, self.hidden, ctypes.c_float(LN_EPS),
-                                         _ptr(x_out), _stream()))
+        check(lib.pdx_combine_layernorm(_ptr(b["rows"]), _ptr(st.weights), _ptr(st.inverse), t_count, self.top_k,
+                                        self.hidden, _ptr(x_in), ctypes.c_float(LN_EPS), _ptr(x_out), _stream()))
 
     def _step_staged(self, t_count, mode):
         for l in range(self.num_layers):
             self.route_and_pack(l, t_count, mode)
             self.ffn(l, t_count, mode)
             self.combine(l, t_count, mode)
-            self.norm(l, t_count, mode)
 
     # -- public step --------------------------------------------------------------------
     def input(self, t_count, mode=_lib.FFN_AUTO):
@@ -194,16 +188,16 @@ class ResidentMoEStack:
 
     def stage_times_us(self, t_count, mode=_lib.FFN_AUTO, layers=8, repeats=3):
         """Mean device time per layer of each stage of the staged path, from CUDA
-        events on the current stream: route (logits + top-k), pack, FFN, combine,
-        and the next-layer norm of the synthetic stack (not part of the MoE path)."""
+        events on the current stream: route (logits + top-k), pack, FFN, combine
+        (with the stack's next-layer norm fused in)."""
         b = self.buffers(t_count, mode)
         st_ws, s = b["ws"], _stream()
-        names = ("route", "pack", "ffn", "combine", "norm")
+        names = ("route", "pack", "ffn", "combine")
         tot = dict.fromkeys(names, 0.0)
         n = 0
         for _ in range(repeats):
             for l in range(min(layers, self.num_layers)):
-                ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
                 st = b["stages"][l]
                 x = self._act_in(b["acts"], l)
                 ev[0].record()
@@ -220,8 +214,6 @@ class ResidentMoEStack:
                 ev[3].record()
                 self.combine(l, t_count, mode)
                 ev[4].record()
-                self.norm(l, t_count, mode)
-                ev[5].record()
                 torch.cuda.synchronize(self.device)
                 for i, name in enumerate(names):
                     tot[name] += ev[i].elapsed_time(ev[i + 1]) * 1e3

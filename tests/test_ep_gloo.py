@@ -162,18 +162,21 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("tokens,mode", [(5, "padded"), (13, "exact"), (40, None)])
-def test_expert_parallel_two_ranks_gloo(tokens, mode):
+@pytest.mark.parametrize("world,tokens,mode", [(2, 5, "padded"), (2, 13, "exact"), (2, 40, None),
+                                              (4, 6, "padded"), (4, 11, "exact")])
+def test_expert_parallel_gloo(world, tokens, mode):
+    """2 and 4 ranks (EL = 8 and 4 local experts; at 4 ranks min(k, EL) = k
+    bounds the padded capacity)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, tokens, mode, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, tokens, mode, q)) for r in range(world)]
     for p in procs:
         p.start()
-    results = dict(q.get(timeout=180) for _ in procs)
+    results = dict(q.get(timeout=240) for _ in procs)
     for p in procs:
         p.join(timeout=60)
-    assert results == {0: True, 1: True}, results
+    assert results == {r: True for r in range(world)}, results
 
 
 def test_capacity_bound():

@@ -46,3 +46,32 @@ def test_stack_activations_stay_finite():
     out = stack.output(t).float()
     assert torch.isfinite(out).all()
     assert 0.5 < out.pow(2).mean().sqrt().item() < 2.0
+
+
+@pytest.mark.parametrize("tokens,mode", [(1, 0), (33, 0), (300, 0), (300, 1)])
+def test_fused_combine_norm_bit_identical(tokens, mode):
+    """PDX_LAYER_OUT_NORM / pdx_combine_layernorm == combine (no residual) then
+    residual_layernorm, bit for bit."""
+    import ctypes
+    from pdscope_b200 import _lib
+    from pdscope_b200.runtime import ExpertSlab, ResidentMoELayer, combine, pack, residual_layernorm, route
+    gen = torch.Generator(device="cuda").manual_seed(tokens)
+    hidden, experts, inter = 512, 16, 256
+    slab = ExpertSlab.allocate(experts, hidden, inter, "cuda", generator=gen)
+    gate = (torch.randn(experts, hidden, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+    x = torch.randn(tokens, hidden, device="cuda", generator=gen).to(torch.bfloat16)
+    layer = ResidentMoELayer(gate, slab, top_k=4)
+    two_step = residual_layernorm(layer.forward(x, mode=mode).out, x)
+    fused = layer.forward(x, residual=x, mode=mode | _lib.LAYER_OUT_NORM).out
+    assert torch.equal(fused, two_step)
+    # the standalone entry point over packed expert rows
+    r = route(x, gate, 4, True)
+    p = pack(r.selected, r.weights, experts)
+    rows = torch.randn(tokens * 4, hidden, device="cuda", generator=gen).to(torch.bfloat16)
+    want = residual_layernorm(combine(rows, r.weights, p.inverse), x)
+    got = torch.empty_like(x)
+    _lib.check(_lib.lib.pdx_combine_layernorm(
+        ctypes.c_void_p(rows.data_ptr()), ctypes.c_void_p(r.weights.data_ptr()), ctypes.c_void_p(p.inverse.data_ptr()),
+        tokens, 4, hidden, ctypes.c_void_p(x.data_ptr()), ctypes.c_float(1e-5), ctypes.c_void_p(got.data_ptr()),
+        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    assert torch.equal(got, want)
