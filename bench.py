@@ -69,6 +69,8 @@ def parse():
     ap.add_argument("--offload-decode-steps", type=int, default=64)
     ap.add_argument("--offload-cap-gib", type=float, default=24.0)
     ap.add_argument("--offload-hot", type=int, default=16)
+    ap.add_argument("--offload-warm", type=int, default=30,
+                    help="static cache tier: the next experts per layer by the hot table's rank")
     return ap.parse_args()
 
 
@@ -483,12 +485,14 @@ def run_offload(args, dev, W, pk, L):
     with tempfile.TemporaryDirectory() as td:
         hot_path = Path(td) / "hot_offload.txt"
         write_hot_file(hot_path, zipf_hot_sets(gates, E))          # full Zipf ranking, hottest first
-        hot = load_hot_file(hot_path, args.offload_hot, L)
-    hot_bytes = sum(len(h) for h in hot) * EXPERT_BYTES
+        ranked = load_hot_file(hot_path, args.offload_hot + args.offload_warm, L)
+    hot = [r[:args.offload_hot] for r in ranked]
+    warm = [r[args.offload_hot:] for r in ranked]
+    hot_bytes = sum(len(h) + len(w) for h, w in zip(hot, warm)) * EXPERT_BYTES
     reserve = int(1.5 * 2 ** 30)   # activations, packing and FFN workspace at the largest prefill
     free = cap - torch.cuda.memory_allocated(dev) - hot_bytes - reserve
     slots = max(E, free // EXPERT_BYTES)
-    stack = OffloadMoEStack(gates, host, hot, hidden=H, inter=I, cache_slots=slots, top_k=k)
+    stack = OffloadMoEStack(gates, host, hot, hidden=H, inter=I, cache_slots=slots, top_k=k, warm=warm)
 
     prefills = [int(v) for v in args.offload_prefills.split(",") if v.strip()]
     n_dec = max(1, args.offload_decode_steps)
@@ -528,7 +532,8 @@ def run_offload(args, dev, W, pk, L):
                 decode_h2d_gb=dd["h2d_bytes"] / 1e9, decode_h2d_gbs=dd["h2d_bytes"] / 1e9 / td_,
                 decode_link_frac=dd["h2d_bytes"] / 1e9 / td_ / link_gbs,
                 decode_hot_hit_rate=dd["hot_hits"] / max(1, dd["expert_uses"]),
-                decode_ring_hit_rate=dd["cache_hits"] / max(1, nonhot_uses),
+                decode_warm_hit_rate=dd["warm_hits"] / max(1, dd["expert_uses"]),
+                decode_ring_hit_rate=dd["cache_hits"] / max(1, nonhot_uses - dd["warm_hits"]),
                 decode_prefetch_used=dd["prefetch_used"], decode_prefetch_copies=dd["prefetch_copies"],
                 decode_demand_copies=dd["demand_copies"], launches=dp["launches"] + dd["launches"]))
     clocks = sampler.summary()
@@ -538,10 +543,11 @@ def run_offload(args, dev, W, pk, L):
                 value=statistics.mean(dec_vals), unit="tok/s", n_gpus=1, steps=len(requests), warmup=W,
                 ms_per_step=1e3 / statistics.mean(dec_vals), higher_is_better=True, scaling="weak",
                 vs_baseline=None, dtype="bf16", data="synthetic",
-                config=dict(workload="config4 offload: 48 layers, hot %d/layer by Zipf rank, rest in pinned host "
-                                     "memory, prefills %s then %d decode steps each" % (args.offload_hot,
-                                                                                       prefills, n_dec),
-                            hbm_cap_gib=args.offload_cap_gib, hot_gib=hot_bytes / 2 ** 30,
+                config=dict(workload="config4 offload: 48 layers, hot %d/layer by Zipf rank (+%d/layer static "
+                                     "cache tier), rest in pinned host memory, prefills %s then %d decode steps "
+                                     "each" % (args.offload_hot, args.offload_warm, prefills, n_dec),
+                            hbm_cap_gib=args.offload_cap_gib, hot_per_layer=args.offload_hot,
+                            warm_per_layer=args.offload_warm, hot_and_warm_gib=hot_bytes / 2 ** 30,
                             cache_ring_slots=int(slots), cache_ring_gib=slots * EXPERT_BYTES / 2 ** 30,
                             host_gib=L * E * EXPERT_BYTES / 2 ** 30, zipf=dict(s=ZIPF_S, alpha=ZIPF_ALPHA),
                             value="mean decode tok/s over the requests"),

@@ -110,6 +110,7 @@ class OffloadStats:
     prefetch_wasted: int = 0       # prefetched slots evicted unread
     cache_hits: int = 0            # non-hot experts found in the ring (any origin)
     hot_hits: int = 0
+    warm_hits: int = 0             # static-tier experts (fixed cache slots)
     expert_uses: int = 0           # (layer, expert) pairs computed
     layers: int = 0
 
@@ -157,13 +158,16 @@ class OffloadMoEStack:
 
     ``gates``: list of [E, H] BF16 CUDA routers.  ``host_experts``: pinned CPU
     BF16 tensor [L, E, 3*I*H] (per expert gate_proj | up_proj | down_proj).
-    ``hot``: per layer, the expert ids kept resident.  ``cache_slots``: size of
-    the device cache ring (demand + prefetch + reuse).  ``chunk``: demand
-    experts per FFN launch.
+    ``hot``: per layer, the expert ids kept resident.  ``warm``: optional, per
+    layer, further experts given fixed cache slots (a static cache tier, the
+    reference's 'static' ExpertCache policy, filled from the next rows of the
+    hot table); they are copies of host experts, never evicted.
+    ``cache_slots``: size of the LRU cache ring (demand + prefetch + reuse).
+    ``chunk``: demand experts per FFN launch.
     """
 
     def __init__(self, gates, host_experts, hot, *, hidden, inter, cache_slots, top_k=8, normalize=True,
-                 prefetch=True, chunk=16):
+                 prefetch=True, chunk=16, warm=None):
         self.gates = list(gates)
         self.L = len(self.gates)
         self.E = self.gates[0].shape[0]
@@ -176,16 +180,23 @@ class OffloadMoEStack:
         self.per = 3 * inter * hidden
         self.dev = self.gates[0].device
         self.hot = [list(h) for h in hot]
+        self.warm = [list(w) for w in warm] if warm is not None else [[] for _ in range(self.L)]
         n_hot = sum(len(h) for h in self.hot)
-        self.pool = torch.empty((n_hot + cache_slots) * self.per, dtype=torch.bfloat16, device=self.dev)
-        self.hot_slot = {}
+        n_fixed = n_hot + sum(len(w) for w in self.warm)
+        self.pool = torch.empty((n_fixed + cache_slots) * self.per, dtype=torch.bfloat16, device=self.dev)
+        self.hot_slot, self.warm_keys = {}, set()
         s = 0
-        for l, hs in enumerate(self.hot):
-            for e in hs:
+        for l in range(self.L):
+            for e in self.hot[l] + self.warm[l]:
+                if (l, e) in self.hot_slot:
+                    raise ValueError(f"expert {e} of layer {l} listed twice in the hot/warm tiers")
                 self.hot_slot[(l, e)] = s
+                if e in self.warm[l]:
+                    self.warm_keys.add((l, e))
                 self.pool[s * self.per:(s + 1) * self.per].copy_(self.host[l, e])
                 s += 1
-        self.ring0 = n_hot
+        self.ring0 = n_fixed
+        n_hot = n_fixed
         self.ring = CacheRing(cache_slots)
         self.copy_stream = torch.cuda.Stream(device=self.dev)
         self.prefetch, self.chunk = prefetch, max(1, chunk)
@@ -303,7 +314,10 @@ class OffloadMoEStack:
             if hs is not None:
                 table[e] = hs
                 ready.append(e)
-                self.stats.hot_hits += 1
+                if (l, e) in self.warm_keys:
+                    self.stats.warm_hits += 1
+                else:
+                    self.stats.hot_hits += 1
                 continue
             idx = self.ring.lookup((l, e))
             if idx is not None:

@@ -54,7 +54,7 @@ def test_offload_ledger(stacks):
     d = {k: s[k] - before[k] for k in s}
     assert d["layers"] == 6 * L
     # every non-hot expert use is either a ring hit or a demand copy
-    assert d["expert_uses"] == d["hot_hits"] + d["cache_hits"] + d["demand_copies"]
+    assert d["expert_uses"] == d["hot_hits"] + d["warm_hits"] + d["cache_hits"] + d["demand_copies"]
     assert d["h2d_bytes"] == (d["demand_copies"] + d["prefetch_copies"]) * 3 * H * I * 2
     assert d["prefetch_copies"] > 0
 
@@ -65,3 +65,21 @@ def test_offload_rejects_pageable_host():
     with pytest.raises(ValueError, match="pinned"):
         OffloadMoEStack(g, torch.zeros(1, E, 3 * H * I, dtype=torch.bfloat16), [[0]], hidden=H, inter=I,
                         cache_slots=4, top_k=K)
+
+
+def test_offload_warm_tier_matches_resident(stacks):
+    """A static cache tier (fixed slots for the next experts by rank) changes
+    where weights come from, not the result."""
+    from pdscope_b200.offload import OffloadMoEStack, zipf_hot_sets
+    from pdscope_b200.stack import activations
+    res, off = stacks
+    ranked = zipf_hot_sets(res.gates, 7)
+    warm_stack = OffloadMoEStack(res.gates, off.host, [r[:3] for r in ranked], hidden=H, inter=I, cache_slots=12,
+                                 top_k=K, chunk=2, warm=[r[3:] for r in ranked])
+    for t_count in (1, 50):
+        x = activations(t_count, H, seed=700 + t_count, zipf=True)
+        want = _resident(res, x)
+        got = warm_stack.forward(x).clone()
+        torch.cuda.synchronize()
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16)), t_count
+    assert warm_stack.stats.warm_hits > 0
