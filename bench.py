@@ -71,6 +71,8 @@ def parse():
     ap.add_argument("--offload-hot", type=int, default=16)
     ap.add_argument("--offload-warm", type=int, default=30,
                     help="static cache tier: the next experts per layer by the hot table's rank")
+    ap.add_argument("--offload-python", action="store_true",
+                    help="per-layer orchestration in Python instead of the C++ engine (pdx_offload_*)")
     return ap.parse_args()
 
 
@@ -453,8 +455,8 @@ def run_offload(args, dev, W, pk, L):
     import tempfile
     import torch
     from pdscope_b200 import _lib
-    from pdscope_b200.offload import (OffloadMoEStack, PinnedHostBuffer, load_hot_file, measure_h2d_gbs,
-                                      write_hot_file, zipf_hot_sets)
+    from pdscope_b200.offload import (NativeOffloadMoEStack, OffloadMoEStack, PinnedHostBuffer, load_hot_file,
+                                      measure_h2d_gbs, write_hot_file, zipf_hot_sets)
     from pdscope_b200.stack import activations, ZIPF_ALPHA, ZIPF_S
 
     H, E, I, k = CFG["hidden"], CFG["experts"], CFG["inter"], CFG["top_k"]
@@ -492,9 +494,13 @@ def run_offload(args, dev, W, pk, L):
     reserve = int(1.5 * 2 ** 30)   # activations, packing and FFN workspace at the largest prefill
     free = cap - torch.cuda.memory_allocated(dev) - hot_bytes - reserve
     slots = max(E, free // EXPERT_BYTES)
-    stack = OffloadMoEStack(gates, host, hot, hidden=H, inter=I, cache_slots=slots, top_k=k, warm=warm)
-
     prefills = [int(v) for v in args.offload_prefills.split(",") if v.strip()]
+    if args.offload_python:
+        stack = OffloadMoEStack(gates, host, hot, hidden=H, inter=I, cache_slots=slots, top_k=k, warm=warm)
+    else:
+        stack = NativeOffloadMoEStack(gates, host, hot, hidden=H, inter=I, cache_slots=slots, top_k=k, warm=warm,
+                                      max_tokens=max(prefills + [16]))
+
     n_dec = max(1, args.offload_decode_steps)
     for w in range(W):   # warm: tensor maps, device attributes, allocator
         stack.forward(activations(16 if w == 0 else 1, H, device=dev, seed=900 + w, zipf=True))
@@ -546,6 +552,7 @@ def run_offload(args, dev, W, pk, L):
                 config=dict(workload="config4 offload: 48 layers, hot %d/layer by Zipf rank (+%d/layer static "
                                      "cache tier), rest in pinned host memory, prefills %s then %d decode steps "
                                      "each" % (args.offload_hot, args.offload_warm, prefills, n_dec),
+                            orchestration="python" if args.offload_python else "native (pdx_offload_*)",
                             hbm_cap_gib=args.offload_cap_gib, hot_per_layer=args.offload_hot,
                             warm_per_layer=args.offload_warm, hot_and_warm_gib=hot_bytes / 2 ** 30,
                             cache_ring_slots=int(slots), cache_ring_gib=slots * EXPERT_BYTES / 2 ** 30,
@@ -565,6 +572,8 @@ def run_offload(args, dev, W, pk, L):
                                                 note="whole model (attention + MoE) on A100 PCIe with kt CPU "
                                                      "experts; not like for like"))
     print(json.dumps(line), flush=True)
+    if hasattr(stack, "close"):
+        stack.close()
     del stack
     host_buf.close()
     return 0

@@ -214,6 +214,50 @@ int pdx_combine_layernorm(const void *y, const void *weights, const int32_t *inv
 #define PDX_LAYER_OUT_NORM 0x100
 #define PDX_LAYER_NORM_EPS 1e-5f
 
+/* ---- Offload mode: experts in pinned host memory, copy-engine pipeline ------
+ * The native host side of the reference's demand/prefetch pipeline
+ * (ExpertExecutor.load/finish_load, expertbench/executor.py:333-390; the
+ * demand loop and next-layer prefetch of PDScopeCudaRuntime.forward,
+ * expertbench/pdscope_runtime.py:284-399).  Expert (l, e) is the
+ * 3*inter*hidden BF16 slot [gate_proj | up_proj | down_proj] at
+ * host_experts + (l*experts + e) * 3*inter*hidden.  Per layer a fixed list of
+ * experts (the hot table's first hot_per_layer rows, then an optional static
+ * tier) keeps device slots; every other expert is copied on demand into an
+ * LRU ring of cache_slots slots; the experts the next layer's gate picks on
+ * the current activation are prefetched behind the demand copies.  The
+ * caller provides the device pool (pdx_offload_pool_bytes) and workspace
+ * (pdx_offload_workspace_bytes); create() allocates only host-side objects
+ * (a copy stream, events, pinned staging).  One handle per device; calls on
+ * one handle must be serialised. */
+typedef struct pdx_offload pdx_offload;
+typedef struct {
+    int32_t layers, experts, hidden, inter, top_k, normalize;
+    const void *const *gates;      /* [layers] device BF16 [experts, hidden] */
+    const void *host_experts;      /* pinned host BF16, layout above */
+    const int32_t *fixed_count;    /* [layers] experts with fixed slots per layer */
+    const int32_t *fixed_experts;  /* per layer, fixed_count[l] expert ids, concatenated */
+    int32_t hot_per_layer;         /* the first this-many fixed experts of a layer count as hot */
+    int32_t chunk;                 /* demand experts per FFN launch */
+    int32_t prefetch;              /* 1: prefetch the next layer's predicted experts */
+    int64_t cache_slots;           /* LRU ring slots */
+    int64_t max_tokens;            /* largest T of a forward call */
+} pdx_offload_config;
+typedef struct {
+    int64_t h2d_bytes, demand_copies, prefetch_copies, prefetch_used, prefetch_wasted;
+    int64_t cache_hits, hot_hits, warm_hits, expert_uses, layers;
+} pdx_offload_stats;
+size_t pdx_offload_pool_bytes(const pdx_offload_config *cfg);
+size_t pdx_offload_workspace_bytes(const pdx_offload_config *cfg);
+int pdx_offload_create(const pdx_offload_config *cfg, void *pool, void *workspace, size_t workspace_bytes,
+                       pdx_offload **out);
+/* out = residual + MoE_layer(x) (residual may be NULL), or with norm != 0
+ * layer_norm(MoE_layer(x) + residual).  Synchronises `stream` once (the
+ * routing counts), as the reference's grouping does. */
+int pdx_offload_forward_layer(pdx_offload *h, int32_t layer, const void *x, int64_t T, const void *residual,
+                              int32_t norm, void *out, pdx_stream_t stream);
+int pdx_offload_get_stats(const pdx_offload *h, pdx_offload_stats *out);
+void pdx_offload_destroy(pdx_offload *h);
+
 /* ---------------------------------------------------------------------------
  * Whole layer: route -> pack -> grouped FFN -> combine, all on `stream`, no
  * host synchronisation (PDScopeCudaRuntime.forward's GPU work,

@@ -42,6 +42,22 @@ class ExpertWeights(ctypes.Structure):
                 ("num_slots", c_i64), ("slot_of_expert", c_vp)]
 
 
+class OffloadConfig(ctypes.Structure):
+    """pdx_offload_config."""
+    _fields_ = [("layers", c_i32), ("experts", c_i32), ("hidden", c_i32), ("inter", c_i32), ("top_k", c_i32),
+                ("normalize", c_i32), ("gates", ctypes.POINTER(c_vp)), ("host_experts", c_vp),
+                ("fixed_count", ctypes.POINTER(c_i32)), ("fixed_experts", ctypes.POINTER(c_i32)),
+                ("hot_per_layer", c_i32), ("chunk", c_i32), ("prefetch", c_i32), ("cache_slots", c_i64),
+                ("max_tokens", c_i64)]
+
+
+class OffloadStats(ctypes.Structure):
+    """pdx_offload_stats."""
+    _fields_ = [(name, c_i64) for name in ("h2d_bytes", "demand_copies", "prefetch_copies", "prefetch_used",
+                                           "prefetch_wasted", "cache_hits", "hot_hits", "warm_hits",
+                                           "expert_uses", "layers")]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "pdx_last_error": (ctypes.c_char_p, []),
@@ -78,6 +94,12 @@ SIGNATURES = {
     "pdx_ep_ungroup": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "pdx_ep_combine": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i32, c_i64, c_vp, c_vp, c_vp]),
     "pdx_device_error": (ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_uint32)]),
+    "pdx_offload_pool_bytes": (c_sz, [ctypes.POINTER(OffloadConfig)]),
+    "pdx_offload_workspace_bytes": (c_sz, [ctypes.POINTER(OffloadConfig)]),
+    "pdx_offload_create": (ctypes.c_int, [ctypes.POINTER(OffloadConfig), c_vp, c_vp, c_sz, ctypes.POINTER(c_vp)]),
+    "pdx_offload_forward_layer": (ctypes.c_int, [c_vp, c_i32, c_vp, c_i64, c_vp, c_i32, c_vp, c_vp]),
+    "pdx_offload_get_stats": (ctypes.c_int, [c_vp, ctypes.POINTER(OffloadStats)]),
+    "pdx_offload_destroy": (None, [c_vp]),
 }
 
 

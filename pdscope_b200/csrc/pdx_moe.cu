@@ -938,3 +938,6 @@ int pdx_device_error(pdx_stream_t stream, uint32_t* code_out) {
 
 // Allocation-free packing (fixed device scratch); uses the helpers above.
 #include "pack_static.cu"
+
+// native host side of offload mode (calls the entry points above)
+#include "offload_host.cu"

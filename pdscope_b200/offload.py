@@ -338,8 +338,10 @@ class OffloadMoEStack:
         chunks = []
         for c0 in range(0, len(demand), self.chunk):
             part = demand[c0:c0 + self.chunk]
-            idxs = [self._copy_in((l, e), pinned, prefetched=False) for e in part]
-            pinned.update(idxs)
+            idxs = []
+            for e in part:   # each slot joins the live set at once: a later copy cannot take it
+                idxs.append(self._copy_in((l, e), pinned, prefetched=False))
+                pinned.add(idxs[-1])
             for e, i in zip(part, idxs):
                 table[e] = self.ring0 + i
             chunks.append((part, self._mark_ready(idxs)))
@@ -395,6 +397,86 @@ class OffloadMoEStack:
             self.forward_layer(l, h, out, residual=h, norm=True)
             h = out
         return h
+
+
+class NativeOffloadMoEStack:
+    """OffloadMoEStack with the per-layer orchestration in C++
+    (``pdx_offload_*``): same placement policy, copies and launches, no Python
+    on the per-layer path.  Arguments as OffloadMoEStack, plus ``max_tokens``
+    (the largest batch a call may carry; sizes the device workspace)."""
+
+    def __init__(self, gates, host_experts, hot, *, hidden, inter, cache_slots, top_k=8, normalize=True,
+                 prefetch=True, chunk=16, warm=None, max_tokens=4096):
+        self.gates = list(gates)
+        self.L, self.E = len(self.gates), self.gates[0].shape[0]
+        self.H, self.I, self.k = hidden, inter, top_k
+        if host_experts.device.type != "cpu" or not host_experts.is_pinned():
+            raise ValueError("host experts must be a pinned CPU tensor (copy-engine transfers)")
+        if host_experts.dtype != torch.bfloat16 or tuple(host_experts.shape) != (self.L, self.E, 3 * inter * hidden):
+            raise ValueError("host experts must be BF16 [layers, experts, 3*inter*hidden]")
+        self.host = host_experts
+        self.dev = self.gates[0].device
+        warm = warm if warm is not None else [[] for _ in range(self.L)]
+        fixed = [list(h) + list(w) for h, w in zip(hot, warm)]
+        hot_n = {len(h) for h in hot}
+        if len(hot_n) > 1:
+            raise ValueError("the native engine needs the same hot-set size in every layer")
+        self._gate_ptrs = (ctypes.c_void_p * self.L)(*[g.data_ptr() for g in self.gates])
+        self._fixed_count = (ctypes.c_int32 * self.L)(*[len(f) for f in fixed])
+        flat = [e for f in fixed for e in f]
+        self._fixed = (ctypes.c_int32 * max(1, len(flat)))(*flat)
+        self.cfg = _lib.OffloadConfig(layers=self.L, experts=self.E, hidden=hidden, inter=inter, top_k=top_k,
+                                      normalize=int(normalize), gates=self._gate_ptrs,
+                                      host_experts=host_experts.data_ptr(), fixed_count=self._fixed_count,
+                                      fixed_experts=self._fixed, hot_per_layer=hot_n.pop() if hot_n else 0,
+                                      chunk=chunk, prefetch=int(prefetch), cache_slots=cache_slots,
+                                      max_tokens=max_tokens)
+        pool_bytes = lib.pdx_offload_pool_bytes(ctypes.byref(self.cfg))
+        ws_bytes = lib.pdx_offload_workspace_bytes(ctypes.byref(self.cfg))
+        if not pool_bytes or not ws_bytes:
+            check(_lib.PDX_ERR_INVALID)
+        self.pool = torch.empty(pool_bytes, dtype=torch.uint8, device=self.dev)
+        self.ws = torch.empty(ws_bytes, dtype=torch.uint8, device=self.dev)
+        h = ctypes.c_void_p()
+        check(lib.pdx_offload_create(ctypes.byref(self.cfg), _ptr(self.pool), _ptr(self.ws), ws_bytes,
+                                     ctypes.byref(h)))
+        self._h = h
+        self._acts = {}
+
+    @property
+    def stats(self):
+        st = _lib.OffloadStats()
+        check(lib.pdx_offload_get_stats(self._h, ctypes.byref(st)))
+        return OffloadStats(**{name: getattr(st, name) for name, _ in _lib.OffloadStats._fields_})
+
+    def forward_layer(self, l, x, out, residual=None, norm=False):
+        check(lib.pdx_offload_forward_layer(self._h, l, _ptr(x), x.shape[0], _ptr(residual), int(norm), _ptr(out),
+                                            _stream()))
+        return out
+
+    def forward(self, x):
+        """Every layer on ``x``; layer l+1's input is layer_norm(MoE_l(x_l) + x_l)."""
+        t = x.shape[0]
+        acts = self._acts.get(t)
+        if acts is None:
+            acts = self._acts[t] = [torch.empty_like(x) for _ in range(2)]
+        h = x
+        for l in range(self.L):
+            self.forward_layer(l, h, acts[l % 2], residual=h, norm=True)
+            h = acts[l % 2]
+        return h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            torch.cuda.synchronize(self.dev)
+            lib.pdx_offload_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class PinnedHostBuffer:

@@ -83,3 +83,42 @@ def test_offload_warm_tier_matches_resident(stacks):
         torch.cuda.synchronize()
         assert torch.equal(got.view(torch.int16), want.view(torch.int16)), t_count
     assert warm_stack.stats.warm_hits > 0
+
+
+def _fresh(res, native, **kw):
+    from pdscope_b200.offload import NativeOffloadMoEStack, OffloadMoEStack, zipf_hot_sets
+    host = torch.stack([s.storage.view(E, -1).cpu() for s in res.slabs]).pin_memory()
+    ranked = zipf_hot_sets(res.gates, 6)
+    cls = NativeOffloadMoEStack if native else OffloadMoEStack
+    extra = dict(max_tokens=128) if native else {}
+    return cls(res.gates, host, [r[:4] for r in ranked], hidden=H, inter=I, cache_slots=14, top_k=K, chunk=3,
+               warm=[r[4:] for r in ranked], **extra, **kw)
+
+
+def test_native_engine_matches_python_and_resident(stacks):
+    """The C++ host engine: same outputs as the resident stack, and the same
+    placement decisions (ledger counters) as the Python orchestration."""
+    from pdscope_b200.stack import activations
+    res, _ = stacks
+    nat, py = _fresh(res, True), _fresh(res, False)
+    for step, t_count in enumerate((1, 7, 96, 1, 1, 33)):
+        x = activations(t_count, H, seed=1200 + step, zipf=True)
+        want = _resident(res, x)
+        a = nat.forward(x).clone()
+        b = py.forward(x).clone()
+        torch.cuda.synchronize()
+        assert torch.equal(a.view(torch.int16), want.view(torch.int16)), (step, t_count)
+        assert torch.equal(b.view(torch.int16), want.view(torch.int16)), (step, t_count)
+    assert nat.stats.as_dict() == py.stats.as_dict()
+    nat.close()
+
+
+def test_native_engine_rejects_bad_calls(stacks):
+    res, _ = stacks
+    nat = _fresh(res, True)
+    x = torch.zeros(200, H, dtype=torch.bfloat16, device="cuda")   # above max_tokens
+    with pytest.raises(ValueError):
+        nat.forward_layer(0, x, torch.empty_like(x))
+    with pytest.raises(ValueError):
+        nat.forward_layer(L, x[:4], torch.empty_like(x[:4]))        # layer out of range
+    nat.close()
