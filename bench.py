@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU baseline sample")
     ap.add_argument("--cpu-threads", type=int, default=0, help="0 = all usable cores")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--ep-transport", choices=("p2p", "nccl"), default="p2p",
+                    help="N>1 decode exchange: NVLink peer stores + flags (p2p) or NCCL all-to-all")
     ap.add_argument("--ep-shape", choices=("30b", "235b"), default="30b",
                     help="N>1 expert-parallel workload: 30b (config 2 per GPU) or 235b (config 5)")
     ap.add_argument("--offload", action="store_true",
@@ -591,7 +593,7 @@ def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
     split over the ranks."""
     import torch
     from pdscope_b200 import _lib
-    from pdscope_b200.expert_parallel import ExpertParallelStack, TorchDistExchange
+    from pdscope_b200.expert_parallel import ExpertParallelStack, PeerExchange, TorchDistExchange
     from pdscope_b200.runtime import ExpertSlab
     from pdscope_b200.stack import activations, prefill_lengths, ZIPF_ALPHA, ZIPF_S
 
@@ -615,7 +617,16 @@ def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
             g[:, 0] = -ZIPF_ALPHA * ZIPF_S * torch.log(ranks)
         gates.append(g.to(torch.bfloat16))
     slabs = [ExpertSlab.allocate(el, H, I, dev, generator=g_w) for _ in range(L)]
-    stack = ExpertParallelStack(gates, slabs, rank=rank, world=world, exchange=TorchDistExchange(), top_k=k)
+    if big:
+        decode_sizes = [max(1, 256 // world)]
+    else:
+        decode_sizes = sorted(set(int(v) for v in args.decode_batches.split(",") if v.strip()) | {args.decode_batch})
+    peer = None
+    if args.ep_transport == "p2p":
+        peer = PeerExchange(L, max(decode_sizes), world=world, rank=rank, local_experts=el, hidden=H, top_k=k,
+                            device=dev)
+    stack = ExpertParallelStack(gates, slabs, rank=rank, world=world, exchange=TorchDistExchange(), top_k=k,
+                                peer=peer)
     torch.cuda.synchronize(dev)
 
     def max_over_ranks(v):
@@ -645,12 +656,8 @@ def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
         return max_over_ranks(e0.elapsed_time(e1))
 
     decode = {}
-    if big:
-        headline_t = max(1, 256 // world)
-        batches = [headline_t]
-    else:
-        headline_t = args.decode_batch
-        batches = sorted(set(int(v) for v in args.decode_batches.split(",") if v.strip()) | {headline_t})
+    headline_t = max(1, 256 // world) if big else args.decode_batch
+    batches = decode_sizes
     clocks = None
     for t_count in batches:
         x, _ = stack.io(t_count)
@@ -708,12 +715,12 @@ def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
         if big:
             workload = (f"config5 decode batch {headline_t * world} in all ({headline_t} per GPU): {L}-layer "
                         f"Qwen3-235B-A22B-shape MoE stack (H={H}, I={I}), expert parallel {el} experts/GPU, "
-                        f"NCCL all-to-all dispatch/combine, one CUDA graph per step")
+                        f"dispatch/combine exchange over NVLink, one CUDA graph per step")
             scaling = "strong"
         else:
             workload = (f"config2 decode batch {headline_t} per GPU: 48-layer Qwen3-30B-A3B-shape "
-                        f"MoE stack, expert parallel {el} experts/GPU, NCCL all-to-all "
-                        f"dispatch/combine, one CUDA graph per step")
+                        f"MoE stack, expert parallel {el} experts/GPU, dispatch/combine exchange over NVLink, "
+                        f"one CUDA graph per step")
             scaling = "weak"
         line = dict(metric=METRIC, value=d["tok_s"], unit="tok/s", n_gpus=world, steps=K, warmup=W,
                     ms_per_step=d["ms_per_step"], higher_is_better=True, scaling=scaling, vs_baseline=None,
@@ -734,7 +741,12 @@ def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
                              ms_per_step=e2e_ms / K),
                     clocks=clocks, gpu_launches=d["launches_per_step"] * K,
                     decode={str(t): r for t, r in decode.items()}, prefill=prefill)
+        line["config"]["exchange"] = ("NVLink peer stores + flags (pdx_ep_*_p2p)" if peer is not None
+                                      else "NCCL all-to-all")
         print(json.dumps(line), flush=True)
+    stack.release_graphs()
+    if peer is not None:
+        peer.close()
     dist.destroy_process_group()
     return 0
 

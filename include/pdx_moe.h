@@ -320,6 +320,40 @@ int pdx_ep_combine(const void *y, int64_t y_rows, const void *weights, const int
                    int64_t T, int32_t top_k, int64_t H, const void *residual, void *out,
                    pdx_stream_t stream);
 
+/* ---- Expert-parallel exchange over NVLink peer memory ----------------------
+ * The padded (decode) exchange without a collective library: each rank's
+ * exchange region is mapped into the other ranks (CUDA IPC).  Per layer and
+ * rank the region holds recv [R][C][H] and back [R][C][H] BF16 blocks, cnt
+ * [R][EL] int32 and rflag/bflag [R] uint64; a pdx_p2p_layer gives, per rank
+ * (index = rank), the addresses of that rank's recv/back/cnt/rflag/bflag of
+ * this layer as mapped in the calling process, plus this rank's step counter
+ * and two ticket words (zero-initialised).  Sequence per layer:
+ *   pdx_ep_dispatch_p2p -> pdx_ep_layout_p2p -> pdx_ep_regroup (local recv) ->
+ *   pdx_moe_ffn_grouped -> pdx_ep_return_p2p -> pdx_ep_wait_back ->
+ *   pdx_ep_combine / pdx_combine_layernorm (local back, y_rows = R*C).
+ * The two wait steps spin (bounded, 2 s) on flags written by the other ranks:
+ * every rank must run the same sequence, one rank per GPU. */
+typedef struct {
+    const uint64_t *recv, *back, *cnt, *rflag, *bflag; /* device arrays [R] of addresses */
+    uint64_t *step;                                     /* device, this rank */
+    uint32_t *ticket;                                   /* device [2], this rank */
+} pdx_p2p_layer;
+int pdx_p2p_alloc(size_t bytes, void **ptr_out);   /* cudaMalloc + zero fill (exchange regions only) */
+int pdx_p2p_free(void *ptr);
+int pdx_ipc_handle(void *ptr, void *handle_out);   /* 64-byte cudaIpcMemHandle_t */
+int pdx_ipc_open(const void *handle, void **ptr_out);
+int pdx_ipc_close(void *ptr);
+int pdx_ep_dispatch_p2p(const void *x, const int32_t *tokens, const int32_t *positions, const int32_t *offsets,
+                        int64_t T, int32_t top_k, int64_t H, int64_t E, int32_t ranks, int32_t rank, int64_t capacity,
+                        const pdx_p2p_layer *layer, int32_t *inv_ep, pdx_stream_t stream);
+int pdx_ep_layout_p2p(int32_t ranks, int32_t rank, int64_t local_experts, int64_t capacity, int64_t rows_cap,
+                      const pdx_p2p_layer *layer, int32_t *offsets_l, int32_t *active_l, int32_t *perm,
+                      pdx_stream_t stream);
+int pdx_ep_return_p2p(const void *grouped, const int32_t *perm, const int32_t *offsets_l, int64_t local_experts,
+                      int64_t rows_cap, int64_t H, int32_t ranks, int32_t rank, int64_t capacity,
+                      const pdx_p2p_layer *layer, pdx_stream_t stream);
+int pdx_ep_wait_back(int32_t ranks, int32_t rank, const pdx_p2p_layer *layer, pdx_stream_t stream);
+
 /* Synchronise `stream`, then read and clear this device's error word.
  * *code_out receives a PDX_DEVERR_* value; returns PDX_ERR_DEVICE if nonzero. */
 int pdx_device_error(pdx_stream_t stream, uint32_t *code_out);

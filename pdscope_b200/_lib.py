@@ -58,6 +58,12 @@ class OffloadStats(ctypes.Structure):
                                            "expert_uses", "layers")]
 
 
+class P2PLayer(ctypes.Structure):
+    """pdx_p2p_layer."""
+    _fields_ = [("recv", c_vp), ("back", c_vp), ("cnt", c_vp), ("rflag", c_vp), ("bflag", c_vp), ("step", c_vp),
+                ("ticket", c_vp)]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "pdx_last_error": (ctypes.c_char_p, []),
@@ -94,6 +100,18 @@ SIGNATURES = {
     "pdx_ep_ungroup": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "pdx_ep_combine": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i32, c_i64, c_vp, c_vp, c_vp]),
     "pdx_device_error": (ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_uint32)]),
+    "pdx_p2p_alloc": (ctypes.c_int, [c_sz, ctypes.POINTER(c_vp)]),
+    "pdx_p2p_free": (ctypes.c_int, [c_vp]),
+    "pdx_ipc_handle": (ctypes.c_int, [c_vp, c_vp]),
+    "pdx_ipc_open": (ctypes.c_int, [c_vp, ctypes.POINTER(c_vp)]),
+    "pdx_ipc_close": (ctypes.c_int, [c_vp]),
+    "pdx_ep_dispatch_p2p": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i64, c_i64, c_i32, c_i32, c_i64,
+                                           ctypes.POINTER(P2PLayer), c_vp, c_vp]),
+    "pdx_ep_layout_p2p": (ctypes.c_int, [c_i32, c_i32, c_i64, c_i64, c_i64, ctypes.POINTER(P2PLayer), c_vp, c_vp,
+                                         c_vp, c_vp]),
+    "pdx_ep_return_p2p": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_i32, c_i64,
+                                         ctypes.POINTER(P2PLayer), c_vp]),
+    "pdx_ep_wait_back": (ctypes.c_int, [c_i32, c_i32, ctypes.POINTER(P2PLayer), c_vp]),
     "pdx_offload_pool_bytes": (c_sz, [ctypes.POINTER(OffloadConfig)]),
     "pdx_offload_workspace_bytes": (c_sz, [ctypes.POINTER(OffloadConfig)]),
     "pdx_offload_create": (ctypes.c_int, [ctypes.POINTER(OffloadConfig), c_vp, c_vp, c_sz, ctypes.POINTER(c_vp)]),

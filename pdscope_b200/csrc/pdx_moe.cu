@@ -20,6 +20,7 @@
 #include "ffn_stream.cu"
 #include "pack.cu"
 #include "ep.cu"
+#include "ep_p2p.cu"
 #include "route.cu"
 
 namespace pdx {
@@ -918,6 +919,115 @@ int pdx_ep_combine(const void* y, int64_t y_rows, const void* weights, const int
                            static_cast<int>(T), static_cast<int>(top_k), static_cast<int>(H),
                            static_cast<int>(y_rows), static_cast<const uint16_t*>(residual),
                            static_cast<uint16_t*>(out)));
+    return ok();
+}
+
+int pdx_p2p_alloc(size_t bytes, void** ptr_out) {
+    if (!ptr_out || bytes == 0) return fail(PDX_ERR_INVALID, "invalid exchange allocation");
+    *ptr_out = nullptr;
+    PDX_CUDA_TRY(cudaMalloc(ptr_out, bytes));
+    PDX_CUDA_TRY(cudaMemset(*ptr_out, 0, bytes));
+    return ok();
+}
+
+int pdx_p2p_free(void* ptr) {
+    if (ptr) PDX_CUDA_TRY(cudaFree(ptr));
+    return ok();
+}
+
+int pdx_ipc_handle(void* ptr, void* handle_out) {
+    if (!ptr || !handle_out) return fail(PDX_ERR_INVALID, "null IPC argument");
+    cudaIpcMemHandle_t h;
+    PDX_CUDA_TRY(cudaIpcGetMemHandle(&h, ptr));
+    std::memcpy(handle_out, &h, sizeof(h));
+    return ok();
+}
+
+int pdx_ipc_open(const void* handle, void** ptr_out) {
+    if (!handle || !ptr_out) return fail(PDX_ERR_INVALID, "null IPC argument");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    PDX_CUDA_TRY(cudaIpcOpenMemHandle(ptr_out, h, cudaIpcMemLazyEnablePeerAccess));
+    return ok();
+}
+
+int pdx_ipc_close(void* ptr) {
+    if (ptr) PDX_CUDA_TRY(cudaIpcCloseMemHandle(ptr));
+    return ok();
+}
+
+static pdx::P2PLayer to_p2p(const pdx_p2p_layer* l) {
+    pdx::P2PLayer o;
+    o.recv = reinterpret_cast<const unsigned long long*>(l->recv);
+    o.back = reinterpret_cast<const unsigned long long*>(l->back);
+    o.cnt = reinterpret_cast<const unsigned long long*>(l->cnt);
+    o.rflag = reinterpret_cast<const unsigned long long*>(l->rflag);
+    o.bflag = reinterpret_cast<const unsigned long long*>(l->bflag);
+    o.step = reinterpret_cast<unsigned long long*>(l->step);
+    o.ticket = l->ticket;
+    return o;
+}
+
+static int check_p2p(const pdx_p2p_layer* l, int32_t ranks, int32_t rank) {
+    if (!l || !l->recv || !l->back || !l->cnt || !l->rflag || !l->bflag || !l->step || !l->ticket)
+        return fail(PDX_ERR_INVALID, "incomplete exchange layer");
+    if (ranks < 1 || ranks > 32 || rank < 0 || rank >= ranks) return fail(PDX_ERR_INVALID, "invalid rank");
+    return PDX_OK;
+}
+
+int pdx_ep_dispatch_p2p(const void* x, const int32_t* tokens, const int32_t* positions, const int32_t* offsets,
+                        int64_t T, int32_t top_k, int64_t H, int64_t E, int32_t ranks, int32_t rank, int64_t capacity,
+                        const pdx_p2p_layer* layer, int32_t* inv_ep, pdx_stream_t stream) {
+    int st = check_p2p(layer, ranks, rank);
+    if (st) return st;
+    if (!x || !tokens || !positions || !offsets || !inv_ep) return fail(PDX_ERR_INVALID, "null EP argument");
+    if (T < 1 || top_k < 1 || E % ranks || capacity < 1 || E / ranks > kEpMaxExperts / ranks)
+        return fail(PDX_ERR_INVALID, "invalid expert-parallel shape");
+    if (H < 8 || H % 8) return fail(PDX_ERR_UNSUPPORTED, "H must be a positive multiple of 8");
+    pdx::k_ep_dispatch_p2p<<<static_cast<unsigned>(T * top_k), 256, 0, stream>>>(
+        static_cast<const uint16_t*>(x), tokens, positions, offsets, static_cast<int>(T * top_k),
+        static_cast<int>(H), static_cast<int>(E), static_cast<int>(E / ranks), ranks, rank, capacity,
+        to_p2p(layer), inv_ep);
+    PDX_LAUNCHED();
+    return ok();
+}
+
+int pdx_ep_layout_p2p(int32_t ranks, int32_t rank, int64_t local_experts, int64_t capacity, int64_t rows_cap,
+                      const pdx_p2p_layer* layer, int32_t* offsets_l, int32_t* active_l, int32_t* perm,
+                      pdx_stream_t stream) {
+    int st = check_p2p(layer, ranks, rank);
+    if (st) return st;
+    if (!offsets_l || !active_l || !perm) return fail(PDX_ERR_INVALID, "null EP layout argument");
+    if (local_experts < 1 || ranks * local_experts > pdx::kEpMaxExperts || capacity < 1 || rows_cap < 1)
+        return fail(PDX_ERR_UNSUPPORTED, "expert-parallel layout supports ranks*local_experts <= %d",
+                    pdx::kEpMaxExperts);
+    pdx::k_ep_layout_p2p<<<1, 1024, 0, stream>>>(ranks, static_cast<int>(local_experts), capacity,
+                                                 static_cast<int>(rows_cap), to_p2p(layer), rank, offsets_l,
+                                                 active_l, perm);
+    PDX_LAUNCHED();
+    return ok();
+}
+
+int pdx_ep_return_p2p(const void* grouped, const int32_t* perm, const int32_t* offsets_l, int64_t local_experts,
+                      int64_t rows_cap, int64_t H, int32_t ranks, int32_t rank, int64_t capacity,
+                      const pdx_p2p_layer* layer, pdx_stream_t stream) {
+    int st = check_p2p(layer, ranks, rank);
+    if (st) return st;
+    if (!grouped || !perm || !offsets_l || rows_cap < 1 || capacity < 1)
+        return fail(PDX_ERR_INVALID, "invalid EP return argument");
+    if (H < 8 || H % 8) return fail(PDX_ERR_UNSUPPORTED, "H must be a positive multiple of 8");
+    pdx::k_ep_return_p2p<<<static_cast<unsigned>(rows_cap), 256, 0, stream>>>(
+        static_cast<const uint16_t*>(grouped), perm, offsets_l, static_cast<int>(local_experts),
+        static_cast<int>(rows_cap), static_cast<int>(H), ranks, rank, capacity, to_p2p(layer));
+    PDX_LAUNCHED();
+    return ok();
+}
+
+int pdx_ep_wait_back(int32_t ranks, int32_t rank, const pdx_p2p_layer* layer, pdx_stream_t stream) {
+    int st = check_p2p(layer, ranks, rank);
+    if (st) return st;
+    pdx::k_ep_wait_back<<<1, 32, 0, stream>>>(ranks, rank, to_p2p(layer));
+    PDX_LAUNCHED();
     return ok();
 }
 

@@ -210,6 +210,40 @@ class ExpertParallelMoE:
     def finish(self, d, back, residual=None):
         return self.ops.combine(back, back.shape[0], d.weights, d.inverse, residual)
 
+    # ---- padded exchange over NVLink peer memory ----------------------------------------
+    def forward_p2p(self, x, peer, layer, residual=None):
+        """The padded layer with the exchange done by peer stores and flags
+        (pdx_ep_dispatch_p2p ... pdx_ep_wait_back) instead of all-to-alls."""
+        t_count, hidden = x.shape
+        cap = self.capacity(t_count)
+        if cap > peer.cap_max:
+            raise ValueError("batch larger than the peer exchange was sized for")
+        R, EL, k, dev = self.world, self.local, self.top_k, x.device
+        sel, w = self.ops.route(x, self.gate, k, self.normalize)
+        p = self.ops.pack(sel, w, self.experts)
+        lay = ctypes.byref(peer.structs[layer])
+        inv = torch.empty(t_count * k, dtype=torch.int32, device=dev)
+        s = _stream()
+        check(lib.pdx_ep_dispatch_p2p(_ptr(x), _ptr(p.tokens), _ptr(p.positions), _ptr(p.offsets), t_count, k, hidden,
+                                      self.experts, R, self.rank, cap, lay, _ptr(inv), s))
+        rows_cap = R * cap
+        ly = Layout(offsets=torch.empty(EL + 1, dtype=torch.int32, device=dev),
+                    active=torch.empty(EL + 1, dtype=torch.int32, device=dev),
+                    perm=torch.empty(rows_cap, dtype=torch.int32, device=dev), experts=EL)
+        check(lib.pdx_ep_layout_p2p(R, self.rank, EL, cap, rows_cap, lay, _ptr(ly.offsets), _ptr(ly.active),
+                                    _ptr(ly.perm), s))
+        grouped = torch.empty((rows_cap, hidden), dtype=x.dtype, device=dev)
+        check(lib.pdx_ep_regroup(ctypes.c_void_p(peer.local(layer, "recv")), _ptr(ly.perm), _ptr(ly.offsets), EL,
+                                 rows_cap, hidden, _ptr(grouped), s))
+        y = self.ops.ffn(grouped, ly, self.slab, _lib.FFN_GEMV)
+        check(lib.pdx_ep_return_p2p(_ptr(y), _ptr(ly.perm), _ptr(ly.offsets), EL, rows_cap, hidden, R, self.rank, cap,
+                                    lay, s))
+        check(lib.pdx_ep_wait_back(R, self.rank, lay, s))
+        out = torch.empty((t_count, hidden), dtype=torch.bfloat16, device=dev)
+        check(lib.pdx_ep_combine(ctypes.c_void_p(peer.local(layer, "back")), rows_cap, _ptr(w), _ptr(inv), t_count,
+                                 k, hidden, _ptr(residual), _ptr(out), s))
+        return out
+
     # ---- the whole layer over the exchange -------------------------------------------
     def forward(self, x, residual=None, mode=None):
         ex = self.exchange
@@ -235,6 +269,75 @@ def local_slab_of(full_slab, rank, world):
     return ExpertSlab(full_slab.storage[rank * el * per:(rank + 1) * el * per], full_slab.hidden, full_slab.inter)
 
 
+class PeerExchange:
+    """Exchange regions of every layer mapped into every rank of the group
+    (CUDA IPC), for the padded exchange over NVLink peer memory
+    (pdx_ep_*_p2p).  Per layer: recv / back blocks [R][C][H] BF16 for up to
+    ``max_tokens`` tokens per rank, per-source expert counts and flags; a local
+    step counter and two ticket words per layer.  Collective construction and
+    ``close`` (every rank calls both)."""
+
+    def __init__(self, layers, max_tokens, *, world, rank, local_experts, hidden, top_k, device, group=None):
+        import torch.distributed as dist
+        self.L, self.R, self.rank, self.EL, self.H = layers, world, rank, local_experts, hidden
+        self.cap_max = max_tokens * min(top_k, local_experts)
+        a = lambda n: (n + 255) // 256 * 256
+        blk = a(self.R * self.cap_max * hidden * 2)
+        self.off = dict(recv=0, back=blk, cnt=2 * blk, rflag=2 * blk + a(self.R * self.EL * 4),
+                        bflag=2 * blk + a(self.R * self.EL * 4) + a(self.R * 8))
+        self.per_layer = self.off["bflag"] + a(self.R * 8)
+        ptr = ctypes.c_void_p()
+        check(lib.pdx_p2p_alloc(self.per_layer * layers, ctypes.byref(ptr)))
+        self.base = ptr.value
+        handle = ctypes.create_string_buffer(64)
+        check(lib.pdx_ipc_handle(self.base, handle))
+        handles = [None] * world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self.peer_base, self._opened = [], []
+        for r in range(world):
+            if r == rank:
+                self.peer_base.append(self.base)
+                continue
+            q = ctypes.c_void_p()
+            check(lib.pdx_ipc_open(ctypes.create_string_buffer(handles[r], 64), ctypes.byref(q)))
+            self.peer_base.append(q.value)
+            self._opened.append(q.value)
+        tbl = torch.empty((layers, 5, world), dtype=torch.int64)
+        for l in range(layers):
+            for i, key in enumerate(("recv", "back", "cnt", "rflag", "bflag")):
+                for r in range(world):
+                    tbl[l, i, r] = self.peer_base[r] + l * self.per_layer + self.off[key]
+        self.tbl = tbl.to(device)
+        self.step = torch.zeros(layers, dtype=torch.int64, device=device)
+        self.ticket = torch.zeros((layers, 2), dtype=torch.int32, device=device)
+        self.structs = []
+        for l in range(layers):
+            t = self.tbl[l]
+            self.structs.append(_lib.P2PLayer(recv=t[0].data_ptr(), back=t[1].data_ptr(), cnt=t[2].data_ptr(),
+                                              rflag=t[3].data_ptr(), bflag=t[4].data_ptr(),
+                                              step=self.step[l].data_ptr(), ticket=self.ticket[l].data_ptr()))
+        self.group = group
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)
+
+    def local(self, layer, key):
+        return self.base + layer * self.per_layer + self.off[key]
+
+    def close(self):
+        """Unmap the peers' regions and free this rank's (collective)."""
+        import torch.distributed as dist
+        if self.base is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for q in self._opened:
+            lib.pdx_ipc_close(q)
+        self._opened = []
+        dist.barrier(group=self.group)
+        lib.pdx_p2p_free(self.base)
+        self.base = None
+
+
 class ExpertParallelStack:
     """``layers`` expert-parallel MoE layers driven as one step on every rank.
 
@@ -244,11 +347,12 @@ class ExpertParallelStack:
     use the same batch size).
     """
 
-    def __init__(self, gates, local_slabs, *, rank, world, exchange, top_k=8):
+    def __init__(self, gates, local_slabs, *, rank, world, exchange, top_k=8, peer=None):
         self.layers = [ExpertParallelMoE(g, s, rank=rank, world=world, exchange=exchange, top_k=top_k)
                        for g, s in zip(gates, local_slabs)]
         self.hidden = gates[0].shape[1]
         self.device = gates[0].device
+        self.peer = peer          # PeerExchange: padded layers exchange over peer memory
         self._graphs, self._io = {}, {}
 
     def io(self, t_count):
@@ -260,8 +364,11 @@ class ExpertParallelStack:
     def _run(self, t_count, mode):
         x, out = self.io(t_count)
         h = x
-        for layer in self.layers:
-            y = layer.forward(h, residual=None, mode=mode)
+        for i, layer in enumerate(self.layers):
+            if mode == "padded" and self.peer is not None:
+                y = layer.forward_p2p(h, self.peer, i)
+            else:
+                y = layer.forward(h, residual=None, mode=mode)
             h = residual_layernorm(y, h, out=y)
         out.copy_(h)
 
