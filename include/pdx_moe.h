@@ -319,6 +319,11 @@ int pdx_ep_ungroup(const void *grouped, const int32_t *perm, const int32_t *offs
 int pdx_ep_combine(const void *y, int64_t y_rows, const void *weights, const int32_t *inv_ep,
                    int64_t T, int32_t top_k, int64_t H, const void *residual, void *out,
                    pdx_stream_t stream);
+/* pdx_ep_combine with the next-layer norm fused (as pdx_combine_layernorm):
+ * out[t] = bf16(layer_norm(bf16(sum_s bf16(y[inv_ep[t*k+s]] * w)) + residual[t])). */
+int pdx_ep_combine_layernorm(const void *y, int64_t y_rows, const void *weights, const int32_t *inv_ep, int64_t T,
+                             int32_t top_k, int64_t H, const void *residual, float eps, void *out,
+                             pdx_stream_t stream);
 
 /* ---- Expert-parallel exchange over NVLink peer memory ----------------------
  * The padded (decode) exchange without a collective library: each rank's

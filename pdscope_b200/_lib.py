@@ -99,6 +99,8 @@ SIGNATURES = {
     "pdx_ep_regroup": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "pdx_ep_ungroup": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "pdx_ep_combine": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i32, c_i64, c_vp, c_vp, c_vp]),
+    "pdx_ep_combine_layernorm": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i32, c_i64, c_vp, ctypes.c_float,
+                                                c_vp, c_vp]),
     "pdx_device_error": (ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_uint32)]),
     "pdx_p2p_alloc": (ctypes.c_int, [c_sz, ctypes.POINTER(c_vp)]),
     "pdx_p2p_free": (ctypes.c_int, [c_vp]),

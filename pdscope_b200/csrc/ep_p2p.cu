@@ -67,7 +67,8 @@ __device__ bool wait_flags(const unsigned long long* flags, int R, unsigned long
 
 // Dispatch: packed row p (expert e, destination d = e / EL, position pos in the
 // block for d) -> recv block `me` of rank d; inv_ep[positions[p]] = d*C + pos.
-// The last CTA publishes the per-expert counts and then the flags of all ranks.
+// One warp per row, grid-stride; the last CTA publishes the per-expert counts
+// and then the flags of all ranks.
 __global__ void __launch_bounds__(256) k_ep_dispatch_p2p(const uint16_t* __restrict__ x,
                                                          const int32_t* __restrict__ tokens,
                                                          const int32_t* __restrict__ positions,
@@ -76,34 +77,35 @@ __global__ void __launch_bounds__(256) k_ep_dispatch_p2p(const uint16_t* __restr
                                                          int32_t* __restrict__ inv_ep) {
     griddep_wait();
     const unsigned long long step = *lay.step + 1ull;
-    const int p = static_cast<int>(blockIdx.x);
-    __shared__ int64_t s_dst;
-    __shared__ int s_d;
-    if (threadIdx.x == 0) {
-        int lo = 0, hi = E - 1;
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (offsets[mid] <= p) lo = mid; else hi = mid - 1;
+    const int warps = static_cast<int>(blockDim.x >> 5);
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    for (int p = static_cast<int>(blockIdx.x) * warps + static_cast<int>(threadIdx.x >> 5); p < rows;
+         p += static_cast<int>(gridDim.x) * warps) {
+        int64_t dst = -1;
+        int d = 0;
+        if (lane == 0) {
+            int lo = 0, hi = E - 1;  // expert of row p: largest e with offsets[e] <= p
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (offsets[mid] <= p) lo = mid; else hi = mid - 1;
+            }
+            d = lo / EL;
+            const int64_t pos = p - offsets[d * EL];
+            dst = static_cast<int64_t>(d) * C + pos;
+            if (pos >= C) {
+                raise_error(PDX_DEVERR_BAD_EXPERT);
+                dst = -1;
+            }
+            inv_ep[positions[p]] = static_cast<int32_t>(dst < 0 ? 0 : dst);
         }
-        const int d = lo / EL;
-        const int64_t pos = p - offsets[d * EL];
-        int64_t dst = static_cast<int64_t>(d) * C + pos;
-        if (pos >= C) {
-            raise_error(PDX_DEVERR_BAD_EXPERT);
-            dst = -1;
-        }
-        s_dst = dst;
-        s_d = d;
-        inv_ep[positions[p]] = static_cast<int32_t>(dst < 0 ? 0 : dst);
-    }
-    __syncthreads();
-    if (s_dst >= 0) {
-        const int d = s_d;
-        const int64_t pos = s_dst - static_cast<int64_t>(d) * C;
-        uint16_t* dst = reinterpret_cast<uint16_t*>(lay.recv[d]) + (static_cast<int64_t>(me) * C + pos) * H;
+        dst = __shfl_sync(0xffffffffu, dst, 0);
+        d = __shfl_sync(0xffffffffu, d, 0);
+        if (dst < 0) continue;
+        const int64_t pos = dst - static_cast<int64_t>(d) * C;
+        uint16_t* out = reinterpret_cast<uint16_t*>(lay.recv[d]) + (static_cast<int64_t>(me) * C + pos) * H;
         const uint16_t* src = x + static_cast<size_t>(tokens[p]) * H;
-        for (int c = static_cast<int>(threadIdx.x) * 8; c < H; c += blockDim.x * 8)
-            *reinterpret_cast<uint4*>(dst + c) = __ldg(reinterpret_cast<const uint4*>(src + c));
+        for (int c = lane * 8; c < H; c += 32 * 8)
+            *reinterpret_cast<uint4*>(out + c) = __ldg(reinterpret_cast<const uint4*>(src + c));
     }
     // completion: every CTA's stores are visible system-wide before the last
     // CTA publishes
@@ -187,27 +189,30 @@ __global__ void __launch_bounds__(1024) k_ep_layout_p2p(int R, int EL, int64_t C
 }
 
 // Return: regrouped FFN row g (receive position perm[g] = s*C + pos) -> back
-// block `me` of rank s at pos.  The last CTA publishes the flags of all ranks
-// (also those this rank returned nothing to).
+// block `me` of rank s at pos; one warp per row, grid-stride.  The last CTA
+// publishes the flags of all ranks (also those this rank returned nothing to).
 __global__ void __launch_bounds__(256) k_ep_return_p2p(const uint16_t* __restrict__ yg,
                                                        const int32_t* __restrict__ perm,
                                                        const int32_t* __restrict__ offsets_l, int EL, int rows_cap,
                                                        int H, int R, int me, int64_t C, P2PLayer lay) {
     griddep_wait();
     const unsigned long long step = *lay.step + 1ull;
-    const int g = static_cast<int>(blockIdx.x);
-    if (g < rows_cap && g < offsets_l[EL]) {
+    const int warps = static_cast<int>(blockDim.x >> 5);
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    const int total = min(rows_cap, offsets_l[EL]);
+    for (int g = static_cast<int>(blockIdx.x) * warps + static_cast<int>(threadIdx.x >> 5); g < total;
+         g += static_cast<int>(gridDim.x) * warps) {
         const int p = perm[g];
-        if (p >= 0 && p < rows_cap) {
-            const int s = static_cast<int>(p / C);
-            const int64_t pos = p - static_cast<int64_t>(s) * C;
-            uint16_t* dst = reinterpret_cast<uint16_t*>(lay.back[s]) + (static_cast<int64_t>(me) * C + pos) * H;
-            for (int c = static_cast<int>(threadIdx.x) * 8; c < H; c += blockDim.x * 8)
-                *reinterpret_cast<uint4*>(dst + c) =
-                    __ldg(reinterpret_cast<const uint4*>(yg + static_cast<size_t>(g) * H + c));
-        } else {
-            raise_error(PDX_DEVERR_BAD_EXPERT);
+        if (p < 0 || p >= rows_cap) {
+            if (lane == 0) raise_error(PDX_DEVERR_BAD_EXPERT);
+            continue;
         }
+        const int s = static_cast<int>(p / C);
+        const int64_t pos = p - static_cast<int64_t>(s) * C;
+        uint16_t* dst = reinterpret_cast<uint16_t*>(lay.back[s]) + (static_cast<int64_t>(me) * C + pos) * H;
+        for (int c = lane * 8; c < H; c += 32 * 8)
+            *reinterpret_cast<uint4*>(dst + c) =
+                __ldg(reinterpret_cast<const uint4*>(yg + static_cast<size_t>(g) * H + c));
     }
     __threadfence_system();
     __syncthreads();

@@ -401,8 +401,13 @@ struct StreamPlan {
     size_t partial_bytes, ticket_bytes;
 };
 
+#ifndef PDX_SPLIT_UNITS_PER_SM
+#define PDX_SPLIT_UNITS_PER_SM 8
+#endif
+// K splits per weight tile of the decode GEMMs: enough work units
+// (tiles x splits) for PDX_SPLIT_UNITS_PER_SM per SM, each split >= 4 K blocks.
 int plan_splits(int num_kb, int64_t est_tiles) {
-    const int64_t want = (8 * kPlanSMs + est_tiles / 2) / std::max<int64_t>(est_tiles, 1);
+    const int64_t want = (PDX_SPLIT_UNITS_PER_SM * kPlanSMs + est_tiles / 2) / std::max<int64_t>(est_tiles, 1);
     return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, std::max(1, num_kb / 4))));
 }
 
@@ -763,6 +768,23 @@ int pdx_combine_layernorm(const void* y, const void* weights, const int32_t* inv
     return ok();
 }
 
+int pdx_ep_combine_layernorm(const void* y, int64_t y_rows, const void* weights, const int32_t* inv_ep, int64_t T,
+                             int32_t top_k, int64_t H, const void* residual, float eps, void* out,
+                             pdx_stream_t stream) {
+    if (!y || !weights || !inv_ep || !residual || !out) return fail(PDX_ERR_INVALID, "null combine argument");
+    if (T < 1 || top_k < 1 || y_rows < 1) return fail(PDX_ERR_INVALID, "empty combine");
+    if (top_k > kMaxTopK) return fail(PDX_ERR_UNSUPPORTED, "top_k > %d", kMaxTopK);
+    int st = check_norm_shape(H);
+    if (st) return st;
+    if (!(eps > 0.f)) return fail(PDX_ERR_INVALID, "eps must be positive");
+    PDX_PDL_TRY(launch_pdl(k_combine_norm, dim3(static_cast<unsigned>(T)), dim3(kCombineThreads), 0, stream,
+                           static_cast<const uint16_t*>(y), static_cast<const uint16_t*>(weights), inv_ep,
+                           static_cast<int>(T), static_cast<int>(top_k), static_cast<int>(H),
+                           static_cast<int>(y_rows), static_cast<const uint16_t*>(residual), eps,
+                           static_cast<uint16_t*>(out)));
+    return ok();
+}
+
 int pdx_combine(const void* y, const void* weights, const int32_t* inverse, int64_t T, int32_t top_k, int64_t H,
                 const void* residual, void* out, pdx_stream_t stream) {
     if (!y || !weights || !inverse || !out) return fail(PDX_ERR_INVALID, "null combine argument");
@@ -984,7 +1006,11 @@ int pdx_ep_dispatch_p2p(const void* x, const int32_t* tokens, const int32_t* pos
     if (T < 1 || top_k < 1 || E % ranks || capacity < 1 || E / ranks > kEpMaxExperts / ranks)
         return fail(PDX_ERR_INVALID, "invalid expert-parallel shape");
     if (H < 8 || H % 8) return fail(PDX_ERR_UNSUPPORTED, "H must be a positive multiple of 8");
-    pdx::k_ep_dispatch_p2p<<<static_cast<unsigned>(T * top_k), 256, 0, stream>>>(
+    int sms = 0;
+    if ((st = device_setup(&sms))) return st;
+    const int64_t rows = T * top_k;
+    const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((rows + 7) / 8, 2 * sms)));
+    pdx::k_ep_dispatch_p2p<<<grid, 256, 0, stream>>>(
         static_cast<const uint16_t*>(x), tokens, positions, offsets, static_cast<int>(T * top_k),
         static_cast<int>(H), static_cast<int>(E), static_cast<int>(E / ranks), ranks, rank, capacity,
         to_p2p(layer), inv_ep);
@@ -1016,7 +1042,10 @@ int pdx_ep_return_p2p(const void* grouped, const int32_t* perm, const int32_t* o
     if (!grouped || !perm || !offsets_l || rows_cap < 1 || capacity < 1)
         return fail(PDX_ERR_INVALID, "invalid EP return argument");
     if (H < 8 || H % 8) return fail(PDX_ERR_UNSUPPORTED, "H must be a positive multiple of 8");
-    pdx::k_ep_return_p2p<<<static_cast<unsigned>(rows_cap), 256, 0, stream>>>(
+    int sms = 0;
+    if ((st = device_setup(&sms))) return st;
+    const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((rows_cap + 7) / 8, 2 * sms)));
+    pdx::k_ep_return_p2p<<<grid, 256, 0, stream>>>(
         static_cast<const uint16_t*>(grouped), perm, offsets_l, static_cast<int>(local_experts),
         static_cast<int>(rows_cap), static_cast<int>(H), ranks, rank, capacity, to_p2p(layer));
     PDX_LAUNCHED();

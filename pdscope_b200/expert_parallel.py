@@ -35,7 +35,7 @@ import torch
 
 from . import _lib
 from ._lib import check, lib
-from .runtime import ExpertSlab, Packed, _ptr, _stream, pack as _pack, residual_layernorm
+from .runtime import LN_EPS, ExpertSlab, Packed, _ptr, _stream, pack as _pack, residual_layernorm
 
 PADDED_MAX_TOKENS = 256
 
@@ -211,9 +211,10 @@ class ExpertParallelMoE:
         return self.ops.combine(back, back.shape[0], d.weights, d.inverse, residual)
 
     # ---- padded exchange over NVLink peer memory ----------------------------------------
-    def forward_p2p(self, x, peer, layer, residual=None):
+    def forward_p2p(self, x, peer, layer, residual=None, norm=False):
         """The padded layer with the exchange done by peer stores and flags
-        (pdx_ep_dispatch_p2p ... pdx_ep_wait_back) instead of all-to-alls."""
+        (pdx_ep_dispatch_p2p ... pdx_ep_wait_back) instead of all-to-alls.
+        With ``norm`` the output is layer_norm(MoE(x) + residual)."""
         t_count, hidden = x.shape
         cap = self.capacity(t_count)
         if cap > peer.cap_max:
@@ -240,8 +241,13 @@ class ExpertParallelMoE:
                                     lay, s))
         check(lib.pdx_ep_wait_back(R, self.rank, lay, s))
         out = torch.empty((t_count, hidden), dtype=torch.bfloat16, device=dev)
-        check(lib.pdx_ep_combine(ctypes.c_void_p(peer.local(layer, "back")), rows_cap, _ptr(w), _ptr(inv), t_count,
-                                 k, hidden, _ptr(residual), _ptr(out), s))
+        back = ctypes.c_void_p(peer.local(layer, "back"))
+        if norm:
+            check(lib.pdx_ep_combine_layernorm(back, rows_cap, _ptr(w), _ptr(inv), t_count, k, hidden, _ptr(residual),
+                                               ctypes.c_float(LN_EPS), _ptr(out), s))
+        else:
+            check(lib.pdx_ep_combine(back, rows_cap, _ptr(w), _ptr(inv), t_count, k, hidden, _ptr(residual),
+                                     _ptr(out), s))
         return out
 
     # ---- the whole layer over the exchange -------------------------------------------
@@ -366,10 +372,10 @@ class ExpertParallelStack:
         h = x
         for i, layer in enumerate(self.layers):
             if mode == "padded" and self.peer is not None:
-                y = layer.forward_p2p(h, self.peer, i)
+                h = layer.forward_p2p(h, self.peer, i, residual=h, norm=True)
             else:
                 y = layer.forward(h, residual=None, mode=mode)
-            h = residual_layernorm(y, h, out=y)
+                h = residual_layernorm(y, h, out=y)
         out.copy_(h)
 
     def step(self, t_count, *, graph=True):
