@@ -402,10 +402,14 @@ struct StreamPlan {
 };
 
 #ifndef PDX_SPLIT_UNITS_PER_SM
-#define PDX_SPLIT_UNITS_PER_SM 8
+#define PDX_SPLIT_UNITS_PER_SM 1
 #endif
-// K splits per weight tile of the decode GEMMs: enough work units
-// (tiles x splits) for PDX_SPLIT_UNITS_PER_SM per SM, each split >= 4 K blocks.
+// K splits per weight tile of the decode GEMMs: about PDX_SPLIT_UNITS_PER_SM
+// work units (tiles x splits) per SM, each split >= 4 K blocks.  One unit per
+// SM measured best at every decode batch (1..64 tokens at the Qwen3-30B-A3B
+// shape): a split costs an extra FP32 partial round trip and a ticketed
+// reduction, and one weight tile per SM already keeps HBM busy once about 30
+// experts are active.
 int plan_splits(int num_kb, int64_t est_tiles) {
     const int64_t want = (PDX_SPLIT_UNITS_PER_SM * kPlanSMs + est_tiles / 2) / std::max<int64_t>(est_tiles, 1);
     return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, std::max(1, num_kb / 4))));
