@@ -10,7 +10,8 @@
 //   warp 0      TMA producer: A tile [128 x 64] + B tile [256 x 64] per stage
 //   warp 1      MMA issuer: tcgen05.mma.cta_group::1.kind::f16, M=128 N=256
 //               K=16, FP32 accumulators in TMEM (two 256-column buffers)
-//   warps 2..5  epilogue: tcgen05.ld 32x32b, BF16 rounding, global stores
+//   warps 2..9  epilogue: tcgen05.ld 32x32b, BF16 rounding, global stores;
+//               two warps per TMEM lane quadrant, each on half of the columns
 // GEMM1 (SwiGLU): B = [128 gate rows ; 128 up rows] of the expert, epilogue
 //   h = bf16(bf16(silu(bf16(g))) * bf16(u)) -> h[rows, I].
 // GEMM2 (down):   B = 256 rows of Wd, epilogue y = bf16(acc) -> y[rows, H].
@@ -29,7 +30,9 @@ constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;   // 64 BF16 = one 128-byte swizzle row
 constexpr int kGemmBN = 256;  // MMA N (B rows per stage)
 constexpr int kGemmStages = 4;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmEpiWarps = 8;                          // two per TMEM lane quadrant
+constexpr int kGemmThreads = 64 + 32 * kGemmEpiWarps;      // producer, MMA, epilogue
+constexpr int kPairThreads = 192;                          // producer, MMA, 4 epilogue warps
 constexpr uint32_t kTileABytes = kGemmBM * kGemmBK * 2;  // 16 KiB
 constexpr uint32_t kTileBBytes = kGemmBN * kGemmBK * 2;  // 32 KiB
 constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
@@ -115,54 +118,78 @@ __device__ __forceinline__ void build_tile_tables(const GemmArgs& args, int n_ac
     if (lane == 31) { s_misc[0] = inc; s_misc[1] = n_active; }
 }
 
-// One accumulator row (this thread's TMEM lane) -> BF16 output row.
-// swiglu: columns [0,128) hold gate, [128,256) up; h = bf16(bf16(silu(bf16(g))) * bf16(u)).
-// otherwise: y = bf16(acc) over 256 columns.
-__device__ __forceinline__ void epilogue_row(int swiglu, uint32_t taddr, uint16_t* orow, bool valid) {
+// Orders the use of registers filled by tcgen05.ld after tcgen05.wait::ld: the
+// empty asm statements follow the (volatile) wait and their outputs are what
+// the conversion reads.
+template <int N>
+__device__ __forceinline__ void tmem_wait_pin(uint32_t (&r)[N]) {
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
+
+// Columns [c0, c0 + nc) of one accumulator row (this thread's TMEM lane) ->
+// BF16 output row.  Several TMEM loads are in flight per wait.
+// swiglu: accumulator columns [0,128) hold gate, [128,256) up; output column c
+//   h = bf16(bf16(silu(bf16(g[c]))) * bf16(u[c])).
+// otherwise: y = bf16(acc) over the 256 columns.
+__device__ __forceinline__ void epilogue_cols(int swiglu, uint32_t taddr, uint16_t* orow, bool valid, int c0,
+                                              int nc) {
     if (swiglu) {
 #pragma unroll 1
-        for (int c = 0; c < kGemmBN / 2; c += 16) {
-            uint32_t g[16], u[16];
+        for (int c = c0; c < c0 + nc; c += 32) {
+            uint32_t g[32], u[32];
             tmem_ld16(taddr + c, g);
+            tmem_ld16(taddr + c + 16, g + 16);
             tmem_ld16(taddr + kGemmBN / 2 + c, u);
-            tmem_wait_ld();
-            uint32_t packed[8];
+            tmem_ld16(taddr + kGemmBN / 2 + c + 16, u + 16);
+            tmem_wait_pin(g);
+            tmem_wait_pin(u);
+            uint32_t packed[16];
 #pragma unroll
-            for (int i = 0; i < 16; i += 2) {
+            for (int i = 0; i < 32; i += 2) {
                 float hv[2];
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
                     const float gb = round_bf16(__uint_as_float(g[i + j]));
                     const float ub = round_bf16(__uint_as_float(u[i + j]));
-                    const float s = round_bf16(__fdiv_rn(gb, 1.0f + expf(-gb)));
-                    hv[j] = s * ub;
+                    const float sv = round_bf16(__fdiv_rn(gb, 1.0f + expf(-gb)));
+                    hv[j] = sv * ub;
                 }
                 packed[i / 2] = static_cast<uint32_t>(f2bits(hv[0])) | (static_cast<uint32_t>(f2bits(hv[1])) << 16);
             }
             if (valid) {
                 uint4* dst = reinterpret_cast<uint4*>(orow + c);
-                dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
             }
         }
     } else {
 #pragma unroll 1
-        for (int c = 0; c < kGemmBN; c += 16) {
-            uint32_t v[16];
-            tmem_ld16(taddr + c, v);
-            tmem_wait_ld();
-            uint32_t packed[8];
+        for (int c = c0; c < c0 + nc; c += 64) {
+            uint32_t v[64];
 #pragma unroll
-            for (int i = 0; i < 16; i += 2)
+            for (int i = 0; i < 4; ++i) tmem_ld16(taddr + c + 16 * i, v + 16 * i);
+            tmem_wait_pin(v);
+            uint32_t packed[32];
+#pragma unroll
+            for (int i = 0; i < 64; i += 2)
                 packed[i / 2] = static_cast<uint32_t>(f2bits(__uint_as_float(v[i]))) |
                                 (static_cast<uint32_t>(f2bits(__uint_as_float(v[i + 1]))) << 16);
             if (valid) {
                 uint4* dst = reinterpret_cast<uint4*>(orow + c);
-                dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
             }
         }
     }
+}
+
+// Whole accumulator row: 128 SwiGLU output columns or 256 down columns.
+__device__ __forceinline__ void epilogue_row(int swiglu, uint32_t taddr, uint16_t* orow, bool valid) {
+    epilogue_cols(swiglu, taddr, orow, valid, 0, swiglu ? kGemmBN / 2 : kGemmBN);
 }
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -200,7 +227,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tmem_full[b], 1);
-            mbar_init(&tmem_empty[b], 128);
+            mbar_init(&tmem_empty[b], 32 * kGemmEpiWarps);
         }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
@@ -291,9 +318,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             __syncwarp();
         }
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
+        // ---------------- epilogue (warps 2..9) ----------------
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
         const int row_in_tile = q * 32 + static_cast<int>(lane);
+        const int half = (warp - 2) >> 2;  // which half of the tile's columns
+        const int half_cols = (args.swiglu ? kGemmBN / 2 : kGemmBN) / 2;
         int lt = 0;
         for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++lt) {
             const int b = lt & 1;
@@ -307,7 +336,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const bool valid = r < n_e;
             uint16_t* orow = args.out + static_cast<int64_t>(seg0 + r) * args.out_ld + ti.n * out_cols_per_tile;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * kGemmBN);
-            epilogue_row(args.swiglu, taddr, orow, valid);
+            epilogue_cols(args.swiglu, taddr, orow, valid, half * half_cols, half_cols);
             tc_fence_before();
             mbar_arrive(&tmem_empty[b]);
         }
@@ -362,7 +391,7 @@ __device__ __forceinline__ void pair_abort(volatile int* abort_flag, uint32_t pe
     st_shared_remote_u32(peer_abort_addr, 1u);
 }
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     k_grouped_gemm_pair(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b0,
                         const __grid_constant__ CUtensorMap tm_b1, GemmArgs args) {
     extern __shared__ __align__(1024) unsigned char smem_pair[];

@@ -144,7 +144,7 @@ int device_setup(int* sms_out) {
         {   // CTA pairs that can be resident at once (one CTA per SM)
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(2 * (sms / 2));
-            cfg.blockDim = dim3(kGemmThreads);
+            cfg.blockDim = dim3(kPairThreads);
             cfg.dynamicSmemBytes = kGemmPairSmemBytes;
             int clusters = 0;
             if (cudaOccupancyMaxActiveClusters(&clusters, k_grouped_gemm_pair, &cfg) != cudaSuccess || clusters < 1) {
@@ -555,12 +555,12 @@ int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* o
         GemmArgs a1{offsets, active, w->slot_of_expert, w->num_slots, gs, us, static_cast<int>(H),
                     static_cast<int>(I), 1, h, I};
         const int pairs1 = static_cast<int>(std::min<int64_t>(max_pairs, pair_tiles_bound * (I / (kGemmBN / 2))));
-        PDX_PDL_TRY(launch_pdl(k_grouped_gemm_pair, dim3(2 * pairs1), dim3(kGemmThreads), kGemmPairSmemBytes,
+        PDX_PDL_TRY(launch_pdl(k_grouped_gemm_pair, dim3(2 * pairs1), dim3(kPairThreads), kGemmPairSmemBytes,
                                stream, tm_x, tm_g, tm_u, a1));
         GemmArgs a2{offsets, active, w->slot_of_expert, w->num_slots, ds, ds, static_cast<int>(I),
                     static_cast<int>(H), 0, static_cast<uint16_t*>(y), H};
         const int pairs2 = static_cast<int>(std::min<int64_t>(max_pairs, pair_tiles_bound * (H / kGemmBN)));
-        PDX_PDL_TRY(launch_pdl(k_grouped_gemm_pair, dim3(2 * pairs2), dim3(kGemmThreads), kGemmPairSmemBytes,
+        PDX_PDL_TRY(launch_pdl(k_grouped_gemm_pair, dim3(2 * pairs2), dim3(kPairThreads), kGemmPairSmemBytes,
                                stream, tm_h, tm_d, tm_d, a2));
         return PDX_OK;
     }
