@@ -33,6 +33,23 @@ def test_library_exports_every_declared_symbol():
     assert _lib.lib.pdx_abi_version() == _lib.ABI_VERSION
 
 
+def test_python_constants_match_header():
+    """The integer constants the bindings mirror (status codes, device error
+    codes, FFN modes, the layer flag) have the header's values."""
+    from pdscope_b200 import _lib
+    text = (ROOT / "include" / "pdx_moe.h").read_text()
+    consts = {m.group(1): int(m.group(2), 0)
+              for m in re.finditer(r"\b(PDX_[A-Z0-9_]+)\s*(?:=\s*|\s+)(0x[0-9a-fA-F]+|\d+)u?\b", text)}
+    mirrored = {}
+    for name, value in consts.items():
+        for py_name in (name, name[len("PDX_"):]):
+            if hasattr(_lib, py_name):
+                mirrored[name] = (getattr(_lib, py_name), value)
+    for required in ("PDX_OK", "PDX_ERR_DEVICE", "PDX_DEVERR_BAD_SLOT", "PDX_FFN_GEMM_1CTA", "PDX_LAYER_OUT_NORM"):
+        assert required in mirrored, required
+    assert all(py == c for py, c in mirrored.values()), mirrored
+
+
 def test_workspace_queries_are_monotone():
     from pdscope_b200._lib import lib
     a = lib.pdx_layer_workspace_bytes(1, 2048, 128, 8, 768, 0)
