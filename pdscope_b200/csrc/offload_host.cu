@@ -357,12 +357,16 @@ int pdx_offload_forward_layer(pdx_offload* h, int32_t layer, const void* x, int6
         *slot_out = i;
         return PDX_OK;
     };
-    auto mark_ready = [&](const std::vector<int64_t>& idxs) -> int {
+    // Records a copy-stream event after the copies into `idxs` and makes it
+    // their ready event.  Also called on an error path, so that no slot whose
+    // copy was issued is left without one (a later hit waits on it).
+    auto mark_ready = [&](const std::vector<int64_t>& idxs, int* ev_out) -> int {
         const int ev = e->copy_next;
         e->copy_next = (e->copy_next + 1) % OffloadEngine::kEvents;
         PDX_CUDA_TRY(cudaEventRecord(e->copy_ev[ev], e->copy_stream));
         for (int64_t i : idxs) e->ring_ready[i] = ev;
-        return ev;
+        if (ev_out) *ev_out = ev;
+        return PDX_OK;
     };
     std::vector<std::vector<int32_t>> chunks;
     std::vector<int> chunk_ev;
@@ -371,13 +375,18 @@ int pdx_offload_forward_layer(pdx_offload* h, int32_t layer, const void* x, int6
         std::vector<int64_t> idxs;
         for (int32_t ex : part) {
             int64_t slot;
-            if ((st = copy_in(base + ex, false, &slot))) return st;
+            if ((st = copy_in(base + ex, false, &slot))) {
+                if (!idxs.empty()) mark_ready(idxs, nullptr);
+                return st;
+            }
             pinned.push_back(slot);
             idxs.push_back(slot);
             table[ex] = static_cast<int32_t>(e->n_fixed + slot);
         }
+        int ev = 0;
+        if ((st = mark_ready(idxs, &ev))) return st;
         chunks.push_back(part);
-        chunk_ev.push_back(mark_ready(idxs));
+        chunk_ev.push_back(ev);
     }
     // 3. the next layer's predicted experts, queued behind the demand copies
     if (predict) {
@@ -392,10 +401,13 @@ int pdx_offload_forward_layer(pdx_offload* h, int32_t layer, const void* x, int6
             pinned.insert(pinned.end(), issued.begin(), issued.end());
             st = copy_in(nbase + ex, true, &slot);
             pinned.resize(before);
-            if (st) return st;
+            if (st) {
+                if (!issued.empty()) mark_ready(issued, nullptr);
+                return st;
+            }
             issued.push_back(slot);
         }
-        if (!issued.empty()) mark_ready(issued);
+        if (!issued.empty() && (st = mark_ready(issued, nullptr))) return st;
     }
     // 4. tables and active lists, then the FFN launches
     const int launches = 1 + static_cast<int>(chunks.size());
