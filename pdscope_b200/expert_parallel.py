@@ -219,6 +219,9 @@ class ExpertParallelMoE:
         cap = self.capacity(t_count)
         if cap > peer.cap_max:
             raise ValueError("batch larger than the peer exchange was sized for")
+        if (hidden, self.local, self.world, self.rank) != (peer.H, peer.EL, peer.R, peer.rank) or \
+                not 0 <= layer < peer.L:
+            raise ValueError("peer exchange regions were sized for another layer shape, group or layer count")
         R, EL, k, dev = self.world, self.local, self.top_k, x.device
         sel, w = self.ops.route(x, self.gate, k, self.normalize)
         p = self.ops.pack(sel, w, self.experts)
