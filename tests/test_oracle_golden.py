@@ -198,3 +198,27 @@ def test_oracle_rejects_bad_inputs():
         mo.compact_expert_groups(np.full((2, 2), 200, np.int64), np.zeros((2, 2), np.uint16), 128)
     with pytest.raises(ValueError):
         mo.route_from_logits(np.zeros((1, 4), np.uint16), 5, True)
+
+
+def test_cpu_baseline_path_matches_reference_layer(golden):
+    """The torch-CPU layer path bench.py times as the reference arm
+    (oracle/cpu_path.py) reproduces the reference's own fused-merge output of
+    the golden layer: same routing, and the merged output bit for bit on
+    nearly every element (CPU BF16 GEMM blocking may move a rare ulp)."""
+    import torch
+    from oracle import cpu_path
+    x, gate, wg, wu, wd = _layer_inputs()
+
+    def t(bits):
+        return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16)
+
+    experts = [(t(wg[e]), t(wu[e]), t(wd[e])) for e in range(16)]
+    _, sel, w = cpu_path.route(t(x), t(gate), 4, True)
+    assert np.array_equal(sel.numpy(), golden["layer_selected"].astype(np.int64))
+    assert np.array_equal(w.view(torch.int16).numpy().view(np.uint16), golden["layer_weights"])
+    out, n_active = cpu_path.layer_forward(t(x), t(gate), experts, top_k=4)
+    ours = out.view(torch.int16).numpy().view(np.uint16)
+    assert n_active == int((golden["layer_selected"].reshape(-1, 1) == np.arange(16)).any(0).sum())
+    assert (ours == golden["layer_fused_out"]).mean() > 0.99
+    np.testing.assert_allclose(mo.bf16_to_f32(ours), mo.bf16_to_f32(golden["layer_fused_out"]), rtol=2e-2,
+                               atol=2e-2)
