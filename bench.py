@@ -19,12 +19,16 @@ Workload (synthetic seeded data, random-init weights):
     algorithmic bytes = active experts x 9,437,184 B + activation rows.
   * ``cpu_baseline``: the reference's CPU layer path (oracle/cpu_path.py, torch
     CPU ops) on this host's cores, a bounded sample of layers.
-Multi-GPU (N>1): one process per GPU, each a full replica of the stack serving
-its own batch (weak scaling); value = tokens of all ranks / max-over-ranks time.
+Multi-GPU (N>1, torchrun): expert parallel, 128/N experts per GPU, each rank
+routing its own decode batch (64 tokens per GPU, weak scaling) and exchanging
+rows over NVLink peer memory (``--ep-transport nccl``: NCCL all-to-all);
+value = tokens of all ranks / max-over-ranks time.  ``--ep-shape 235b`` runs
+config 5 instead (Qwen3-235B shape, 256 decode tokens in all).
 
 ``--impl reference`` times the reference's own CPU implementation of the path
-(the torch-CPU restatement in oracle/cpu_path.py) on all host cores and prints
-the same metric.
+(the torch-CPU restatement in oracle/cpu_path.py) on all host cores on the
+pdx arm's whole-job workload (at N GPUs the N x 64-token batch, or config 5's
+shape) and prints the same metric; under torchrun rank 0 alone runs it.
 """
 from __future__ import annotations
 
@@ -183,28 +187,43 @@ def run_reference(args, rank):
     warm = max(0, args.warmup)
     from oracle import cpu_path
     cores = args.cpu_threads or usable_cores()
-    sample = [cpu_path.make_layer(CFG["hidden"], CFG["experts"], CFG["inter"], seed=100 + i)
-              for i in range(max(1, args.cpu_layers))]
-    t_count = args.decode_batch
+    # the whole job's workload of the pdx arm with the same flags: at N GPUs the
+    # decode batch is N x the per-GPU batch (weak scaling), or config 5's 256
+    # tokens at the Qwen3-235B shape over as many layers as the pdx arm holds
+    world = max(1, args.gpus)
+    E = CFG["experts"]
+    if world > 1 and args.ep_shape == "235b":
+        H, I = 4096, 1536
+        t_count = max(1, 256 // world) * world
+        fit = int(150e9 // ((E // world) * 3 * H * I * 2))
+        L = min(94 if args.layers == CFG["layers"] else args.layers, fit)
+        workload = f"config5 decode batch {t_count} in all: {L}-layer Qwen3-235B-A22B-shape MoE stack"
+        scaling = "strong"
+    else:
+        H, I, L = CFG["hidden"], CFG["inter"], args.layers
+        t_count = args.decode_batch * world
+        per_gpu = f" ({args.decode_batch} per GPU x {world} GPUs)" if world > 1 else ""
+        workload = f"config2 decode batch {t_count}{per_gpu}: {L}-layer Qwen3-30B-A3B-shape MoE stack"
+        scaling = "weak"
+    sample = [cpu_path.make_layer(H, E, I, seed=100 + i) for i in range(max(1, args.cpu_layers))]
     for _ in range(min(warm, 1)):
-        cpu_path.time_layers(sample[:1], t_count, CFG["hidden"], cores, repeats=1)
+        cpu_path.time_layers(sample[:1], t_count, H, cores, repeats=1)
     t0 = time.perf_counter()
     per_layer_all = []
     for s in range(steps):
-        per_layer, _ = cpu_path.time_layers(sample[:1], t_count, CFG["hidden"], cores, repeats=1, seed=s)
+        per_layer, _ = cpu_path.time_layers(sample[:1], t_count, H, cores, repeats=1, seed=s)
         per_layer_all.append(per_layer)
     elapsed = time.perf_counter() - t0
     per_layer = statistics.mean(per_layer_all)
-    value = t_count / (per_layer * CFG["layers"])
+    value = t_count / (per_layer * L)
     line = dict(metric=METRIC, value=value, unit="tok/s", impl="reference", n_gpus=args.gpus, steps=steps,
-                warmup=warm, ms_per_step=per_layer * CFG["layers"] * 1e3, higher_is_better=True, scaling="weak",
+                warmup=warm, ms_per_step=per_layer * L * 1e3, higher_is_better=True, scaling=scaling,
                 vs_baseline=None, dtype="bf16", data="synthetic",
-                config=dict(workload=f"config2 decode batch {t_count}: 48-layer Qwen3-30B-A3B-shape MoE stack",
-                            hidden=CFG["hidden"], experts=CFG["experts"], inter=CFG["inter"], top_k=CFG["top_k"],
-                            layers=CFG["layers"], decode_batch=t_count, parallelism="cpu"),
+                config=dict(workload=workload, hidden=H, experts=E, inter=I, top_k=CFG["top_k"], layers=L,
+                            decode_batch=t_count, parallelism="cpu"),
                 cpu_baseline=dict(value=value, unit="tok/s", cores=cores, kind="port",
                                   sample=(f"each step = 1 random-init layer at batch {t_count} on the reference's "
-                                          f"CPU path (torch CPU, oracle/cpu_path.py), scaled to 48 layers; "
+                                          f"CPU path (torch CPU, oracle/cpu_path.py), scaled to {L} layers; "
                                           f"wall {elapsed:.1f}s")),
                 e2e=dict(value=value, unit="tok/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
     print(json.dumps(line), flush=True)
