@@ -452,7 +452,7 @@ def main():
                                 hidden=CFG["hidden"], experts=CFG["experts"], inter=CFG["inter"],
                                 top_k=CFG["top_k"], layers=L, decode_batch=headline_t,
                                 global_batch=headline_t * world,
-                                parallelism=f"replicas{world}" if world > 1 else "single",
+                                parallelism="single",
                                 l2="not flushed: each step streams ~%.1f GB of expert weights (> 126 MB L2)"
                                    % d["weight_gb_per_step"]),
                     roofline=roofline, cpu_baseline=cpu, e2e=e2e, clocks=d["clocks"],
