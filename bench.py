@@ -180,52 +180,83 @@ def cpu_baseline(tokens, layers, threads, steps=1):
                 ms_per_layer=per_layer * 1e3, torch_threads=torch.get_num_threads())
 
 
-def run_reference(args, rank):
-    if rank != 0:
-        return 0
-    steps = max(1, args.steps)
-    warm = max(0, args.warmup)
-    from oracle import cpu_path
-    cores = args.cpu_threads or usable_cores()
-    # the whole job's workload of the pdx arm with the same flags: at N GPUs the
-    # decode batch is N x the per-GPU batch (weak scaling), or config 5's 256
-    # tokens at the Qwen3-235B shape over as many layers as the pdx arm holds
-    world = max(1, args.gpus)
-    E = CFG["experts"]
+def ep_layers(args, world, H, I):
+    """Layers of the config-5 stack that fit one GPU's share of the experts."""
+    fit = int(150e9 // ((CFG["experts"] // world) * 3 * H * I * 2))
+    return min(94 if args.layers == CFG["layers"] else args.layers, fit)
+
+
+def headline_config(args, world):
+    """The workload of the headline line, identical for both arms: the pdx arm
+    runs it on the GPUs, the reference arm on the host cores."""
+    E, k = CFG["experts"], CFG["top_k"]
     if world > 1 and args.ep_shape == "235b":
         H, I = 4096, 1536
-        t_count = max(1, 256 // world) * world
-        fit = int(150e9 // ((E // world) * 3 * H * I * 2))
-        L = min(94 if args.layers == CFG["layers"] else args.layers, fit)
-        workload = f"config5 decode batch {t_count} in all: {L}-layer Qwen3-235B-A22B-shape MoE stack"
-        scaling = "strong"
+        L = ep_layers(args, world, H, I)
+        per_gpu = max(1, 256 // world)
+        return dict(workload=f"config5 decode batch {per_gpu * world} in all ({per_gpu} per GPU): {L}-layer "
+                             f"Qwen3-235B-A22B-shape MoE stack, experts split evenly over {world} GPUs",
+                    hidden=H, experts=E, inter=I, top_k=k, layers=L, decode_batch=per_gpu,
+                    global_batch=per_gpu * world, parallelism=f"ep{world}",
+                    l2="not flushed: every step streams the routed experts' weights (GBs, > 126 MB L2)"), "strong"
+    t = args.decode_batch
+    if world > 1:
+        workload = (f"config2 decode batch {t} per GPU: {args.layers}-layer Qwen3-30B-A3B-shape MoE stack, "
+                    f"experts split evenly over {world} GPUs")
     else:
-        H, I, L = CFG["hidden"], CFG["inter"], args.layers
-        t_count = args.decode_batch * world
-        per_gpu = f" ({args.decode_batch} per GPU x {world} GPUs)" if world > 1 else ""
-        workload = f"config2 decode batch {t_count}{per_gpu}: {L}-layer Qwen3-30B-A3B-shape MoE stack"
-        scaling = "weak"
+        workload = f"config2 decode batch {t}: {args.layers}-layer Qwen3-30B-A3B-shape MoE stack, all experts resident"
+    return dict(workload=workload, hidden=CFG["hidden"], experts=E, inter=CFG["inter"], top_k=k, layers=args.layers,
+                decode_batch=t, global_batch=t * world, parallelism=f"ep{world}" if world > 1 else "single",
+                l2="not flushed: every step streams the routed experts' weights (GBs, > 126 MB L2)"), "weak"
+
+
+def run_reference(args, rank):
+    """The reference's CPU layer path (oracle/cpu_path.py: route ->
+    compact_expert_groups -> per-expert torch CPU expert_forward -> index_add_
+    merge) on all host cores, timing the whole headline workload: every step
+    runs every layer of the stack on the whole job's token batch (N x the
+    per-GPU batch at N GPUs).  The stack's layers cycle through
+    ``--cpu-layers`` distinct random-init layers (the weights of all 48 would
+    not fit host memory), with x <- layer_norm(MoE(x) + x) between layers as
+    on the GPU arm."""
+    if rank != 0:
+        return 0
+    import torch
+    from oracle import cpu_path
+    steps = max(1, args.steps)
+    warm = max(0, args.warmup)
+    cores = args.cpu_threads or usable_cores()
+    world = max(1, args.gpus)
+    config, scaling = headline_config(args, world)
+    H, E, I, L = config["hidden"], config["experts"], config["inter"], config["layers"]
+    t_count = config["global_batch"]
+    torch.set_num_threads(cores)
     sample = [cpu_path.make_layer(H, E, I, seed=100 + i) for i in range(max(1, args.cpu_layers))]
-    for _ in range(min(warm, 1)):
-        cpu_path.time_layers(sample[:1], t_count, H, cores, repeats=1)
+    gen = torch.Generator(device="cpu").manual_seed(5)
+    x0 = torch.randn(t_count, H, generator=gen).to(torch.bfloat16)
+    for _ in range(warm):
+        cpu_path.stack_step(x0, sample, L)
+    times, active = [], []
     t0 = time.perf_counter()
-    per_layer_all = []
-    for s in range(steps):
-        per_layer, _ = cpu_path.time_layers(sample[:1], t_count, H, cores, repeats=1, seed=s)
-        per_layer_all.append(per_layer)
+    for _ in range(steps):
+        s0 = time.perf_counter()
+        _, act = cpu_path.stack_step(x0, sample, L)
+        times.append(time.perf_counter() - s0)
+        active.extend(act)
     elapsed = time.perf_counter() - t0
-    per_layer = statistics.mean(per_layer_all)
-    value = t_count / (per_layer * L)
+    ms = elapsed / steps * 1e3
+    value = t_count * steps / elapsed
     line = dict(metric=METRIC, value=value, unit="tok/s", impl="reference", n_gpus=args.gpus, steps=steps,
-                warmup=warm, ms_per_step=per_layer * L * 1e3, higher_is_better=True, scaling=scaling,
-                vs_baseline=None, dtype="bf16", data="synthetic",
-                config=dict(workload=workload, hidden=H, experts=E, inter=I, top_k=CFG["top_k"], layers=L,
-                            decode_batch=t_count, parallelism="cpu"),
+                warmup=warm, ms_per_step=ms, higher_is_better=True, scaling=scaling, vs_baseline=None,
+                dtype="bf16", data="synthetic", config=config,
                 cpu_baseline=dict(value=value, unit="tok/s", cores=cores, kind="port",
-                                  sample=(f"each step = 1 random-init layer at batch {t_count} on the reference's "
-                                          f"CPU path (torch CPU, oracle/cpu_path.py), scaled to {L} layers; "
-                                          f"wall {elapsed:.1f}s")),
-                e2e=dict(value=value, unit="tok/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+                                  sample=(f"every step runs all {L} layers at batch {t_count} on the reference's "
+                                          f"CPU path (torch CPU, oracle/cpu_path.py), cycling {len(sample)} "
+                                          f"random-init layers; {steps} steps in {elapsed:.1f} s wall, "
+                                          f"median {statistics.median(times) * 1e3:.0f} ms/step, mean active "
+                                          f"experts {statistics.mean(active):.1f}")),
+                e2e=dict(value=value, unit="tok/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0),
+                timed_layers_per_step=L, extrapolated=False)
     print(json.dumps(line), flush=True)
     return 0
 
@@ -436,6 +467,28 @@ def main():
                h2d_bytes_per_step=host_in.numel() * 2, d2h_bytes_per_step=host_out.numel() * 2,
                ms_per_step=e2e_ms / K)
 
+    # ---- parity of the timed path (after the timed regions) ---------------------------
+    # routing ids against the reference's own device route (F.linear/softmax/topk on this
+    # GPU) over whole rows, and the graph-replayed step against the eager step
+    from pdscope_b200.agreement import route_agreement
+    parity = dict(route_vs_device_reference={})
+    for t_count, zipf in ((1, False), (64, False), (512, False), (12450, True)):
+        gate0 = stack.gates[0]
+        if zipf:
+            gen = torch.Generator(device=dev).manual_seed(4321)
+            ranks_z = torch.randperm(CFG["experts"], device=dev, generator=gen).float() + 1
+            gate0 = gate0.clone()
+            gate0[:, 0] = (-ZIPF_ALPHA * ZIPF_S * torch.log(ranks_z)).to(torch.bfloat16)
+        xa = activations(t_count, CFG["hidden"], device=dev, seed=600 + t_count, zipf=zipf)
+        parity["route_vs_device_reference"][str(t_count)] = route_agreement(xa, gate0, CFG["top_k"], True)
+    t_count = headline_t
+    stack.input(t_count).copy_(activations(t_count, CFG["hidden"], device=dev, seed=606))
+    stack.step(t_count, graph=False)
+    eager_out = stack.output(t_count).clone()
+    stack.step(t_count)
+    torch.cuda.synchronize(dev)
+    parity["graph_step_equals_eager_step"] = bool(torch.equal(stack.output(t_count), eager_out))
+
     # ---- CPU baseline (rank 0, N = 1 only) -------------------------------------------
     cpu = None
     if world == 1 and not args.no_cpu:
@@ -447,18 +500,12 @@ def main():
         line = dict(metric=METRIC, value=d["tok_s"], unit="tok/s", n_gpus=world, steps=K, warmup=W,
                     ms_per_step=d["ms_per_step"], higher_is_better=True, scaling="weak", vs_baseline=None,
                     dtype="bf16", data="synthetic",
-                    config=dict(workload=f"config2 decode batch {headline_t}: 48-layer Qwen3-30B-A3B-shape MoE "
-                                         f"stack, all experts resident, one CUDA graph per step",
-                                hidden=CFG["hidden"], experts=CFG["experts"], inter=CFG["inter"],
-                                top_k=CFG["top_k"], layers=L, decode_batch=headline_t,
-                                global_batch=headline_t * world,
-                                parallelism="single",
-                                l2="not flushed: each step streams ~%.1f GB of expert weights (> 126 MB L2)"
-                                   % d["weight_gb_per_step"]),
+                    config=headline_config(args, 1)[0],
+                    execution="all experts resident in HBM; one CUDA graph per 48-layer step",
                     roofline=roofline, cpu_baseline=cpu, e2e=e2e, clocks=d["clocks"],
                     gpu_launches=d["launches_per_step"] * K,
                     decode={str(t): {k: v for k, v in r.items() if k != "clocks"} for t, r in decode.items()},
-                    prefill=prefill, config1_layer=config1)
+                    prefill=prefill, config1_layer=config1, parity=parity)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -624,8 +671,7 @@ def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
         raise SystemExit(f"{E} experts do not divide over {world} GPUs")
     el = E // world
     if big:
-        fit = int(150e9 // (el * expert_bytes))      # leave ~30 GB of HBM for activations and workspaces
-        L = min(94 if args.layers == CFG["layers"] else args.layers, fit)
+        L = ep_layers(args, world, H, I)             # leave ~30 GB of HBM for activations and workspaces
     g_gate = torch.Generator(device=dev).manual_seed(0)          # routers replicated on every rank
     g_w = torch.Generator(device=dev).manual_seed(1000 + rank)   # this rank's experts
     gates = []
@@ -731,24 +777,12 @@ def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
 
     d = decode[headline_t]
     if rank == 0:
-        if big:
-            workload = (f"config5 decode batch {headline_t * world} in all ({headline_t} per GPU): {L}-layer "
-                        f"Qwen3-235B-A22B-shape MoE stack (H={H}, I={I}), expert parallel {el} experts/GPU, "
-                        f"dispatch/combine exchange over NVLink, one CUDA graph per step")
-            scaling = "strong"
-        else:
-            workload = (f"config2 decode batch {headline_t} per GPU: 48-layer Qwen3-30B-A3B-shape "
-                        f"MoE stack, expert parallel {el} experts/GPU, dispatch/combine exchange over NVLink, "
-                        f"one CUDA graph per step")
-            scaling = "weak"
+        config, scaling = headline_config(args, world)
         line = dict(metric=METRIC, value=d["tok_s"], unit="tok/s", n_gpus=world, steps=K, warmup=W,
                     ms_per_step=d["ms_per_step"], higher_is_better=True, scaling=scaling, vs_baseline=None,
-                    dtype="bf16", data="synthetic",
-                    config=dict(workload=workload, hidden=H, experts=E, inter=I, top_k=k, layers=L,
-                                decode_batch=headline_t, global_batch=headline_t * world,
-                                parallelism=f"ep{world}",
-                                l2="not flushed: each step streams the rank's %.1f GB of expert weights"
-                                   % d["local_weight_gb_per_step"]),
+                    dtype="bf16", data="synthetic", config=config,
+                    execution=(f"expert parallel, {el} experts per GPU, dispatch/combine exchange over NVLink, "
+                               f"one CUDA graph per step"),
                     roofline=dict(bound="hbm", kernel="whole expert-parallel decode step (local expert weights "
                                                       "per step / step time, per GPU)",
                                   achieved=d["hbm_gbs_step_per_gpu"], peak=pk["hbm_gbs"], unit="GB/s",
@@ -760,8 +794,8 @@ def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
                              ms_per_step=e2e_ms / K),
                     clocks=clocks, gpu_launches=d["launches_per_step"] * K,
                     decode={str(t): r for t, r in decode.items()}, prefill=prefill)
-        line["config"]["exchange"] = ("NVLink peer stores + flags (pdx_ep_*_p2p)" if peer is not None
-                                      else "NCCL all-to-all")
+        line["exchange"] = ("NVLink peer stores + flags (pdx_ep_*_p2p)" if peer is not None
+                            else "NCCL all-to-all")
         print(json.dumps(line), flush=True)
     stack.release_graphs()
     if peer is not None:

@@ -129,7 +129,8 @@ int pdx_pack(const int64_t *selected, const void *weights, int64_t T, int32_t to
  * return PDX_ERR_UNSUPPORTED.  All calls share that array: calls whose kernels
  * overlap on the GPU race.  The first call on a device resolves the array's
  * device address (cudaGetSymbolAddress) with that device current; make it
- * before any stream capture. */
+ * before any stream capture.  The address is kept for the life of the
+ * process's primary context on that device (not across cudaDeviceReset). */
 #define PDX_PACK_STATIC_MAX_HIST_INTS 65536
 int pdx_pack_static(const int64_t *selected, const void *weights, int64_t T, int32_t top_k,
                     int64_t E, int32_t *counts, int32_t *offsets, int32_t *tokens,
@@ -358,6 +359,14 @@ int pdx_ep_return_p2p(const void *grouped, const int32_t *perm, const int32_t *o
                       int64_t rows_cap, int64_t H, int32_t ranks, int32_t rank, int64_t capacity,
                       const pdx_p2p_layer *layer, pdx_stream_t stream);
 int pdx_ep_wait_back(int32_t ranks, int32_t rank, const pdx_p2p_layer *layer, pdx_stream_t stream);
+
+/* Wall-time limit of the two flag waits above, in ns (0 = the default 2 s;
+ * at most 60 s), for launches made after the call (a captured graph keeps the
+ * limit it was captured with).  A wait that runs out raises
+ * PDX_DEVERR_WAIT_TIMEOUT, leaves the layout empty and returns.  No
+ * counterpart in the reference, which has no multi-GPU path; the analogue
+ * there is the run guard's deadline (benchmarks/pdscope_compare.py:153-161). */
+int pdx_set_flag_wait_limit_ns(uint64_t ns);
 
 /* Synchronise `stream`, then read and clear this device's error word.
  * *code_out receives a PDX_DEVERR_* value; returns PDX_ERR_DEVICE if nonzero. */

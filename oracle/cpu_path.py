@@ -75,6 +75,22 @@ def make_layer(hidden, experts, inter, seed):
     return gate, ex
 
 
+def stack_step(x, layers, num_layers, top_k=8, normalize=True):
+    """One step of a ``num_layers``-deep stack on the CPU: layer l uses
+    ``layers[l % len(layers)]`` and the next activation is formed as the
+    reference's two-layer protocol does (benchmarks/pdscope_compare.py:609-705,
+    ``x = F.layer_norm(out.float() + x.float(), (H,)).to(bf16)``).  Returns the
+    last activation and the active experts of every layer."""
+    active = []
+    with torch.inference_mode():
+        for l in range(num_layers):
+            gate, ex = layers[l % len(layers)]
+            out, n_active = layer_forward(x, gate, ex, top_k, normalize)
+            active.append(n_active)
+            x = F.layer_norm(out.float() + x.float(), (x.shape[1],)).to(torch.bfloat16)
+    return x, active
+
+
 def time_layers(layers, tokens, hidden, threads, repeats=1, seed=7):
     """Seconds per layer (mean) and active experts per layer for a token batch."""
     torch.set_num_threads(threads)

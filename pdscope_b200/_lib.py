@@ -114,6 +114,7 @@ SIGNATURES = {
     "pdx_ep_return_p2p": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_i32, c_i64,
                                          ctypes.POINTER(P2PLayer), c_vp]),
     "pdx_ep_wait_back": (ctypes.c_int, [c_i32, c_i32, ctypes.POINTER(P2PLayer), c_vp]),
+    "pdx_set_flag_wait_limit_ns": (ctypes.c_int, [ctypes.c_uint64]),
     "pdx_offload_pool_bytes": (c_sz, [ctypes.POINTER(OffloadConfig)]),
     "pdx_offload_workspace_bytes": (c_sz, [ctypes.POINTER(OffloadConfig)]),
     "pdx_offload_create": (ctypes.c_int, [ctypes.POINTER(OffloadConfig), c_vp, c_vp, c_sz, ctypes.POINTER(c_vp)]),

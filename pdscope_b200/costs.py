@@ -6,9 +6,15 @@ per-expert completion times by routed token count, read by ``FileCosts``
 measured on an A100 PCIe).  This module measures the same three columns on a
 B200 so the policy makes B200-appropriate decisions unchanged:
 
-* ``gpu_ms``  one resident expert through ``pdx_expert_ffn`` (the sm_100a
-              kernels behind the executor's gpu_backend hook), CUDA events on
-              the launching stream, median of repeats;
+* ``gpu_ms``  what one more resident expert with n routed rows adds to a
+              layer on the B200: one grouped FFN launch (``pdx_moe_ffn_grouped``,
+              row gather + the tcgen05 GEMMs) over G experts of n rows each,
+              divided by G.  The reference runs one cuBLAS chain per expert, so
+              its per-expert time is a whole launch; here experts share one
+              launch and each costs its weight stream (about 1.5 us at one
+              token) or its tensor-core time.  The time of a lone single-expert
+              launch (``pdx_expert_ffn``, the gpu_backend hook) is kept as
+              ``gpu_single_launch_ms``;
 * ``h2d_ms``  one expert's 9 MiB gate|up|down slot from pinned host memory on
               a dedicated copy stream (the executor's load path, executor.py:333-372);
 * ``cpu_ms``  the reference's CPU expert path without kt (``ExpertExecutor.cpu``
@@ -16,18 +22,50 @@ B200 so the policy makes B200-appropriate decisions unchanged:
               executor.py:513-530), on all host cores.
 
     python -m pdscope_b200.costs --out pdscope_b200/cost_table_b200.json
+
+``TableCosts`` reads a table as FileCosts does (exact points, linear
+interpolation inside the 1..4096 domain) for callers without the
+reference's harness module.
 """
 from __future__ import annotations
 
 import argparse
+import bisect
+import ctypes
 import json
 import os
 import statistics
 import time
+from pathlib import Path
 
 import torch
 
 LOADS = (1, 4, 16, 64, 128, 256, 1024, 4096)   # FileCosts requires the 1..4096 domain
+DEFAULT_TABLE = Path(__file__).resolve().parent / "cost_table_b200.json"
+
+
+class TableCosts:
+    """``for_load(n)`` over a pdscope_cost_table file, as FileCosts computes it
+    (benchmarks/pdscope_compare.py:55-85): the measured point at n, else the
+    linear interpolation between the two measured loads around n; loads
+    outside the measured domain raise ValueError."""
+
+    def __init__(self, path=DEFAULT_TABLE):
+        payload = json.loads(Path(path).read_text())
+        self.loads = validate(payload)
+        self.points = {int(n): {k: float(v) for k, v in p.items()} for n, p in payload["points"].items()}
+        self.path = str(path)
+
+    def for_load(self, n):
+        if not self.loads[0] <= n <= self.loads[-1]:
+            raise ValueError("expert load outside the measured domain")
+        if n in self.points:
+            return dict(tokens=n, **self.points[n])
+        hi = bisect.bisect_left(self.loads, n)
+        lo, up = self.loads[hi - 1], self.loads[hi]
+        r = (n - lo) / (up - lo)
+        return dict(tokens=n, **{k: self.points[lo][k] + r * (self.points[up][k] - self.points[lo][k])
+                                 for k in self.points[lo]})
 
 
 def _median_ms(fn, repeats, stream):
@@ -42,14 +80,39 @@ def _median_ms(fn, repeats, stream):
     return statistics.median(times)
 
 
+def _grouped_ms_per_expert(n, hidden, inter, experts, repeats, dev, gen, slab):
+    """One grouped FFN launch over ``experts`` experts with n rows each (the
+    layer's gather + GEMMs), its median time divided by the expert count."""
+    from . import _lib
+    rows = n * experts
+    x = torch.randn((rows, hidden), device=dev, generator=gen).to(torch.bfloat16)
+    tokens = torch.arange(rows, dtype=torch.int32, device=dev)
+    offsets = (torch.arange(experts + 1, dtype=torch.int32, device=dev) * n).contiguous()
+    active = torch.cat([torch.tensor([experts], dtype=torch.int32),
+                        torch.arange(experts, dtype=torch.int32)]).to(dev)
+    y = torch.empty((rows, hidden), dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(_lib.lib.pdx_ffn_workspace_bytes(rows, experts, hidden, inter, _lib.FFN_AUTO),
+                     dtype=torch.uint8, device=dev)
+    comp = torch.cuda.current_stream(dev)
+    s = ctypes.c_void_p(comp.cuda_stream)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())
+
+    def launch():
+        _lib.check(_lib.lib.pdx_moe_ffn_grouped(p(x), rows, p(tokens), p(offsets), p(active), experts, rows,
+                                                ctypes.byref(slab.struct), hidden, inter, p(y), _lib.FFN_AUTO,
+                                                p(ws), ws.numel(), s))
+    for _ in range(3):
+        launch()
+    return _median_ms(launch, repeats, comp) / experts
+
+
 def calibrate(device="cuda", hidden=2048, inter=768, loads=LOADS, repeats=20, cpu_threads=0, cpu_repeats=2,
-              seed=0):
-    from .runtime import expert_forward
+              seed=0, experts=128):
+    from .runtime import ExpertSlab, expert_forward
     dev = torch.device(device)
     gen = torch.Generator(device=dev).manual_seed(seed)
-    w = {name: (torch.randn(shape, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
-         for name, shape in (("gate_proj", (inter, hidden)), ("up_proj", (inter, hidden)),
-                             ("down_proj", (hidden, inter)))}
+    slab = ExpertSlab.allocate(experts, hidden, inter, dev, generator=gen)
+    w = slab.expert_tensors(0)
     w_cpu = {k: v.cpu() for k, v in w.items()}
     slot_bytes = 3 * hidden * inter * 2
     host = torch.empty(slot_bytes, dtype=torch.uint8).pin_memory()
@@ -71,11 +134,12 @@ def calibrate(device="cuda", hidden=2048, inter=768, loads=LOADS, repeats=20, cp
         x = torch.randn((n, hidden), device=dev, generator=gen).to(torch.bfloat16)
         for _ in range(3):
             expert_forward(x, w)
-        gpu_ms = _median_ms(lambda: expert_forward(x, w), repeats, comp)
-        dev_ms[n] = (x, gpu_ms, _median_ms(h2d, repeats, copy_stream))
+        single = _median_ms(lambda: expert_forward(x, w), repeats, comp)
+        grouped = _grouped_ms_per_expert(n, hidden, inter, experts, max(5, repeats // 2), dev, gen, slab)
+        dev_ms[n] = (x, grouped, single, _median_ms(h2d, repeats, copy_stream))
     points = {}
     for n in loads:
-        x, gpu_ms, h2d_ms = dev_ms[n]
+        x, grouped, single, h2d_ms = dev_ms[n]
         xc = x.cpu()
         g, u, d = w_cpu["gate_proj"], w_cpu["up_proj"], w_cpu["down_proj"]
 
@@ -88,8 +152,8 @@ def calibrate(device="cuda", hidden=2048, inter=768, loads=LOADS, repeats=20, cp
             t0 = time.perf_counter()
             cpu_expert()
             ct.append((time.perf_counter() - t0) * 1e3)
-        points[str(n)] = dict(cpu_ms=round(statistics.median(ct), 6), gpu_ms=round(gpu_ms, 6),
-                              h2d_ms=round(h2d_ms, 6))
+        points[str(n)] = dict(cpu_ms=round(statistics.median(ct), 6), gpu_ms=round(grouped, 6),
+                              h2d_ms=round(h2d_ms, 6), gpu_single_launch_ms=round(single, 6))
     props = torch.cuda.get_device_properties(dev)
     try:
         cpu_model = next((l.split(":", 1)[1].strip() for l in open("/proc/cpuinfo") if l.startswith("model name")),
@@ -102,12 +166,14 @@ def calibrate(device="cuda", hidden=2048, inter=768, loads=LOADS, repeats=20, cp
         "model": f"Qwen3-30B-A3B-shape expert (H={hidden}, I={inter}) BF16, random-init weights",
         "platform": f"{props.name} ({props.multi_processor_count} SMs) + {cpu_model}",
         "native_operator": "none: cpu_ms is torch CPU expert_forward (the cpu_backend=None path); "
-                           "gpu_ms is pdx_expert_ffn (sm_100a tcgen05 kernels)",
+                           f"gpu_ms is one grouped pdx_moe_ffn_grouped launch over {experts} experts divided by "
+                           f"{experts} (sm_100a tcgen05 kernels); gpu_single_launch_ms is pdx_expert_ffn alone",
         "workers": threads,
         "loads": list(loads),
         "points": points,
-        "scope": "per-expert completion time by routed token count: CPU torch, resident GPU (libpdx_moe), "
-                 "pinned host->device copy of one 9 MiB expert slot on a copy stream",
+        "scope": "per-expert completion time by routed token count: CPU torch, resident GPU (libpdx_moe, "
+                 "marginal per expert in a grouped launch), pinned host->device copy of one 9 MiB expert slot "
+                 "on a copy stream",
     }
 
 

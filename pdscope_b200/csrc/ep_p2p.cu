@@ -14,9 +14,9 @@
 // rank has finished step n, so no block is rewritten while being read.  The
 // step number of the layer is a local counter, advanced by the last kernel of
 // the layer (k_ep_wait_back), so the graph of a decode step replays unchanged.
-// Waits are bounded (kWaitLimitNs); on a timeout the error word is raised and
-// the layout is left empty, so nothing downstream reads or writes outside its
-// buffers.  Every TMA-free, plain st/ld over NVLink; no cluster or multicast
+// Waits are bounded (2 s unless pdx_set_flag_wait_limit_ns sets another
+// limit); on a timeout the error word is raised and the layout is left empty,
+// so nothing downstream reads or writes outside its buffers.  Every TMA-free, plain st/ld over NVLink; no cluster or multicast
 // operation is involved.
 #include "pdx_common.cuh"
 
@@ -45,15 +45,16 @@ struct P2PLayer {
 };
 
 // Bounded wait until every flag[s] (s < R) reaches `want`; one CTA.  Returns
-// false (and raises the error word) on a timeout.
-__device__ bool wait_flags(const unsigned long long* flags, int R, unsigned long long want) {
+// false (and raises the error word) after `limit_ns` of wall time.
+__device__ bool wait_flags(const unsigned long long* flags, int R, unsigned long long want,
+                           unsigned long long limit_ns) {
     __shared__ int s_bad;
     if (threadIdx.x == 0) s_bad = 0;
     __syncthreads();
     if (static_cast<int>(threadIdx.x) < R) {
         const unsigned long long t0 = global_timer_ns();
         while (ld_acquire_sys(flags + threadIdx.x) < want) {
-            if (global_timer_ns() - t0 > kWaitLimitNs) {
+            if (global_timer_ns() - t0 > limit_ns) {
                 raise_error(PDX_DEVERR_WAIT_TIMEOUT);
                 s_bad = 1;
                 break;
@@ -132,10 +133,11 @@ __global__ void __launch_bounds__(256) k_ep_dispatch_p2p(const uint16_t* __restr
 // out by local expert exactly as k_ep_layout (block s at s*C).  One CTA.
 __global__ void __launch_bounds__(1024) k_ep_layout_p2p(int R, int EL, int64_t C, int rows_cap, P2PLayer lay, int me,
                                                         int32_t* __restrict__ offsets_l,
-                                                        int32_t* __restrict__ active_l, int32_t* __restrict__ perm) {
+                                                        int32_t* __restrict__ active_l, int32_t* __restrict__ perm,
+                                                        unsigned long long limit_ns) {
     griddep_wait();
     const unsigned long long step = *lay.step + 1ull;
-    const bool ok = wait_flags(reinterpret_cast<const unsigned long long*>(lay.rflag[me]), R, step);
+    const bool ok = wait_flags(reinterpret_cast<const unsigned long long*>(lay.rflag[me]), R, step, limit_ns);
     __shared__ int s_cnt[kEpMaxExperts];
     __shared__ int s_blk[kEpMaxExperts];
     __shared__ int s_grp[kEpMaxExperts];
@@ -229,10 +231,10 @@ __global__ void __launch_bounds__(256) k_ep_return_p2p(const uint16_t* __restric
 // Waits for every rank's returned block of this layer, then closes the layer
 // (advances its step counter).  One CTA; the combine that follows reads the
 // back blocks.
-__global__ void __launch_bounds__(32) k_ep_wait_back(int R, int me, P2PLayer lay) {
+__global__ void __launch_bounds__(32) k_ep_wait_back(int R, int me, P2PLayer lay, unsigned long long limit_ns) {
     griddep_wait();
     const unsigned long long step = *lay.step + 1ull;
-    wait_flags(reinterpret_cast<const unsigned long long*>(lay.bflag[me]), R, step);
+    wait_flags(reinterpret_cast<const unsigned long long*>(lay.bflag[me]), R, step, limit_ns);
     __syncthreads();
     if (threadIdx.x == 0) *lay.step = step;
 }

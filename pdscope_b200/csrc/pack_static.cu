@@ -28,7 +28,9 @@ namespace {
 // Device address of g_pack_static_hist, resolved once per device.  In host
 // code the array's name is only a stand-in for the symbol, never a pointer a
 // kernel may use, so the address comes from cudaGetSymbolAddress with the
-// device current.
+// device current.  The cached address lives as long as the process's primary
+// context of that device: after cudaDeviceReset (or any teardown of that
+// context) the library must not be called on the device again.
 int* g_pack_static_ptr[kMaxDevices] = {nullptr};
 std::mutex g_pack_static_mutex;
 

@@ -28,6 +28,10 @@ namespace {
 
 thread_local std::string t_last_error;
 std::atomic<uint64_t> g_launches{0};
+// Wall-time limit of the peer-exchange flag waits (k_ep_layout_p2p,
+// k_ep_wait_back), read when those kernels are launched (or captured).
+constexpr uint64_t kMaxFlagWaitNs = 60000000000ull;  // 60 s
+std::atomic<uint64_t> g_flag_wait_ns{kWaitLimitNs};
 
 int fail(int status, const char* fmt, ...) {
     char buf[512];
@@ -358,6 +362,14 @@ int launch_route(const void* x, const void* gate, int64_t T, int64_t H, int64_t 
         tail.do_pack = 1;
         tail.pack = *fused_pack;
         smem = static_cast<size_t>(E + E + 1 + (kRouteWarps * E)) * sizeof(int);
+    }
+    if (false && T <= kSmallRouteT && H <= 64 * 1024) {
+        // decode sizes: one CTA per expert
+        k_router_small<<<static_cast<unsigned>(E), kSmallRouteThreads, smem, stream>>>(
+            static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gate), static_cast<int>(T),
+            static_cast<int>(H), static_cast<int>(E), b.logits, tail);
+        PDX_LAUNCHED();
+        return PDX_OK;
     }
     k_router_logits<<<n_tb * n_eb, kRouteWarps * 32, smem, stream>>>(
         static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gate), static_cast<int>(T), static_cast<int>(H),
@@ -1033,7 +1045,7 @@ int pdx_ep_layout_p2p(int32_t ranks, int32_t rank, int64_t local_experts, int64_
                     pdx::kEpMaxExperts);
     pdx::k_ep_layout_p2p<<<1, 1024, 0, stream>>>(ranks, static_cast<int>(local_experts), capacity,
                                                  static_cast<int>(rows_cap), to_p2p(layer), rank, offsets_l,
-                                                 active_l, perm);
+                                                 active_l, perm, g_flag_wait_ns.load());
     PDX_LAUNCHED();
     return ok();
 }
@@ -1059,8 +1071,16 @@ int pdx_ep_return_p2p(const void* grouped, const int32_t* perm, const int32_t* o
 int pdx_ep_wait_back(int32_t ranks, int32_t rank, const pdx_p2p_layer* layer, pdx_stream_t stream) {
     int st = check_p2p(layer, ranks, rank);
     if (st) return st;
-    pdx::k_ep_wait_back<<<1, 32, 0, stream>>>(ranks, rank, to_p2p(layer));
+    pdx::k_ep_wait_back<<<1, 32, 0, stream>>>(ranks, rank, to_p2p(layer), g_flag_wait_ns.load());
     PDX_LAUNCHED();
+    return ok();
+}
+
+int pdx_set_flag_wait_limit_ns(uint64_t ns) {
+    if (ns == 0) ns = kWaitLimitNs;
+    if (ns > kMaxFlagWaitNs) return fail(PDX_ERR_INVALID, "flag wait limit above %llu ns",
+                                         static_cast<unsigned long long>(kMaxFlagWaitNs));
+    g_flag_wait_ns.store(ns);
     return ok();
 }
 

@@ -132,6 +132,88 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_router_logits(const uint16
     block_pack_all(tail.selected, tail.weights, T, tail.k, E, hist, excl, warp_hist, tail.pack);
 }
 
+// Decode-size router (T <= kSmallRouteT): one CTA per expert, so the 512 KiB
+// of gate rows is read by E CTAs at once instead of E/8.  Thread i takes the
+// 8-element K chunks i, i+256, ... of the expert's gate row and of every
+// token's row and accumulates the exact products in FP64; each token's sum is
+// reduced over the CTA in a fixed order (xor butterfly inside warps, warps in
+// order) and rounded once to BF16, as k_router_logits.  The fused tail is the
+// same: the CTA that writes the last expert's logits routes every token (one
+// warp per token) and, with do_pack, packs them.
+constexpr int kSmallRouteT = 16;
+constexpr int kSmallRouteThreads = 256;
+
+__global__ void __launch_bounds__(kSmallRouteThreads) k_router_small(const uint16_t* __restrict__ x,
+                                                                     const uint16_t* __restrict__ gate, int T,
+                                                                     int H, int E, uint16_t* __restrict__ logits,
+                                                                     RouteTail tail) {
+    constexpr int kWarps = kSmallRouteThreads / 32;
+    __shared__ double s_part[kWarps][kSmallRouteT];
+    const int warp = static_cast<int>(threadIdx.x >> 5);
+    const int lane = static_cast<int>(lane_id());
+    const int e = static_cast<int>(blockIdx.x);
+    griddep_wait();
+    double acc[kSmallRouteT];
+#pragma unroll
+    for (int t = 0; t < kSmallRouteT; ++t) acc[t] = 0.0;
+    const uint16_t* grow = gate + static_cast<size_t>(e) * H;
+    for (int k0 = static_cast<int>(threadIdx.x) * 8; k0 < H; k0 += kSmallRouteThreads * 8) {
+        const uint4 gv = __ldg(reinterpret_cast<const uint4*>(grow + k0));
+        double gd[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const uint32_t w = (&gv.x)[q >> 1];
+            gd[q] = bits_to_f64((q & 1) ? (w >> 16) : (w & 0xFFFFu));
+        }
+#pragma unroll
+        for (int t = 0; t < kSmallRouteT; ++t) {
+            if (t < T) {
+                const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * H + k0));
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const uint32_t w = (&xv.x)[q >> 1];
+                    acc[t] = fma(bits_to_f64((q & 1) ? (w >> 16) : (w & 0xFFFFu)), gd[q], acc[t]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < kSmallRouteT; ++t) {
+        if (t < T) {
+            double v = acc[t];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            if (lane == 0) s_part[warp][t] = v;
+        }
+    }
+    __syncthreads();
+    if (static_cast<int>(threadIdx.x) < T) {
+        const int t = static_cast<int>(threadIdx.x);
+        double sum = s_part[0][t];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) sum += s_part[w][t];
+        logits[static_cast<size_t>(t) * E + e] = f64_to_bf16_bits(sum);
+    }
+    if (!tail.enabled) return;
+    __shared__ unsigned int s_ticket;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_ticket = atomicAdd(&tail.tickets[1], 1u);
+    __syncthreads();
+    if (s_ticket != static_cast<unsigned int>(E - 1)) return;
+    __threadfence();
+    for (int t = warp; t < T; t += kWarps) topk_row(logits, t, E, tail.k, tail.normalize != 0, tail.selected,
+                                                     tail.weights);
+    if (!tail.do_pack) return;
+    __threadfence();
+    __syncthreads();
+    extern __shared__ int smem_small[];
+    int* hist = smem_small;
+    int* excl = hist + E;
+    int* warp_hist = excl + E + 1;
+    block_pack_all(tail.selected, tail.weights, T, tail.k, E, hist, excl, warp_hist, tail.pack);
+}
+
 // Prefill-size router on the FP64 tensor path (mma.sync m8n8k4 .f64; tcgen05
 // has no FP64 kind): exact BF16 products summed in FP64, as k_router_logits,
 // with each warp instruction doing 256 FMAs (8x8x4) from register fragments.  The FP64

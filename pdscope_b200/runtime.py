@@ -10,7 +10,8 @@ Same names, argument meaning and error behaviour as the reference
 * ``PdxGpuBackend``                 the ExpertExecutor.gpu_backend hook,
                                     expertbench/executor.py:178, 476-477
 * ``PDScopeCudaRuntime.forward``    expertbench/pdscope_runtime.py:208-512
-                                    (HBM-resident experts)
+                                    (HBM-resident experts; AdaptSched's
+                                    plan_pdscope decides the placement)
 
 Tensors are torch CUDA tensors (BF16 activations and weights); torch is used
 for device memory and streams only.  Kernels run on the caller's current
@@ -20,6 +21,7 @@ from __future__ import annotations
 
 import ctypes
 import hashlib
+from collections import Counter
 from dataclasses import dataclass
 
 import torch
@@ -422,31 +424,125 @@ def tensor_hash(tensor):
     return hashlib.sha256(tensor.detach().cpu().contiguous().view(torch.uint8).numpy().tobytes()).hexdigest()
 
 
+@dataclass(frozen=True)
+class ExpertKey:
+    """Expert identity handed to CPU backends; the fields of the reference's
+    ``ExpertKey`` (expertbench/cache.py:32-35)."""
+    layer: int
+    expert: int
+    representation: str = "bf16"
+
+
+def _reference_planner():
+    """AdaptSched's ``plan_pdscope`` (expertbench/pdscope_policy.py:72) when the
+    reference package is importable in this process, else None."""
+    try:
+        from expertbench.pdscope_policy import plan_pdscope
+    except ImportError:
+        return None
+    return plan_pdscope
+
+
 class PDScopeCudaRuntime:
     """Layer-level drop-in for ``PDScopeCudaRuntime.forward`` with HBM-resident experts.
 
     ``layers`` maps layer index -> ExpertSlab (slot e = expert e, or an
-    explicit ``slot_of_expert``).  ``forward`` keeps the reference signature
-    and return value ``(output, Routing, row)``; ``row`` carries the keys the
-    reference harness reads (pdscope_compare.py:412-420).  With every expert
-    resident the placement decision is all-GPU: no CPU queue, no demand
-    staging, no prefetch.
+    explicit ``slot_of_expert``).  ``forward`` keeps the reference's signature,
+    checks and return value ``(output, Routing, row)``
+    (expertbench/pdscope_runtime.py:208-512); ``row`` carries the keys the
+    reference harness reads (benchmarks/pdscope_compare.py:412-420).
+
+    Placement follows the reference: every layer asks the AdaptSched planner
+    ``plan`` (the signature of ``plan_pdscope``, pdscope_policy.py:72) with the
+    arguments the reference passes (pdscope_runtime.py:270-280) -- this
+    layer's routed counts, the next layer's predicted counts (the next gate
+    on the current activation, :245-248, when ``prefetch`` and ``next_gate``
+    are given), the resident ids, the cost table ``costs`` (``for_load(n)``,
+    e.g. FileCosts over pdscope_b200/cost_table_b200.json) -- and executes
+    its decision: ``gpu_resident_queue`` in one grouped FFN launch, the
+    ``cpu_queue`` experts through ``cpu_backend(key, rows)`` (the reference's
+    CPU backend duck type, executor.py:513-530) or, without one, the torch
+    CPU ``expert_forward`` over ``masters[layer][e]`` (gate, up, down host
+    tensors), their rows uploaded into their packed places before the merge.
+    With every expert resident the planner has nothing to demand-load or
+    prefetch; a decision that asks for either is rejected.  ``plan=None``
+    uses the reference's ``plan_pdscope`` if it is importable, otherwise the
+    all-GPU decision (row ``planner`` says which).  ``merge`` 'fused' and
+    'reference' both run the deterministic slot-order combine (the reference
+    documents the two as the same math in a different accumulation order,
+    :456-459).
     """
 
     def __init__(self, layers, *, top_k=8, merge="fused", dispatch="compact", demand_slots=2,
-                 input_pregather=False, graph_output_pool=False, diagnostics=True):
+                 input_pregather=False, graph_output_pool=False, diagnostics=True, plan=None, costs=None,
+                 decode_costs=None, cpu_backend=None, masters=None, speculative_slots=0, decode_cpu_target=None):
         if merge not in ("reference", "fused"):
             raise ValueError("invalid merge mode")
         if dispatch not in ("reference", "compact"):
             raise ValueError("invalid dispatch mode")
         if type(demand_slots) is not int or demand_slots not in (2, 3, 4):
             raise ValueError("invalid demand staging depth")
+        if type(speculative_slots) is not int or not 0 <= speculative_slots <= 128:
+            raise ValueError("invalid PDScope cache contract")
+        if cpu_backend is not None and not callable(cpu_backend):
+            raise ValueError("CPU backend must be an explicit synchronous callable")
+        if (decode_cpu_target is not None
+                and (type(decode_cpu_target) is not int or not 0 <= decode_cpu_target <= 8)):
+            raise ValueError("invalid decode CPU balance target")
         self.layers = dict(layers)
         self.top_k = top_k
         self.merge, self.dispatch, self.demand_slots = merge, dispatch, demand_slots
         self.input_pregather, self.graph_output_pool = bool(input_pregather), bool(graph_output_pool)
         self.diagnostics = diagnostics
+        self.plan = plan if plan is not None else _reference_planner()
+        self.planner_name = ("plan_pdscope" if plan is None and self.plan is not None else
+                             getattr(plan, "__name__", "caller planner") if plan is not None else "none")
+        if self.plan is not None and costs is None:
+            from .costs import TableCosts
+            costs = TableCosts()
+        self.costs = costs
+        self.decode_costs = decode_costs if decode_costs is not None else costs
+        self.cpu_backend, self.masters = cpu_backend, masters
+        self.speculative_slots = speculative_slots
+        self.decode_cpu_target = decode_cpu_target
+        self.forecasts = {}
+        self.prediction_counts = {phase: dict(hits=0, total=0) for phase in ("prefill", "decode")}
         self.forwards = 0
+        self.completed = dict(gpu_completed_experts=0, cpu_completed_experts=0)
+
+    def _decision(self, counts, next_counts, *, layer, phase, top_k, attention_ms, hit_rate):
+        resident = list(counts)                 # every expert of every layer is resident in HBM
+        next_resident = list(next_counts)
+        if self.plan is None:
+            gpu = sorted(counts, key=lambda e: (-counts[e], e))
+            return dict(phase=phase, mode="all_resident", cpu_queue=[], gpu_resident_queue=gpu,
+                        on_demand_queue=[], prefetch_queue=[], unload_queue=[],
+                        placements={e: "gpu" for e in sorted(counts)})
+        return self.plan(counts, next_counts, current_layer=layer, phase=phase, current_gpu_ids=resident,
+                         next_gpu_ids=next_resident,
+                         costs=self.decode_costs if phase == "decode" else self.costs,
+                         attention_ms=attention_ms, hit_rate=hit_rate, prefetch_slots=self.speculative_slots,
+                         top_k=top_k,
+                         cpu_balance_target_override=(self.decode_cpu_target if phase == "decode" else None),
+                         joint_next=True, record_checks=False, trusted=True,
+                         compute_formula_target=(self.decode_cpu_target is None))
+
+    def _cpu_expert(self, layer, e, rows):
+        key = ExpertKey(layer, e)
+        if self.cpu_backend is not None:
+            out = self.cpu_backend(key, rows)
+        elif self.masters is not None:
+            g, u, d = self.masters[layer][e]
+            with torch.inference_mode():
+                out = torch.nn.functional.linear(torch.nn.functional.silu(torch.nn.functional.linear(rows, g))
+                                                 * torch.nn.functional.linear(rows, u), d)
+        else:
+            raise ValueError("the decision places experts on the CPU but neither a CPU backend nor host "
+                             "master weights were given")
+        if (not isinstance(out, torch.Tensor) or out.device.type != "cpu" or out.dtype != torch.bfloat16
+                or out.shape != rows.shape):
+            raise ValueError("CPU backend must return completed unweighted CPU BF16 input-shaped output")
+        return out
 
     def forward(self, inputs, gate, *, layer, step, request="pdscope", next_gate=None, top_k=8, normalize=True,
                 attention_ms=0., prefetch=True):
@@ -455,22 +551,69 @@ class PDScopeCudaRuntime:
             raise ValueError("invalid prefill/decode activation or layer")
         phase = "prefill" if step == 0 else "decode"
         slab = self.layers[layer]
-        moe = ResidentMoELayer(gate, slab, top_k=top_k, normalize=normalize)
-        res = moe.forward(inputs)
-        routing = Routing(res.logits, res.selected, res.weights)
-        counts_list = res.counts.cpu().tolist()  # synchronises, as the reference's grouping does
+        _require_cuda_bf16("inputs", inputs, 2)
+        experts, hidden = gate.shape
+        t_count = inputs.shape[0]
+        dev = inputs.device
+        routing = route(inputs, gate, top_k, normalize)
+        p = pack(routing.selected, routing.weights, experts)
+        offsets = p.offsets.cpu()                # synchronises, as the reference's grouping does (:26)
         raise_device_error()
-        counts = {e: n for e, n in enumerate(counts_list) if n}
-        if sum(counts.values()) != inputs.shape[0] * top_k:
+        counts = {e: int(offsets[e + 1] - offsets[e]) for e in range(experts) if offsets[e + 1] > offsets[e]}
+        prior = self.forecasts.pop((request, step, layer), None)
+        if prior:
+            self.prediction_counts[phase]["hits"] += len(set(prior) & set(counts))
+            self.prediction_counts[phase]["total"] += len(prior)
+        observed = self.prediction_counts[phase]
+        hit_rate = observed["hits"] / observed["total"] if observed["total"] else 0.
+        next_routing, next_counts = None, {}
+        if prefetch and next_gate is not None:
+            # layer-local ids of the TARGET gate on the CURRENT activation (:245-248)
+            next_routing = route(inputs, next_gate, top_k, normalize)
+            next_counts = dict(Counter(next_routing.selected.cpu().flatten().tolist()))
+        decision = self._decision(counts, next_counts, layer=layer, phase=phase, top_k=top_k,
+                                  attention_ms=attention_ms, hit_rate=hit_rate)
+        if decision["on_demand_queue"] or decision["prefetch_queue"]:
+            raise AssertionError("every expert is resident: nothing can be demand-loaded or prefetched")
+        gpu_ids = sorted(decision["gpu_resident_queue"])
+        cpu_ids = sorted(decision["cpu_queue"])
+        if set(gpu_ids) & set(cpu_ids) or set(gpu_ids) | set(cpu_ids) != set(counts):
+            raise AssertionError("demand partition failed")
+        rows_total = t_count * top_k
+        y = torch.empty((rows_total, hidden), dtype=torch.bfloat16, device=dev)
+        if gpu_ids:
+            active = torch.zeros(experts + 1, dtype=torch.int32)
+            active[0] = len(gpu_ids)
+            active[1:1 + len(gpu_ids)] = torch.tensor(gpu_ids, dtype=torch.int32)
+            active = active.to(dev, non_blocking=True)
+            ws = _WS.get(dev, lib.pdx_ffn_workspace_bytes(rows_total, experts, hidden, slab.inter, _lib.FFN_AUTO),
+                         "ffn")
+            check(lib.pdx_moe_ffn_grouped(_ptr(inputs), t_count, _ptr(p.tokens), _ptr(p.offsets), _ptr(active),
+                                          experts, rows_total, ctypes.byref(slab.struct), hidden, slab.inter,
+                                          _ptr(y), _lib.FFN_AUTO, _ptr(ws), ws.numel(), _stream()))
+        if cpu_ids:
+            tokens_cpu = p.tokens.cpu().long()
+            x_cpu = inputs.cpu()
+            for e in cpu_ids:
+                a, b = int(offsets[e]), int(offsets[e + 1])
+                y[a:b].copy_(self._cpu_expert(layer, e, x_cpu[tokens_cpu[a:b]]))
+        out = combine(y, routing.weights, p.inverse)
+        raise_device_error()
+        self.completed["gpu_completed_experts"] += len(gpu_ids)
+        self.completed["cpu_completed_experts"] += len(cpu_ids)
+        if len(gpu_ids) + len(cpu_ids) != len(counts) or sum(counts.values()) != rows_total:
             raise AssertionError("lost or duplicated routed expert")
         self.forwards += 1
-        resident = sorted(counts)
-        decision = dict(mode="gpu_resident", phase=phase, cpu_queue=[], gpu_resident_queue=resident,
-                        on_demand_queue=[], prefetch_queue=[], placements={e: "gpu" for e in resident})
         row = dict(phase=phase, step=step, layer=layer, token_counts=counts, dispatch=self.dispatch,
-                   decision=decision, prefetch_issued=[], prefetch_capacity_skipped=[],
+                   decision=decision, planner=self.planner_name, prefetch_issued=[], prefetch_capacity_skipped=[],
+                   next_prediction_counts=next_counts, causal_hit_counts=dict(observed),
+                   predictor="next_layer_gate_on_current_activation",
                    merge_mode=self.merge, input_pregather=self.input_pregather,
                    demand_slots=self.demand_slots, graph_output_pool=self.graph_output_pool,
-                   selected_sha256=tensor_hash(res.selected) if self.diagnostics else None,
+                   ping_pong_slots=[], counters=dict(gpu_completed_experts=len(gpu_ids),
+                                                     cpu_completed_experts=len(cpu_ids)),
+                   selected_sha256=tensor_hash(routing.selected) if self.diagnostics else None,
+                   next_selected_sha256=(tensor_hash(next_routing.selected)
+                                         if self.diagnostics and next_routing is not None else None),
                    backend="pdx_moe sm_100a", measured_performance=False)
-        return res.out, routing, row
+        return out, routing, row

@@ -179,6 +179,55 @@ def test_expert_parallel_gloo(world, tokens, mode):
     assert results == {r: True for r in range(world)}, results
 
 
+def _lost_rank_worker(rank, world, port, q):
+    """Rank 1 serves layer 0 and then leaves (between layers, before layer 1's
+    count exchange, with nothing of its own in flight); rank 0 goes on to
+    layer 1 and must get an error from the exchange, not wait forever."""
+    import datetime
+    import time
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    from pdscope_b200.expert_parallel import ExpertParallelMoE, TorchDistExchange
+    _, gate, wg, wu, wd = mo.synthetic_layer(31, 1, H, E, I)
+    x = mo.synthetic_layer(100 + rank, 4, H, E, I)[0]
+    el = E // world
+    layer = ExpertParallelMoE(_bf16(gate), types.SimpleNamespace(num_slots=el), rank=rank, world=world,
+                              exchange=TorchDistExchange(), top_k=K, ops=HostOps(wg, wu, wd, rank * el))
+    layer.forward(_bf16(x), mode="padded")                  # layer 0 on both ranks
+    if rank == 1:
+        q.put((rank, "left"))
+        q.close()
+        q.join_thread()
+        os._exit(0)                                         # gone without a goodbye
+    t0 = time.monotonic()
+    try:
+        layer.forward(_bf16(x), mode="padded")              # layer 1: the peer never joins
+        q.put((rank, "no error"))
+    except Exception as exc:
+        q.put((rank, ("raised", time.monotonic() - t0, type(exc).__name__)))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_lost_rank_raises_on_the_survivor():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_lost_rank_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert results[1] == "left"
+    outcome = results[0]
+    assert isinstance(outcome, tuple) and outcome[0] == "raised", outcome
+    assert outcome[1] < 40.0, outcome          # within the process-group timeout (10 s) plus slack
+
+
 def test_capacity_bound():
     """The padded block must hold every row a rank can send one destination:
     T tokens x min(k, EL) distinct experts per token."""

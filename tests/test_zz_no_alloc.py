@@ -45,8 +45,10 @@ def test_pack_static_matches_workspace_pack():
     from pdscope_b200 import _lib
     lib = _lib.lib
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    # both calls take the multi-CTA path (T*k > 8192), which uses the scratch
-    for seed, tokens, k, experts in ((1, 1500, 8, 128), (2, 2300, 6, 96)):
+    # the first two calls take the multi-CTA path (T*k > 8192), which uses the
+    # scratch; then the single-CTA path (T*k <= 8192, no scratch), and a shape
+    # whose histograms fill the array exactly (ceil(T*k/4096) * E == 65536)
+    for seed, tokens, k, experts in ((1, 1500, 8, 128), (2, 2300, 6, 96), (3, 64, 8, 128), (4, 32768, 8, 1024)):
         sel, w = _routing(seed, tokens, k, experts)
         ref, got = _outputs(tokens, k, experts), _outputs(tokens, k, experts)
         ws = torch.empty(lib.pdx_pack_workspace_bytes(tokens, k, experts), dtype=torch.uint8, device="cuda")
