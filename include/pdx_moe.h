@@ -125,8 +125,8 @@ int pdx_pack(const int64_t *selected, const void *weights, int64_t T, int32_t to
  * cudaMalloc's device-wide synchronisation).  Its scratch is a fixed
  * file-scope device array of PDX_PACK_STATIC_MAX_HIST_INTS ints (256 KiB, held
  * by every GPU that loads the library until exit); sizes needing more,
- * ceil(T*top_k/4096)*E > PDX_PACK_STATIC_MAX_HIST_INTS when T*top_k > 8192,
- * return PDX_ERR_UNSUPPORTED.  All calls share that array: calls whose kernels
+ * ceil(T*top_k/4096)*E > PDX_PACK_STATIC_MAX_HIST_INTS (possible only when
+ * T*top_k > 8192), return PDX_ERR_UNSUPPORTED.  All calls share that array: calls whose kernels
  * overlap on the GPU race.  The first call on a device resolves the array's
  * device address (cudaGetSymbolAddress) with that device current; make it
  * before any stream capture.  The address is kept for the life of the

@@ -60,7 +60,7 @@ extern "C" int pdx_pack_static(const int64_t* selected, const void* weights, int
     if (!selected || !weights || !counts || !offsets || !tokens || !positions || !packed_w || !inverse || !active)
         return fail(PDX_ERR_INVALID, "null packing argument");
     const int64_t N = T * top_k;
-    const int64_t need = static_cast<int64_t>(pack_chunks(N)) * E;
+    const int64_t need = static_cast<int64_t>(pack_chunks(N, kPackChunk)) * E;
     if (N > kPackSingleMax && need > kPackStaticHistInts)
         return fail(PDX_ERR_UNSUPPORTED,
                     "pdx_pack_static: ceil(T*top_k/%d)*E = %lld histogram entries exceeds the fixed %d "
@@ -69,6 +69,6 @@ extern "C" int pdx_pack_static(const int64_t* selected, const void* weights, int
     int* scratch = nullptr;
     if ((st = pack_static_scratch(&scratch))) return st;
     PackOut o{counts, offsets, tokens, positions, static_cast<uint16_t*>(packed_w), inverse, active};
-    st = launch_pack(selected, static_cast<const uint16_t*>(weights), T, top_k, E, o, scratch, stream);
+    st = launch_pack(selected, static_cast<const uint16_t*>(weights), T, top_k, E, o, scratch, stream, kPackChunk);
     return st ? st : ok();
 }

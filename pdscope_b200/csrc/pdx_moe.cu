@@ -12,6 +12,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <type_traits>
 #include <utility>
 
 #include "combine.cu"
@@ -100,6 +101,10 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     } while (0)
 
 constexpr size_t kAlign = 256;
+// SM count the launch plans assume (B200), so that a workspace query and the
+// launch it sizes always agree; the plans only shape the work, not results.
+constexpr int kPlanSMs = 148;
+constexpr int kMaxExperts = 1024;
 inline size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 // Bump allocator over the caller's workspace.
@@ -141,6 +146,8 @@ int device_setup(int* sms_out) {
         if (major != 10) return fail(PDX_ERR_UNSUPPORTED, "pdx_moe is built for sm_100a; device %d is sm_%d", dev, major);
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_grouped_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           static_cast<int>(kGemmSmemBytes)));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_pack_scan_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>((11 * kMaxExperts + 1 + kPackScanSmemInts) * 4)));
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_router_logits_dmma, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           static_cast<int>(kDmmaSmemBytes)));
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_grouped_gemm_pair, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -167,6 +174,8 @@ int device_setup(int* sms_out) {
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_stream_gemm<16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ss));
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_stream_gemm<32, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ss));
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_stream_gemm<32, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ss));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_stream_gemm<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ss));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_stream_gemm<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ss));
         g_num_sms[dev] = sms;
         g_attrs_set[dev] = true;
     }
@@ -202,9 +211,8 @@ int encode_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, 
 
 // ---- shape checks -----------------------------------------------------------------
 constexpr int kMaxTopK = 32;
-constexpr int kMaxExperts = 1024;
 constexpr int64_t kTailMaxTokens = 64;     // fused route tail up to this many tokens
-constexpr int64_t kPackSingleMax = 8192;   // single-CTA pack up to this many assignments
+constexpr int64_t kPackSingleMax = 1024;   // single-CTA pack up to this many assignments (4 scatter rounds)
 constexpr int64_t kStreamMaxRowsPerExpert = 16;  // auto mode: weight streaming up to this average
 
 int check_route_shape(int64_t T, int64_t H, int64_t E, int32_t k) {
@@ -295,22 +303,39 @@ struct RouteBufs {
 
 size_t route_ticket_bytes(int64_t T) { return static_cast<size_t>(1 + (T + kRouteTB - 1) / kRouteTB) * 4; }
 
-// Split-K partials of the tiled router (T > kTailMaxTokens only).
-constexpr int kMaxRouterSplits = 4;
+// Split-K of the tiled router (T > kTailMaxTokens only).  A 64 x 128 tile
+// over all of K is ~2.7 * 10^5 FP64-tensor cycles at H = 2048 (~130 us on one
+// SM), so a few hundred tokens (a handful of tiles) need many K splits to
+// occupy the GPU, while large batches need few.  The split count is bounded by
+// what three waves of units over two CTAs per SM can use (so the partial
+// buffer stays small at prefill sizes) and by kMaxRouterSplits.
+constexpr int kMaxRouterSplits = 32;
+constexpr int kRouterSlots = 2 * kPlanSMs;
+int64_t router_tiles(int64_t T, int64_t E) { return ((T + kDmT - 1) / kDmT) * ((E + kDmE - 1) / kDmE); }
+int router_split_bound(int64_t T, int64_t E) {
+    const int64_t tiles = std::max<int64_t>(1, router_tiles(T, E));
+    return static_cast<int>(std::min<int64_t>(kMaxRouterSplits, (3 * kRouterSlots + tiles - 1) / tiles));
+}
 size_t route_partial_bytes(int64_t T, int64_t E) {
-    return T > kTailMaxTokens ? static_cast<size_t>(kMaxRouterSplits) * T * E * sizeof(double) : 0;
+    const int s = router_split_bound(T, E);
+    return T > kTailMaxTokens && s > 1 ? static_cast<size_t>(s) * T * E * sizeof(double) : 0;
 }
 
-// K splits per router tile: the count minimising waves/splits (time in units of
-// one whole-K tile) over `slots` resident CTAs; ties keep fewer splits (less
-// partial traffic).  Each split keeps >= 8 K chunks.
-int router_splits(int64_t tiles, int64_t H, int slots) {
+// K splits per router tile: the count minimising the modelled time -- waves
+// of units over the resident CTAs times the unit's share of a whole-K tile,
+// plus the FP64 partials each extra split writes and k_topk_partials reads
+// back; ties keep fewer splits.  Each split keeps >= 2 K chunks.
+int router_splits(int64_t T, int64_t E, int64_t H) {
+    const int64_t tiles = router_tiles(T, E);
+    const double tile_us = static_cast<double>(H) * kDmT * kDmE / (64.0 * 1.9e3);  // FP64 FMA/clk/SM x clk/us
+    const double partial_us_per_split = static_cast<double>(T) * E * 16.0 / 6.5e6;  // write + read at ~6.5 TB/s
     int best = 1;
     double best_t = 1e30;
-    for (int s = 1; s <= kMaxRouterSplits; ++s) {
-        if (s > 1 && H / s < 8 * kDmK) break;
+    for (int s = 1; s <= router_split_bound(T, E); ++s) {
+        if (s > 1 && H / s < 2 * kDmK) break;
         const int64_t units = tiles * s;
-        const double t = static_cast<double>((units + slots - 1) / slots) / s;
+        const double t = static_cast<double>((units + kRouterSlots - 1) / kRouterSlots) * tile_us / s +
+                         (s > 1 ? s * partial_us_per_split : 0.0);
         if (t < best_t - 1e-9) { best_t = t; best = s; }
     }
     return best;
@@ -326,8 +351,8 @@ int launch_route(const void* x, const void* gate, int64_t T, int64_t H, int64_t 
         int sms = 0;
         int st = device_setup(&sms);
         if (st) return st;
-        const int64_t tiles = ((T + kDmT - 1) / kDmT) * ((E + kDmE - 1) / kDmE);
-        const int splits = router_splits(tiles, H, 2 * sms);
+        const int64_t tiles = router_tiles(T, E);
+        const int splits = router_splits(T, E, H);
         const int k_per_split = static_cast<int>(((H + splits - 1) / splits + kDmK - 1) / kDmK * kDmK);
         k_router_logits_dmma<<<static_cast<unsigned>(tiles * splits), kDmThreads, kDmmaSmemBytes, stream>>>(
             static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gate), static_cast<int>(T),
@@ -335,13 +360,18 @@ int launch_route(const void* x, const void* gate, int64_t T, int64_t H, int64_t 
         PDX_LAUNCHED();
         const int warps_per_cta = 8;
         const int grid = static_cast<int>((T + warps_per_cta - 1) / warps_per_cta);
-        if (splits > 1)
-            k_topk_partials<<<grid, warps_per_cta * 32, 0, stream>>>(b.partials, splits, static_cast<int>(T),
-                                                                     static_cast<int>(E), k, normalize, b.logits,
-                                                                     b.selected, b.weights);
-        else
-            k_topk<<<grid, warps_per_cta * 32, 0, stream>>>(b.logits, static_cast<int>(T), static_cast<int>(E), k,
-                                                            normalize, b.selected, b.weights);
+        with_epl(E, [&](auto epl) {
+            constexpr int EPL = decltype(epl)::value;
+            if (splits > 1)
+                k_topk_partials<EPL><<<grid, warps_per_cta * 32, 0, stream>>>(
+                    b.partials, splits, static_cast<int>(T), static_cast<int>(E), k, normalize, b.logits, b.selected,
+                    b.weights);
+            else
+                k_topk<EPL><<<grid, warps_per_cta * 32, 0, stream>>>(b.logits, static_cast<int>(T),
+                                                                     static_cast<int>(E), k, normalize, b.selected,
+                                                                     b.weights);
+            return 0;
+        });
         PDX_LAUNCHED();
         if (fused_pack) return fail(PDX_ERR_UNSUPPORTED, "fused pack is only available for T <= %lld",
                                     static_cast<long long>(kTailMaxTokens));
@@ -363,25 +393,40 @@ int launch_route(const void* x, const void* gate, int64_t T, int64_t H, int64_t 
         tail.pack = *fused_pack;
         smem = static_cast<size_t>(E + E + 1 + (kRouteWarps * E)) * sizeof(int);
     }
-    if (false && T <= kSmallRouteT && H <= 64 * 1024) {
+    if (T <= kSmallRouteT) {
         // decode sizes: one CTA per expert
-        k_router_small<<<static_cast<unsigned>(E), kSmallRouteThreads, smem, stream>>>(
-            static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gate), static_cast<int>(T),
-            static_cast<int>(H), static_cast<int>(E), b.logits, tail);
+        with_epl(E, [&](auto epl) {
+            k_router_small<decltype(epl)::value><<<static_cast<unsigned>(E), kSmallRouteThreads, smem, stream>>>(
+                static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gate), static_cast<int>(T),
+                static_cast<int>(H), static_cast<int>(E), b.logits, tail);
+            return 0;
+        });
         PDX_LAUNCHED();
         return PDX_OK;
     }
-    k_router_logits<<<n_tb * n_eb, kRouteWarps * 32, smem, stream>>>(
-        static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gate), static_cast<int>(T), static_cast<int>(H),
-        static_cast<int>(E), b.logits, tail);
+    with_epl(E, [&](auto epl) {
+        k_router_logits<decltype(epl)::value><<<n_tb * n_eb, kRouteWarps * 32, smem, stream>>>(
+            static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gate), static_cast<int>(T),
+            static_cast<int>(H), static_cast<int>(E), b.logits, tail);
+        return 0;
+    });
     PDX_LAUNCHED();
     return PDX_OK;
 }
 
-size_t pack_chunks(int64_t N) { return static_cast<size_t>((N + kPackChunk - 1) / kPackChunk); }
+// Flat entries per CTA of the multi-CTA pack: enough CTAs to cover the SMs
+// once (a multiple of one scatter round), at most kPackChunk.  The
+// allocation-free entry point keeps kPackChunk (its documented scratch bound).
+int64_t pack_chunk_for(int64_t N) {
+    const int64_t per = (N + kPlanSMs - 1) / kPlanSMs;
+    return std::min<int64_t>(kPackChunk, std::max<int64_t>(kPackMinChunk, (per + kPackMinChunk - 1) / kPackMinChunk *
+                                                                               kPackMinChunk));
+}
+size_t pack_chunks(int64_t N, int64_t chunk) { return static_cast<size_t>((N + chunk - 1) / chunk); }
+size_t pack_chunks(int64_t N) { return pack_chunks(N, pack_chunk_for(N)); }
 
 int launch_pack(const int64_t* selected, const uint16_t* weights, int64_t T, int32_t k, int64_t E, const PackOut& o,
-                int* chunk_hist, cudaStream_t stream) {
+                int* chunk_hist, cudaStream_t stream, int64_t chunk = 0) {
     const int64_t N = T * k;
     if (N <= kPackSingleMax) {
         const size_t smem = static_cast<size_t>(E + E + 1 + 8 * E) * sizeof(int);
@@ -390,21 +435,34 @@ int launch_pack(const int64_t* selected, const uint16_t* weights, int64_t T, int
         PDX_LAUNCHED();
         return PDX_OK;
     }
-    const int chunks = static_cast<int>(pack_chunks(N));
+    if (chunk <= 0) chunk = pack_chunk_for(N);
+    const int chunks = static_cast<int>(pack_chunks(N, chunk));
+    int sms = 0;
+    if (int st = device_setup(&sms)) return st;   // k_pack_scan's shared-memory limit
     k_pack_hist<<<chunks, kPackThreads, E * sizeof(int), stream>>>(selected, static_cast<int>(T), k,
-                                                                     static_cast<int>(E), chunk_hist);
+                                                                     static_cast<int>(E), static_cast<int>(chunk),
+                                                                     chunk_hist);
     PDX_LAUNCHED();
-    k_pack_scan<<<1, kPackThreads, (2 * E + 1) * sizeof(int), stream>>>(chunk_hist, chunks, static_cast<int>(E), o);
+    if (static_cast<int64_t>(chunks) * E <= kPackScanSmemInts) {
+        // every CTA derives its own chunk base from the staged histograms
+        const size_t smem = (static_cast<size_t>(chunks) * E + 11 * E + 1) * sizeof(int);
+        k_pack_scan_scatter<<<chunks, kPackThreads, smem, stream>>>(selected, weights, static_cast<int>(T), k,
+                                                                     static_cast<int>(E), static_cast<int>(chunk),
+                                                                     chunks, chunk_hist, o);
+        PDX_LAUNCHED();
+        return PDX_OK;
+    }
+    k_pack_scan<<<1, kPackThreads, (2 * E + 1) * sizeof(int), stream>>>(chunk_hist, chunks, static_cast<int>(E),
+                                                                         o);
     PDX_LAUNCHED();
     k_pack_scatter<<<chunks, kPackThreads, (E + 8 * E) * sizeof(int), stream>>>(
-        selected, weights, static_cast<int>(T), k, static_cast<int>(E), chunk_hist, o);
+        selected, weights, static_cast<int>(T), k, static_cast<int>(E), static_cast<int>(chunk), chunk_hist, o);
     PDX_LAUNCHED();
     return PDX_OK;
 }
 
 // Split-K / token-tile plan of the weight-streaming path.  It depends only on
 // (rows, E, H, I), so the workspace query and the launch agree.
-constexpr int kPlanSMs = 148;
 
 struct StreamPlan {
     int nt;
@@ -431,7 +489,7 @@ StreamPlan plan_stream(int64_t rows, int64_t E, int64_t H, int64_t I) {
     StreamPlan p{};
     const int64_t est_active = std::max<int64_t>(1, std::min(E, rows));
     const int64_t avg = (rows + est_active - 1) / est_active;
-    p.nt = avg <= 12 ? 16 : 32;
+    p.nt = avg <= 12 ? 16 : (avg <= 24 ? 32 : 64);
     const int64_t nb_bound = rows / p.nt + est_active;
     p.tiles1 = (I / 128) * nb_bound;
     p.tiles2 = (H / 128) * nb_bound;
@@ -550,7 +608,8 @@ int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* o
                       static_cast<int>(H / 128), plan.s2, static_cast<uint16_t*>(y), H, partials,
                       tickets + plan.ticket_bytes / 4};
         if (plan.nt == 16) return launch_stream_pair<16>(tm_g, tm_u, tm_x, tm_d, tm_h, plan, a1, a2, sms, stream);
-        return launch_stream_pair<32>(tm_g, tm_u, tm_x, tm_d, tm_h, plan, a1, a2, sms, stream);
+        if (plan.nt == 32) return launch_stream_pair<32>(tm_g, tm_u, tm_x, tm_d, tm_h, plan, a1, a2, sms, stream);
+        return launch_stream_pair<64>(tm_g, tm_u, tm_x, tm_d, tm_h, plan, a1, a2, sms, stream);
     }
     // prefill: token-tiled grouped GEMM on single CTAs (128 x 256 tiles); CTA-pair
     // 256 x 256 tiles on request (mode PDX_FFN_GEMM_PAIR).  The pair form moves a
@@ -677,9 +736,12 @@ int pdx_topk_from_logits(const void* logits, int64_t T, int64_t E, int32_t top_k
     if (!logits || !selected_out || !weights_out) return fail(PDX_ERR_INVALID, "null routing argument");
     const int warps_per_cta = 8;
     const int grid = static_cast<int>((T + warps_per_cta - 1) / warps_per_cta);
-    k_topk<<<grid, warps_per_cta * 32, 0, stream>>>(static_cast<const uint16_t*>(logits), static_cast<int>(T),
-                                                    static_cast<int>(E), top_k, normalize, selected_out,
-                                                    static_cast<uint16_t*>(weights_out));
+    with_epl(E, [&](auto epl) {
+        k_topk<decltype(epl)::value><<<grid, warps_per_cta * 32, 0, stream>>>(
+            static_cast<const uint16_t*>(logits), static_cast<int>(T), static_cast<int>(E), top_k, normalize,
+            selected_out, static_cast<uint16_t*>(weights_out));
+        return 0;
+    });
     PDX_LAUNCHED();
     return ok();
 }

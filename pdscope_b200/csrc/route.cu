@@ -34,6 +34,7 @@ __device__ __forceinline__ double bits_to_f64(uint32_t b16) {
 // two BF16 values are exact in FP64 and the FP64 sum of 2048 of them is
 // within a few units of 2^-53 relative, so the BF16 rounding equals that of
 // the exact sum except in cases of probability ~1e-12 per logit.
+template <int EPL>
 __global__ void __launch_bounds__(kRouteWarps * 32) k_router_logits(const uint16_t* __restrict__ x,
                                                                      const uint16_t* __restrict__ gate, int T,
                                                                      int H, int E, uint16_t* __restrict__ logits,
@@ -117,7 +118,10 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_router_logits(const uint16
     if (s_ticket != static_cast<unsigned int>(n_eb - 1)) return;
     __threadfence();
     const int t = tb * kRouteTB + warp;  // kRouteWarps == kRouteTB: one token per warp
-    if (t < T) topk_row(logits, t, E, tail.k, tail.normalize != 0, tail.selected, tail.weights);
+    if (t < T)
+        warp_softmax_topk<EPL>(logits + static_cast<size_t>(t) * E, E, tail.k, tail.normalize != 0,
+                               tail.selected + static_cast<size_t>(t) * tail.k,
+                               tail.weights + static_cast<size_t>(t) * tail.k);
     if (!tail.do_pack) return;
     __threadfence();
     __syncthreads();
@@ -143,6 +147,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_router_logits(const uint16
 constexpr int kSmallRouteT = 16;
 constexpr int kSmallRouteThreads = 256;
 
+template <int EPL>
 __global__ void __launch_bounds__(kSmallRouteThreads) k_router_small(const uint16_t* __restrict__ x,
                                                                      const uint16_t* __restrict__ gate, int T,
                                                                      int H, int E, uint16_t* __restrict__ logits,
@@ -202,8 +207,10 @@ __global__ void __launch_bounds__(kSmallRouteThreads) k_router_small(const uint1
     __syncthreads();
     if (s_ticket != static_cast<unsigned int>(E - 1)) return;
     __threadfence();
-    for (int t = warp; t < T; t += kWarps) topk_row(logits, t, E, tail.k, tail.normalize != 0, tail.selected,
-                                                     tail.weights);
+    for (int t = warp; t < T; t += kWarps)
+        warp_softmax_topk<EPL>(logits + static_cast<size_t>(t) * E, E, tail.k, tail.normalize != 0,
+                               tail.selected + static_cast<size_t>(t) * tail.k,
+                               tail.weights + static_cast<size_t>(t) * tail.k);
     if (!tail.do_pack) return;
     __threadfence();
     __syncthreads();
@@ -366,13 +373,26 @@ __device__ __forceinline__ void topk_partials_row(const double* __restrict__ par
     double acc[EPL];
 #pragma unroll
     for (int i = 0; i < EPL; ++i) acc[i] = 0.0;
-    for (int sp = 0; sp < splits; ++sp) {
-        const double* row = partials + (static_cast<size_t>(sp) * T + t) * E;
+    // four splits' partials are loaded before they are added (in split order),
+    // so a many-split row costs splits/4 memory round trips, not splits
+    constexpr int kBatch = 4;
+    for (int sp0 = 0; sp0 < splits; sp0 += kBatch) {
+        double v[kBatch][EPL];
 #pragma unroll
-        for (int i = 0; i < EPL; ++i) {
-            const int idx = lane + 32 * i;
-            if (idx < E) acc[i] += __ldg(row + idx);
+        for (int j = 0; j < kBatch; ++j) {
+            const double* row = partials + (static_cast<size_t>(sp0 + j) * T + t) * E;
+#pragma unroll
+            for (int i = 0; i < EPL; ++i) {
+                const int idx = lane + 32 * i;
+                v[j][i] = 0.0;
+                if (sp0 + j < splits && idx < E) v[j][i] = __ldg(row + idx);
+            }
         }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j)
+#pragma unroll
+            for (int i = 0; i < EPL; ++i)
+                if (sp0 + j < splits) acc[i] += v[j][i];
     }
     float v[EPL];
 #pragma unroll
@@ -390,6 +410,10 @@ __device__ __forceinline__ void topk_partials_row(const double* __restrict__ par
                                 weights + static_cast<size_t>(t) * k);
 }
 
+// Kernels that route a whole row per warp are instantiated per EPL (elements
+// per lane, next_pow2(E) / 32) and dispatched on the host, so each keeps only
+// its own row in registers.
+template <int EPL>
 __global__ void __launch_bounds__(256) k_topk_partials(const double* __restrict__ partials, int splits, int T, int E,
                                                        int k, int normalize, uint16_t* __restrict__ logits,
                                                        int64_t* __restrict__ selected,
@@ -397,23 +421,29 @@ __global__ void __launch_bounds__(256) k_topk_partials(const double* __restrict_
     const int warps = static_cast<int>(blockDim.x >> 5);
     const bool nrm = normalize != 0;
     for (int t = static_cast<int>(blockIdx.x) * warps + static_cast<int>(threadIdx.x >> 5); t < T;
-         t += static_cast<int>(gridDim.x) * warps) {
-        if (E <= 32) topk_partials_row<1>(partials, splits, T, E, t, k, nrm, logits, selected, weights);
-        else if (E <= 64) topk_partials_row<2>(partials, splits, T, E, t, k, nrm, logits, selected, weights);
-        else if (E <= 128) topk_partials_row<4>(partials, splits, T, E, t, k, nrm, logits, selected, weights);
-        else if (E <= 256) topk_partials_row<8>(partials, splits, T, E, t, k, nrm, logits, selected, weights);
-        else if (E <= 512) topk_partials_row<16>(partials, splits, T, E, t, k, nrm, logits, selected, weights);
-        else topk_partials_row<32>(partials, splits, T, E, t, k, nrm, logits, selected, weights);
-    }
+         t += static_cast<int>(gridDim.x) * warps)
+        topk_partials_row<EPL>(partials, splits, T, E, t, k, nrm, logits, selected, weights);
 }
 
 // Softmax + top-k + renormalisation, one warp per token.
+template <int EPL>
 __global__ void __launch_bounds__(256) k_topk(const uint16_t* __restrict__ logits, int T, int E, int k,
                                               int normalize, int64_t* __restrict__ selected,
                                               uint16_t* __restrict__ weights) {
     const int warps = static_cast<int>(blockDim.x >> 5);
     const int first = static_cast<int>(blockIdx.x) * warps + static_cast<int>(threadIdx.x >> 5);
-    topk_rows_dispatch(logits, T, E, k, normalize != 0, selected, weights, first, gridDim.x * warps);
+    block_topk_rows<EPL>(logits, T, E, k, normalize != 0, selected, weights, first, gridDim.x * warps);
+}
+
+// Calls f(std::integral_constant<int, EPL>) for the EPL of E (<= 1024 experts).
+template <typename F>
+inline auto with_epl(int64_t E, F&& f) {
+    if (E <= 32) return f(std::integral_constant<int, 1>{});
+    if (E <= 64) return f(std::integral_constant<int, 2>{});
+    if (E <= 128) return f(std::integral_constant<int, 4>{});
+    if (E <= 256) return f(std::integral_constant<int, 8>{});
+    if (E <= 512) return f(std::integral_constant<int, 16>{});
+    return f(std::integral_constant<int, 32>{});
 }
 
 }  // namespace pdx

@@ -130,13 +130,16 @@ def zipf_hot_sets(gates, count):
 
 
 def write_hot_file(path, hot):
-    """Hot table in the reference's ``layer,expert`` text format (hot/qwen.txt,
-    read by load_hot_profile, pdscope_runtime.py:62-72), hottest first."""
+    """Hot table in the reference's text format (hot/qwen.txt, read by
+    load_hot_profile, pdscope_runtime.py:62-72): one ``layer,expert`` row per
+    line, no header, hottest first across layers -- rank 0 of every layer,
+    then rank 1, ... -- so that a global budget of the first N rows spreads
+    over the layers."""
     with open(path, "w") as f:
-        f.write("layer,expert\n")
-        for l, hs in enumerate(hot):
-            for e in hs:
-                f.write(f"{l},{e}\n")
+        for r in range(max((len(h) for h in hot), default=0)):
+            for l, hs in enumerate(hot):
+                if r < len(hs):
+                    f.write(f"{l},{hs[r]}\n")
 
 
 def load_hot_file(path, per_layer, layers):
@@ -145,7 +148,7 @@ def load_hot_file(path, per_layer, layers):
     with open(path) as f:
         for line in f:
             line = line.strip()
-            if not line or line.startswith("layer"):
+            if not line or not line[0].isdigit():
                 continue
             l, e = (int(v) for v in line.split(","))
             if l < layers and len(hot[l]) < per_layer:

@@ -71,19 +71,22 @@ class ResidentMoEStack:
         # acts[0] is the step input (never overwritten); layers alternate acts[1], acts[2]
         acts = [torch.zeros((t_count, H), **bf) for _ in range(3)]
         n = t_count * k
+        # every layer's expert counts in one [L, E] block, so one copy moves them all
+        counts = torch.zeros((L, E), **i32)
         stages = [StageBuffers(logits=torch.empty((t_count, E), **bf),
                                selected=torch.empty((t_count, k), dtype=torch.int64, device=dev),
-                               weights=torch.empty((t_count, k), **bf), counts=torch.empty(E, **i32),
+                               weights=torch.empty((t_count, k), **bf), counts=counts[l],
                                offsets=torch.empty(E + 1, **i32), tokens=torch.empty(n, **i32),
                                positions=torch.empty(n, **i32), packed_w=torch.empty(n, **bf),
                                inverse=torch.empty(n, **i32), active=torch.empty(E + 1, **i32))
-                  for _ in range(L)]
+                  for l in range(L)]
         rows = torch.empty((n, H), **bf)  # expert outputs of the current layer (staged path)
         ws_layer = lib.pdx_layer_workspace_bytes(t_count, H, E, k, self.inter, mode)
         ws_stage = max(lib.pdx_route_workspace_bytes(t_count, E), lib.pdx_pack_workspace_bytes(t_count, k, E),
                        lib.pdx_ffn_workspace_bytes(n, E, H, self.inter, mode))
         ws = torch.empty(max(ws_layer, ws_stage), dtype=torch.uint8, device=dev)
-        b = dict(acts=acts, stages=stages, ws=ws, rows=rows)
+        b = dict(acts=acts, stages=stages, ws=ws, rows=rows, counts=counts,
+                 counts_host=torch.zeros((L, E), dtype=torch.int32).pin_memory(), counts_ready=torch.cuda.Event())
         self._bufs[key] = b
         return b
 
@@ -96,7 +99,7 @@ class ResidentMoEStack:
         return acts[1 + l % 2]
 
     # -- fused path: one C-ABI call per layer -------------------------------------
-    def _step_fused(self, t_count, mode):
+    def _step_fused(self, t_count, mode, counts_to_host=False):
         b = self.buffers(t_count, mode)
         acts, stages, ws = b["acts"], b["stages"], b["ws"]
         s = _stream()
@@ -108,6 +111,10 @@ class ResidentMoEStack:
                                     _ptr(x_in), _ptr(x_out), _ptr(st.logits), _ptr(st.selected),
                                     _ptr(st.weights), _ptr(st.counts), mode | _lib.LAYER_OUT_NORM, _ptr(ws),
                                     ws.numel(), s))
+        if counts_to_host:
+            # one device-to-host copy of every layer's counts into pinned memory,
+            # inside the step (and its graph): no per-layer host synchronisation
+            b["counts_host"].copy_(b["counts"], non_blocking=True)
 
     # -- staged path: route, pack, FFN, combine as separate calls --------------------
     def route_and_pack(self, l, t_count, mode=_lib.FFN_AUTO):
@@ -151,21 +158,35 @@ class ResidentMoEStack:
     def output(self, t_count, mode=_lib.FFN_AUTO):
         return self._act_out(self.buffers(t_count, mode)["acts"], self.num_layers - 1)
 
-    def step(self, t_count, mode=_lib.FFN_AUTO, *, graph=True):
-        """Run every layer on ``input(t_count)``; result in ``output(t_count)``."""
+    def step(self, t_count, mode=_lib.FFN_AUTO, *, graph=True, counts_to_host=False):
+        """Run every layer on ``input(t_count)``; result in ``output(t_count)``.
+
+        With ``counts_to_host`` the step ends with one asynchronous copy of every
+        layer's routed-token counts into pinned host memory (``expert_counts``
+        reads them once the step has finished)."""
         if not graph:
-            self._step_fused(t_count, mode)
-            return
-        key = ("fused", t_count, mode)
-        g = self._graphs.get(key)
-        if g is None:
-            self._step_fused(t_count, mode)  # warm: device attributes, tensor maps
-            torch.cuda.synchronize(self.device)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                self._step_fused(t_count, mode)
-            self._graphs[key] = g
-        g.replay()
+            self._step_fused(t_count, mode, counts_to_host)
+        else:
+            key = ("fused", t_count, mode, counts_to_host)
+            g = self._graphs.get(key)
+            if g is None:
+                self._step_fused(t_count, mode, counts_to_host)  # warm: device attributes, tensor maps
+                torch.cuda.synchronize(self.device)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self._step_fused(t_count, mode, counts_to_host)
+                self._graphs[key] = g
+            g.replay()
+        if counts_to_host:
+            self.buffers(t_count, mode)["counts_ready"].record()
+
+    def expert_counts(self, t_count, mode=_lib.FFN_AUTO):
+        """[L, E] int32 pinned host tensor of the last ``step(..., counts_to_host=True)``:
+        waits for that step's copy (not for the whole device).  Valid until the
+        next such step."""
+        b = self.buffers(t_count, mode)
+        b["counts_ready"].synchronize()
+        return b["counts_host"]
 
     def ffn_graph(self, t_count, mode=_lib.FFN_AUTO):
         """CUDA graph of the grouped FFN of every layer on the current packing."""
@@ -222,6 +243,34 @@ class ResidentMoEStack:
 
     def release_graphs(self):
         self._graphs.clear()
+
+
+class ExpertLoadTracker:
+    """Routed-token totals per (layer, expert), fed from the pinned count
+    copies of ``ResidentMoEStack.step(..., counts_to_host=True)``.
+
+    The reference derives its static hot table (hot/qwen.txt, read by
+    load_hot_profile, expertbench/pdscope_runtime.py:62-72, which fixes the
+    resident set AdaptSched plans around) from a routing profile of this
+    kind; ``hot_sets`` / ``write_hot_file`` turn the totals into that table,
+    hottest first with ties to the lower expert id.
+    """
+
+    def __init__(self, layers, experts):
+        self.totals = np.zeros((layers, experts), np.int64)
+        self.steps = 0
+
+    def add(self, counts):
+        self.totals += np.asarray(counts.numpy() if hasattr(counts, "numpy") else counts, dtype=np.int64)
+        self.steps += 1
+
+    def hot_sets(self, per_layer):
+        order = np.argsort(-self.totals, axis=1, kind="stable")
+        return [order[l, :per_layer].tolist() for l in range(self.totals.shape[0])]
+
+    def write_hot_file(self, path, per_layer):
+        from .offload import write_hot_file
+        write_hot_file(path, self.hot_sets(per_layer))
 
 
 # ---------------------------------------------------------------------------

@@ -146,3 +146,34 @@ def test_config3_prefill_ffn_at_size_vs_oracle():
     assert worst_l2 <= 0.02
     print(f"config-3 FFN: {len(sample)} experts sampled, {ones} one-row experts, largest segment {n} rows, "
           f"worst FP32 relative L2 {worst_l2:.4f}")
+
+
+def test_graph_step_copies_counts_to_host_for_the_policy():
+    """The whole-step graph ends with one async copy of every layer's expert
+    counts into pinned host memory; the counts equal the device's, feed the
+    load tracker (the hot table the reference's load_hot_profile reads), and
+    the step's output is unchanged by the copy."""
+    from pdscope_b200.stack import ExpertLoadTracker, activations, build_stack
+    layers, tokens = 4, 64
+    stack = build_stack(layers, H, E, I, K, seed=5)
+    tracker = ExpertLoadTracker(layers, E)
+    want_total = torch.zeros((layers, E), dtype=torch.int64)
+    for rep in range(3):
+        stack.input(tokens).copy_(activations(tokens, H, seed=40 + rep))
+        stack.step(tokens, graph=False)
+        eager = stack.output(tokens).clone()
+        stack.step(tokens, counts_to_host=True)
+        host = stack.expert_counts(tokens)
+        torch.cuda.synchronize()
+        device = stack.buffers(tokens)["counts"].cpu()
+        assert torch.equal(host, device)
+        assert (host.sum(dim=1) == tokens * K).all()
+        assert torch.equal(stack.output(tokens), eager)
+        tracker.add(host)
+        want_total += device.long()
+    assert np.array_equal(tracker.totals, want_total.numpy()) and tracker.steps == 3
+    hot = tracker.hot_sets(4)
+    for l in range(layers):
+        top = np.sort(want_total[l].numpy())[::-1][:4]
+        assert sorted(want_total[l].numpy()[hot[l]].tolist(), reverse=True) == top.tolist()
+    stack.release_graphs()

@@ -102,3 +102,26 @@ def test_runtime_without_planner_runs_every_expert_on_gpu():
     d = rt._decision(cur, {}, layer=0, phase="prefill", top_k=8, attention_ms=0., hit_rate=0.)
     assert d["cpu_queue"] == [] and sorted(d["gpu_resident_queue"]) == sorted(cur)
     assert d["placements"] == {e: "gpu" for e in sorted(cur)}
+
+
+def test_reference_load_hot_profile_reads_our_hot_file(tmp_path, ref):
+    """write_hot_file's table is the reference's hot/qwen.txt format: its own
+    load_hot_profile (expertbench/pdscope_runtime.py:62-72) accepts it and
+    takes the hottest rows first."""
+    sys.path.insert(0, str(REF))
+    try:
+        from expertbench.cache import ExpertKey
+        from expertbench.pdscope_runtime import load_hot_profile
+    finally:
+        sys.path.remove(str(REF))
+    from pdscope_b200.stack import ExpertLoadTracker
+    tracker = ExpertLoadTracker(48, 128)
+    rng = np.random.default_rng(0)
+    tracker.add(rng.integers(0, 50, size=(48, 128)))
+    path = tmp_path / "hot.txt"
+    tracker.write_hot_file(path, 16)
+    masters = {ExpertKey(l, e, "bf16"): None for l in range(48) for e in range(128)}
+    keys, meta = load_hot_profile(path, masters, 48 * 4)
+    hot = tracker.hot_sets(16)
+    assert meta["entries"] == 48 * 16
+    assert [(k.layer, k.expert) for k in keys] == [(l, hot[l][r]) for r in range(4) for l in range(48)]

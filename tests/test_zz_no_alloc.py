@@ -45,8 +45,8 @@ def test_pack_static_matches_workspace_pack():
     from pdscope_b200 import _lib
     lib = _lib.lib
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    # the first two calls take the multi-CTA path (T*k > 8192), which uses the
-    # scratch; then the single-CTA path (T*k <= 8192, no scratch), and a shape
+    # the first two calls take the multi-CTA path (T*k > 1024), which uses the
+    # scratch; then the single-CTA path (T*k <= 1024, no scratch), and a shape
     # whose histograms fill the array exactly (ceil(T*k/4096) * E == 65536)
     for seed, tokens, k, experts in ((1, 1500, 8, 128), (2, 2300, 6, 96), (3, 64, 8, 128), (4, 32768, 8, 1024)):
         sel, w = _routing(seed, tokens, k, experts)
