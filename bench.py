@@ -434,7 +434,15 @@ def main():
     for t_count, reps in ((1, 200), (512, 50)):
         x1 = activations(t_count, CFG["hidden"], device=dev, seed=300 + t_count)
         outs = layer0.forward(x1)
-        ms1 = timed(lambda: layer0.forward(x1, outputs=outs), reps, W) / reps
+        # ten pdx_moe_layer calls per CUDA graph, as a serving loop replays them
+        # (the layer's 1.2 GB of expert weights exceed L2, so no call hits in it)
+        torch.cuda.synchronize(dev)
+        g1 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g1):
+            for _ in range(10):
+                layer0.forward(x1, outputs=outs)
+        ms1 = timed(g1.replay, reps // 10, W) / (reps // 10 * 10)
+        del g1
         u = int((outs.counts > 0).sum().item())
         layer_bytes = u * EXPERT_BYTES + CFG["experts"] * CFG["hidden"] * 2 + 2 * t_count * CFG["hidden"] * 2
         config1[str(t_count)] = dict(us_per_layer=ms1 * 1e3, active_experts=u,

@@ -259,6 +259,36 @@ int pdx_offload_forward_layer(pdx_offload *h, int32_t layer, const void *x, int6
 int pdx_offload_get_stats(const pdx_offload *h, pdx_offload_stats *out);
 void pdx_offload_destroy(pdx_offload *h);
 
+/* Trace of the last pdx_offload_forward_layer call: what the reference's
+ * per-layer row records (PDScopeCudaRuntime.forward's return value,
+ * expertbench/pdscope_runtime.py:492-512 -- token counts, the placement of
+ * every routed expert, the demand copies, the prefetch ledger), produced by
+ * the native engine itself.  Optional outputs (NULL = skipped):
+ * counts_out [2*experts] (routed counts of this layer, then the predicted
+ * counts of the next layer, zeros on the last layer), placement_out [experts]
+ * (PDX_PLACE_*), prefetch_out [experts] (the first prefetch_issued entries:
+ * next-layer experts whose copies this layer issued, in issue order),
+ * demand_out [experts] (the first `demand` entries, in copy order). */
+#define PDX_PLACE_NONE 0     /* not routed in this layer */
+#define PDX_PLACE_HOT 1      /* hot-table slot */
+#define PDX_PLACE_WARM 2     /* static cache tier slot */
+#define PDX_PLACE_CACHE 3    /* cache-ring hit whose copy had completed at reveal */
+#define PDX_PLACE_LOADING 4  /* cache-ring hit whose copy was still in flight at reveal */
+#define PDX_PLACE_DEMAND 5   /* copied on demand by this layer */
+typedef struct {
+    int32_t layer, routed_experts, hot, warm, cache_ready, cache_loading, demand, demand_chunks;
+    int32_t prefetch_issued, prefetch_used, prefetch_skipped;
+    int64_t tokens, h2d_bytes;
+} pdx_offload_trace;
+int pdx_offload_last_trace(const pdx_offload *h, pdx_offload_trace *out, int32_t *counts_out,
+                           int32_t *placement_out, int32_t *prefetch_out, int32_t *demand_out);
+/* Device-to-device copy of the last call's selected ids [T, top_k] int64
+ * (which = 0) or of the next-layer prediction's (which = 1), so a caller can
+ * fingerprint the routing as the reference's row does (selected_sha256).
+ * T must be the last call's token count. */
+int pdx_offload_copy_selected(const pdx_offload *h, int32_t which, int64_t T, int64_t *selected_out,
+                              pdx_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * Whole layer: route -> pack -> grouped FFN -> combine, all on `stream`, no
  * host synchronisation (PDScopeCudaRuntime.forward's GPU work,

@@ -58,6 +58,16 @@ class OffloadStats(ctypes.Structure):
                                            "expert_uses", "layers")]
 
 
+class OffloadTrace(ctypes.Structure):
+    """pdx_offload_trace."""
+    _fields_ = [(name, c_i32) for name in ("layer", "routed_experts", "hot", "warm", "cache_ready", "cache_loading",
+                                           "demand", "demand_chunks", "prefetch_issued", "prefetch_used",
+                                           "prefetch_skipped")] + [("tokens", c_i64), ("h2d_bytes", c_i64)]
+
+
+PLACE_NONE, PLACE_HOT, PLACE_WARM, PLACE_CACHE, PLACE_LOADING, PLACE_DEMAND = 0, 1, 2, 3, 4, 5
+
+
 class P2PLayer(ctypes.Structure):
     """pdx_p2p_layer."""
     _fields_ = [("recv", c_vp), ("back", c_vp), ("cnt", c_vp), ("rflag", c_vp), ("bflag", c_vp), ("step", c_vp),
@@ -121,6 +131,8 @@ SIGNATURES = {
     "pdx_offload_forward_layer": (ctypes.c_int, [c_vp, c_i32, c_vp, c_i64, c_vp, c_i32, c_vp, c_vp]),
     "pdx_offload_get_stats": (ctypes.c_int, [c_vp, ctypes.POINTER(OffloadStats)]),
     "pdx_offload_destroy": (None, [c_vp]),
+    "pdx_offload_last_trace": (ctypes.c_int, [c_vp, ctypes.POINTER(OffloadTrace), c_vp, c_vp, c_vp, c_vp]),
+    "pdx_offload_copy_selected": (ctypes.c_int, [c_vp, c_i32, c_i64, c_vp, c_vp]),
 }
 
 

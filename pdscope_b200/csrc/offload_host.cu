@@ -55,6 +55,12 @@ struct OffloadEngine {
     int32_t* d_table = nullptr;         // [L][E]
     int32_t* d_active = nullptr;        // [max_launch][E+1]
     pdx_offload_stats st{};
+    // trace of the last forward_layer call
+    pdx_offload_trace trace{};
+    std::vector<int32_t> tr_counts;     // [2][E] routed counts of this layer and predicted next-layer counts
+    std::vector<int32_t> tr_place;      // [E] PDX_PLACE_*
+    std::vector<int32_t> tr_prefetch;   // next-layer experts whose copies this layer issued, in issue order
+    std::vector<int32_t> tr_demand;     // demand-copied experts in copy order
 
     void lru_unlink(int64_t i) {
         const int64_t p = ring_prev[i], n = ring_next[i];
@@ -299,6 +305,18 @@ int pdx_offload_forward_layer(pdx_offload* h, int32_t layer, const void* x, int6
     PDX_CUDA_TRY(cudaMemcpyAsync(e->h_counts, b.counts, (predict ? 2 : 1) * E * 4, cudaMemcpyDeviceToHost, stream));
     PDX_CUDA_TRY(cudaStreamSynchronize(stream));  // the per-layer grouping sync
     e->st.layers += 1;
+    // trace of this layer (read back by pdx_offload_last_trace)
+    pdx_offload_trace tr{};
+    tr.layer = layer;
+    tr.tokens = T;
+    const pdx_offload_stats st0 = e->st;
+    e->tr_counts.assign(2 * E, 0);
+    std::copy(e->h_counts, e->h_counts + E, e->tr_counts.begin());
+    if (predict) std::copy(e->h_counts + E, e->h_counts + 2 * E, e->tr_counts.begin() + E);
+    e->tr_place.assign(E, PDX_PLACE_NONE);
+    e->tr_prefetch.clear();
+    e->tr_demand.clear();
+    e->trace = tr;  // a layer that fails below leaves this partial trace
 
     // 2. placement
     const int64_t base = static_cast<int64_t>(layer) * E;
@@ -311,10 +329,12 @@ int pdx_offload_forward_layer(pdx_offload* h, int32_t layer, const void* x, int6
         if (e->h_counts[ex] <= 0) continue;
         e->st.expert_uses += 1;
         const int32_t fs = e->fixed_slot[base + ex];
+        tr.routed_experts += 1;
         if (fs >= 0) {
             table[ex] = fs;
             ready.push_back(static_cast<int32_t>(ex));
             if (e->is_warm[base + ex]) e->st.warm_hits += 1; else e->st.hot_hits += 1;
+            e->tr_place[ex] = e->is_warm[base + ex] ? PDX_PLACE_WARM : PDX_PLACE_HOT;
             continue;
         }
         const int32_t ri = e->where[base + ex];
@@ -328,11 +348,24 @@ int pdx_offload_forward_layer(pdx_offload* h, int32_t layer, const void* x, int6
             pinned.push_back(ri);
             table[ex] = static_cast<int32_t>(e->n_fixed + ri);
             ready.push_back(static_cast<int32_t>(ex));
-            if (e->ring_ready[ri] >= 0) waits.push_back(e->ring_ready[ri]);
+            bool loading = false;
+            if (e->ring_ready[ri] >= 0) {
+                waits.push_back(e->ring_ready[ri]);
+                const cudaError_t q = cudaEventQuery(e->copy_ev[e->ring_ready[ri]]);
+                if (q == cudaErrorNotReady) {
+                    loading = true;
+                    cudaGetLastError();  // a pending copy is a status, not an error
+                } else if (q != cudaSuccess) {
+                    return fail(PDX_ERR_CUDA, "copy event: %s", cudaGetErrorString(q));
+                }
+            }
+            e->tr_place[ex] = loading ? PDX_PLACE_LOADING : PDX_PLACE_CACHE;
             continue;
         }
         demand.push_back(static_cast<int32_t>(ex));
+        e->tr_place[ex] = PDX_PLACE_DEMAND;
     }
+    e->tr_demand.assign(demand.begin(), demand.end());
     const uint16_t* host = static_cast<const uint16_t*>(c.host_experts);
     // acquire the least recently used ring slot outside `pinned` for key
     auto copy_in = [&](int64_t key, bool prefetched, int64_t* slot_out) -> int {
@@ -395,7 +428,12 @@ int pdx_offload_forward_layer(pdx_offload* h, int32_t layer, const void* x, int6
         for (int64_t ex = 0; ex < E; ++ex) {
             if (e->h_counts[E + ex] <= 0) continue;
             if (e->fixed_slot[nbase + ex] >= 0 || e->where[nbase + ex] >= 0) continue;
-            if (static_cast<int64_t>(pinned.size() + issued.size()) >= e->n_ring) break;
+            if (static_cast<int64_t>(pinned.size() + issued.size()) >= e->n_ring) {
+                for (int64_t rest = ex; rest < E; ++rest)   // the reference's prefetch_capacity_skipped
+                    if (e->h_counts[E + rest] > 0 && e->fixed_slot[nbase + rest] < 0 && e->where[nbase + rest] < 0)
+                        tr.prefetch_skipped += 1;
+                break;
+            }
             int64_t slot;
             const size_t before = pinned.size();
             pinned.insert(pinned.end(), issued.begin(), issued.end());
@@ -406,6 +444,7 @@ int pdx_offload_forward_layer(pdx_offload* h, int32_t layer, const void* x, int6
                 return st;
             }
             issued.push_back(slot);
+            e->tr_prefetch.push_back(static_cast<int32_t>(ex));
         }
         if (!issued.empty() && (st = mark_ready(issued, nullptr))) return st;
     }
@@ -445,6 +484,45 @@ int pdx_offload_forward_layer(pdx_offload* h, int32_t layer, const void* x, int6
     e->comp_next = (e->comp_next + 1) % OffloadEngine::kEvents;
     PDX_CUDA_TRY(cudaEventRecord(e->comp_ev[done], stream));
     for (int64_t i : pinned) e->ring_last[i] = done;
+    for (int32_t ex = 0; ex < E; ++ex) {
+        tr.hot += e->tr_place[ex] == PDX_PLACE_HOT;
+        tr.warm += e->tr_place[ex] == PDX_PLACE_WARM;
+        tr.cache_ready += e->tr_place[ex] == PDX_PLACE_CACHE;
+        tr.cache_loading += e->tr_place[ex] == PDX_PLACE_LOADING;
+    }
+    tr.demand = static_cast<int32_t>(demand.size());
+    tr.demand_chunks = static_cast<int32_t>(chunks.size());
+    tr.prefetch_issued = static_cast<int32_t>(e->tr_prefetch.size());
+    tr.prefetch_used = static_cast<int32_t>(e->st.prefetch_used - st0.prefetch_used);
+    tr.h2d_bytes = e->st.h2d_bytes - st0.h2d_bytes;
+    e->trace = tr;
+    return ok();
+}
+
+int pdx_offload_last_trace(const pdx_offload* h, pdx_offload_trace* out, int32_t* counts_out, int32_t* placement_out,
+                           int32_t* prefetch_out, int32_t* demand_out) {
+    const OffloadEngine* e = reinterpret_cast<const OffloadEngine*>(h);
+    if (!e || !out) return pdx::fail(PDX_ERR_INVALID, "null offload trace argument");
+    if (e->tr_place.empty()) return pdx::fail(PDX_ERR_INVALID, "no layer has run on this offload handle");
+    *out = e->trace;
+    if (counts_out) std::copy(e->tr_counts.begin(), e->tr_counts.end(), counts_out);
+    if (placement_out) std::copy(e->tr_place.begin(), e->tr_place.end(), placement_out);
+    if (prefetch_out) std::copy(e->tr_prefetch.begin(), e->tr_prefetch.end(), prefetch_out);
+    if (demand_out) std::copy(e->tr_demand.begin(), e->tr_demand.end(), demand_out);
+    return pdx::ok();
+}
+
+int pdx_offload_copy_selected(const pdx_offload* h, int32_t which, int64_t T, int64_t* selected_out,
+                              pdx_stream_t stream) {
+    using namespace pdx;
+    const OffloadEngine* e = reinterpret_cast<const OffloadEngine*>(h);
+    if (!e || !selected_out || (which != 0 && which != 1)) return fail(PDX_ERR_INVALID, "invalid selected copy");
+    if (e->tr_place.empty() || T != e->trace.tokens)
+        return fail(PDX_ERR_INVALID, "T must be the token count of the last forward_layer call");
+    if (which == 1 && e->trace.layer + 1 >= e->cfg.layers)
+        return fail(PDX_ERR_INVALID, "the last layer has no next-layer prediction");
+    OffloadBufs b = carve_offload(e->cfg, T, e->ws, e->ws_bytes, nullptr);
+    PDX_CUDA_TRY(cudaMemcpyAsync(selected_out, b.sel[which], T * e->cfg.top_k * 8, cudaMemcpyDeviceToDevice, stream));
     return ok();
 }
 

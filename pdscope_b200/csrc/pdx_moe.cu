@@ -213,7 +213,7 @@ int encode_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, 
 constexpr int kMaxTopK = 32;
 constexpr int64_t kTailMaxTokens = 64;     // fused route tail up to this many tokens
 constexpr int64_t kPackSingleMax = 1024;   // single-CTA pack up to this many assignments (4 scatter rounds)
-constexpr int64_t kStreamMaxRowsPerExpert = 16;  // auto mode: weight streaming up to this average
+constexpr int64_t kStreamMaxRowsPerExpert = 48;  // auto mode: weight streaming up to this average
 
 int check_route_shape(int64_t T, int64_t H, int64_t E, int32_t k) {
     if (T < 1) return fail(PDX_ERR_INVALID, "empty expert routing (T=%lld)", static_cast<long long>(T));
@@ -233,10 +233,11 @@ bool is_gemm_mode(int mode) { return mode == PDX_FFN_GEMM || mode == PDX_FFN_GEM
 bool stream_shape_ok(int64_t H, int64_t I) { return H % 128 == 0 && I % 128 == 0 && H >= 128 && I >= 128; }
 
 // Auto mode picks the path from the average rows per expert: the
-// weight-streaming path reads each active expert's weights once per 16/32-row
+// weight-streaming path reads each active expert's weights once per 16/32/64-row
 // token tile, the token-tiled GEMM once per 128-row tile at full tensor-core
-// tile efficiency.  Measured on one Qwen3-30B-A3B layer (E=128, k=8): streaming
-// is ahead up to T = 256 (16 rows per expert), the GEMM from T = 384 on.
+// tile efficiency.  Measured on one Qwen3-30B-A3B layer (E=128, k=8, CUDA-graph
+// replay): streaming is ahead up to T = 512 (32 rows per expert: 265 vs 272 us),
+// the GEMM from T = 1024 (64 rows per expert: 294 vs 309 us) on.
 int resolve_mode(int32_t mode, int64_t rows, int64_t E, int64_t H, int64_t I) {
     if (mode != PDX_FFN_AUTO) return mode;
     const bool few_rows = rows <= kStreamMaxRowsPerExpert * std::max<int64_t>(E, 1);

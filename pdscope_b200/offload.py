@@ -118,6 +118,318 @@ class OffloadStats:
         return dict(self.__dict__)
 
 
+class LedgerPlacer:
+    """Device slot placement driven by an ExpertCache-style ticket ledger.
+
+    The reference keeps expert residency in ``ExpertCache``
+    (expertbench/cache.py:353-647): ``on_demand`` declares a layer's routed
+    experts, ``begin_load`` reserves a copy (evicting by its own policy) and
+    returns a ticket in the 'cache' pool or a 'demand_staging' slot,
+    ``submit`` / ``complete_load`` bracket the transfer (the byte closure
+    h2d_bytes_submitted == h2d_bytes_completed, :552-574), ``acquire`` /
+    ``release`` bracket the compute, ``end_demand`` closes the layer and
+    ``take_retired`` hands back the tickets whose memory may be reused.  This
+    class maps those tickets onto device slots and keeps the ledger's calls
+    in that order, while the copies and kernels themselves run ahead on the
+    device (ordered by events): a transfer is reported complete, and a use
+    released, only once its event has finished.
+
+    ``ledger``: the ExpertCache (or an object with its API); ``key_of(layer,
+    expert)`` and ``demand_of(request, step, layer)`` build its key and demand
+    ids.  Slots: ``cache_slots`` cache-pool slots then one slot per staging
+    slot of the ledger.  ``device``: copy issue and event queries --
+    ``copy(key, slot, after) -> event`` (a copy into ``slot`` that starts after
+    the event ``after``), ``done(event) -> bool`` and ``wait(event)`` (host).
+    CUDA-free, so the reference's own ledger can drive it on any host.
+    """
+
+    def __init__(self, ledger, *, key_of, demand_of, cache_slots, device, request="offload"):
+        self.ledger, self.key_of, self.demand_of, self.device = ledger, key_of, demand_of, device
+        self.request = request
+        self.n_cache = cache_slots
+        self.free = list(range(cache_slots - 1, -1, -1))
+        self.slot_of = {}            # ticket -> slot
+        self.copy_event = {}         # ticket -> event of its submitted, not yet completed transfer
+        self.last_use = {}           # slot -> event of its last reader
+        self.open = None             # (identity, use handles, done event) of the layer awaiting its close
+        self.identity = None         # demand id of the layer being placed
+        self.prefetch_skipped = 0
+
+    # -- tickets and slots --------------------------------------------------------
+    def _slot_for(self, ticket):
+        if ticket.pool == "demand_staging":
+            slot = self.n_cache + ticket.slot
+        else:
+            if not self.free:
+                raise RuntimeError("ledger admitted more cache copies than the device pool has slots")
+            slot = self.free.pop()
+        self.slot_of[ticket] = slot
+        return slot
+
+    def _load(self, key, origin):
+        ticket = self.ledger.begin_load(key, origin=origin)
+        if ticket in self.slot_of:             # a repeated reservation returns the live ticket
+            return ticket, False
+        self._retire()                         # the reservation's evictions free their slots now
+        slot = self._slot_for(ticket)
+        self.copy_event[ticket] = self.device.copy(key, slot, self.last_use.get(slot))
+        self.ledger.submit(ticket)
+        return ticket, True
+
+    def _complete(self, ticket, wait):
+        ev = self.copy_event.get(ticket)
+        if ev is None:
+            return True
+        if not self.device.done(ev):
+            if not wait:
+                return False
+            self.device.wait(ev)
+        self.ledger.complete_load(ticket)
+        del self.copy_event[ticket]
+        return True
+
+    def _retire(self):
+        for ticket in self.ledger.take_retired():
+            slot = self.slot_of.pop(ticket, None)
+            self.copy_event.pop(ticket, None)
+            if slot is not None and slot < self.n_cache:
+                self.free.append(slot)
+
+    def load_initial(self, keys):
+        """The initial hotset (origin 'initial'), loaded before the first demand."""
+        for key in keys:
+            ticket, _ = self._load(key, "initial")
+            self._complete(ticket, wait=True)
+
+    # -- one layer ------------------------------------------------------------------
+    def close_layer(self):
+        """Closes the open layer once its compute event finished: release its
+        uses, end its demand, complete finished transfers, recycle slots."""
+        if self.open is None:
+            return
+        identity, handles, done = self.open
+        self.device.wait(done)
+        for h in handles:
+            self.ledger.release(h)
+        self.ledger.end_demand(identity)
+        self.open = None
+        for ticket in list(self.copy_event):
+            self._complete(ticket, wait=False)
+        self._retire()
+
+    def place_layer(self, step, layer, counts, predicted=()):
+        """Slots for this layer's routed experts ``counts`` {expert: tokens} and
+        prefetch copies of ``predicted`` (next-layer experts).  Returns
+        (slot of each routed expert, {expert: copy event} of the routed experts
+        whose transfers are still in flight, demand experts, prefetched
+        experts)."""
+        self.close_layer()
+        identity = self.identity = self.demand_of(self.request, step, layer)
+        keys = {e: self.key_of(layer, e) for e in counts}
+        self.ledger.on_demand(identity, {keys[e]: int(n) for e, n in counts.items()})
+        slots, pending, demand = {}, {}, []
+        for e in sorted(counts):
+            key = keys[e]
+            view = self.ledger.lookup(key)
+            if view is None:
+                ticket, _ = self._load(key, "demand")
+                demand.append(e)
+            else:
+                ticket = view.ticket
+            slots[e] = self.slot_of[ticket]
+            if ticket in self.copy_event:
+                pending[e] = self.copy_event[ticket]
+        issued = []
+        for e in predicted:
+            key = self.key_of(layer + 1, e)
+            if self.ledger.lookup(key) is not None:
+                continue
+            try:
+                self._load(key, "prefetch")
+            except Exception as exc:           # CapacityBlocked: no evictable cache bytes for speculation
+                if type(exc).__name__ != "CapacityBlocked":
+                    raise
+                self.prefetch_skipped += 1
+                continue
+            issued.append(e)
+        return slots, pending, demand, issued
+
+    def begin_compute(self, layer, counts, done):
+        """The layer's compute is enqueued (``done`` = its completion event):
+        the transfers it reads complete (host wait), its uses are acquired,
+        and its slots are marked read until ``done``."""
+        handles = []
+        for e in sorted(counts):
+            key = self.key_of(layer, e)
+            ticket = self.ledger.lookup(key).ticket
+            self._complete(ticket, wait=True)
+            handles.append(self.ledger.acquire(key))
+            self.last_use[self.slot_of[ticket]] = done
+        self.open = (self.identity, handles, done)
+
+    def drain(self):
+        """Closes the open layer and completes every transfer still in flight
+        (the ledger's byte closure holds afterwards)."""
+        self.close_layer()
+        for ticket in list(self.copy_event):
+            self._complete(ticket, wait=True)
+        self._retire()
+
+
+class _CopyEngine:
+    """LedgerPlacer's device side for an OffloadMoEStack: one cudaMemcpyAsync
+    of the expert's 9 MiB slot from pinned host memory on the copy stream,
+    after the slot's last reader, and an event per copy."""
+
+    def __init__(self, stack):
+        self.stack = stack
+
+    def copy(self, key, slot, after):
+        st = self.stack
+        l, e = (key.layer, key.expert) if hasattr(key, "layer") else key
+        cs = st.copy_stream
+        if after is not None:
+            cs.wait_event(after)
+        with torch.cuda.stream(cs):
+            st.pool[slot * st.per:(slot + 1) * st.per].copy_(st.host[l, e], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(cs)
+        return ev
+
+    def done(self, ev):
+        return ev.query()
+
+    def wait(self, ev):
+        ev.synchronize()
+
+
+class TicketLedger:
+    """A small ticket ledger with ExpertCache's call protocol, for hosts
+    without the reference package: LRU over cache slots of equal size,
+    demand-staging fallback when the cache has no evictable entry, byte
+    counters with the same names.  Keys are (layer, expert) tuples and demand
+    ids (request, step, layer) tuples; ``CapacityBlocked`` is raised as the
+    reference does when speculation finds no evictable room."""
+
+    class CapacityBlocked(RuntimeError):
+        pass
+
+    @dataclass(frozen=True)
+    class Ticket:
+        generation: int
+        key: tuple
+        pool: str
+        slot: object
+
+    @dataclass
+    class View:
+        ticket: object
+        state: str
+
+    def __init__(self, cache_slots, staging_slots, nbytes, initial_hotset=()):
+        self.cache_slots, self.staging_slots, self.nbytes = cache_slots, staging_slots, nbytes
+        self.initial_hotset = frozenset(initial_hotset)
+        self._entries = {}           # key -> dict(ticket, ready, submitted, users)
+        self._lru = OrderedDict()    # cache keys, least recent first
+        self._staging_busy = set()
+        self._retired = []
+        self._gen = 0
+        self._active = None          # (identity, remaining keys)
+        self._stats = dict(h2d_bytes_submitted=0, h2d_bytes_completed=0, gpu_completed_experts=0, evictions=0,
+                           demand_loads_submitted=0, prefetch_loads_submitted=0, initial_loads_submitted=0)
+
+    def stats(self):
+        return dict(self._stats)
+
+    def lookup(self, key):
+        ent = self._entries.get(key)
+        if ent is None:
+            return None
+        return TicketLedger.View(ent["ticket"], "in_use" if ent["users"] else "ready" if ent["ready"] else "loading")
+
+    def on_demand(self, identity, counts):
+        if self._active is not None:
+            raise RuntimeError("another layer-step demand is active")
+        self._active = (identity, set(counts))
+        for key in counts:
+            if key in self._lru:
+                self._lru.move_to_end(key)
+
+    def _evictable(self, key):
+        ent = self._entries[key]
+        return ent["ready"] and not ent["users"] and not (self._active and key in self._active[1])
+
+    def begin_load(self, key, *, origin="demand", admit=True):
+        if key in self._entries:
+            return self._entries[key]["ticket"]
+        cached = sum(1 for k in self._entries if self._entries[k]["ticket"].pool == "cache")
+        victim = None
+        if cached >= self.cache_slots:
+            victim = next((k for k in self._lru if self._evictable(k)), None)
+        if cached < self.cache_slots or victim is not None:
+            if victim is not None:
+                self._retired.append(self._entries.pop(victim)["ticket"])
+                del self._lru[victim]
+                self._stats["evictions"] += 1
+            pool, slot = "cache", None
+            self._lru[key] = None
+        elif origin == "demand":
+            free = [i for i in range(self.staging_slots) if i not in self._staging_busy]
+            if not free:
+                raise TicketLedger.CapacityBlocked("demand staging busy")
+            pool, slot = "demand_staging", free[0]
+            self._staging_busy.add(slot)
+        else:
+            raise TicketLedger.CapacityBlocked("no evictable cache bytes")
+        self._gen += 1
+        t = TicketLedger.Ticket(self._gen, key, pool, slot)
+        self._entries[key] = dict(ticket=t, ready=False, submitted=False, users=set(), origin=origin)
+        return t
+
+    def submit(self, ticket):
+        ent = self._entries[ticket.key]
+        if ent["ticket"] != ticket or ent["submitted"]:
+            raise RuntimeError("stale or repeated submission")
+        ent["submitted"] = True
+        self._stats["h2d_bytes_submitted"] += self.nbytes
+        self._stats[ent["origin"] + "_loads_submitted"] += 1
+
+    def complete_load(self, ticket):
+        ent = self._entries[ticket.key]
+        if ent["ticket"] != ticket or not ent["submitted"] or ent["ready"]:
+            raise RuntimeError("completion needs one submitted, incomplete transfer")
+        ent["ready"] = True
+        self._stats["h2d_bytes_completed"] += self.nbytes
+
+    def acquire(self, key):
+        ent = self._entries[key]
+        if not ent["ready"]:
+            raise RuntimeError("weights are not ready")
+        self._gen += 1
+        ent["users"].add(self._gen)
+        return (key, self._gen)
+
+    def release(self, handle):
+        key, serial = handle
+        ent = self._entries[key]
+        ent["users"].remove(serial)
+        if not ent["users"]:
+            self._active[1].discard(key)
+            self._stats["gpu_completed_experts"] += 1
+            if ent["ticket"].pool == "demand_staging":
+                self._staging_busy.discard(ent["ticket"].slot)
+                self._retired.append(self._entries.pop(key)["ticket"])
+
+    def end_demand(self, identity):
+        if self._active is None or self._active[0] != identity or self._active[1]:
+            raise RuntimeError("cannot finish layer: some experts have not completed")
+        self._active = None
+
+    def take_retired(self):
+        out, self._retired = self._retired, []
+        return out
+
+
 def zipf_hot_sets(gates, count):
     """The ``count`` experts of each layer with the largest router offset on
     the Zipf coordinate (hidden column 0), hottest first: a hot table by Zipf
@@ -170,7 +482,7 @@ class OffloadMoEStack:
     """
 
     def __init__(self, gates, host_experts, hot, *, hidden, inter, cache_slots, top_k=8, normalize=True,
-                 prefetch=True, chunk=16, warm=None):
+                 prefetch=True, chunk=16, warm=None, ledger=None, key_of=None, demand_of=None, request="offload"):
         self.gates = list(gates)
         self.L = len(self.gates)
         self.E = self.gates[0].shape[0]
@@ -182,6 +494,11 @@ class OffloadMoEStack:
         self.host = host_experts
         self.per = 3 * inter * hidden
         self.dev = self.gates[0].device
+        self.placer = None
+        self._step = -1
+        if ledger is not None:
+            self._init_ledger(ledger, hot, warm, key_of, demand_of, request, prefetch, chunk)
+            return
         self.hot = [list(h) for h in hot]
         self.warm = [list(w) for w in warm] if warm is not None else [[] for _ in range(self.L)]
         n_hot = sum(len(h) for h in self.hot)
@@ -220,6 +537,45 @@ class OffloadMoEStack:
         self.counts_host = torch.zeros((2, self.E), **i32).pin_memory()
         self._bufs = {}
         torch.cuda.synchronize(self.dev)
+
+    def _init_ledger(self, ledger, hot, warm, key_of, demand_of, request, prefetch, chunk):
+        """Residency kept by a ticket ledger (ExpertCache's API): its cache pool
+        and staging slots are the device pool, its initial hotset the hot
+        table; LedgerPlacer maps tickets to slots."""
+        if warm:
+            raise ValueError("with a ledger, residency beyond the hot set is the ledger's own policy")
+        slot_bytes = self.per * 2
+        n_cache = getattr(ledger, "cache_slots", None) or ledger.cache_bytes // slot_bytes
+        n_stage = getattr(ledger, "staging_slots", None) or len(ledger.staging_slot_bytes)
+        n_slots = n_cache + n_stage
+        self.pool = torch.empty(n_slots * self.per, dtype=torch.bfloat16, device=self.dev)
+        self.copy_stream = torch.cuda.Stream(device=self.dev)
+        self.prefetch, self.chunk = prefetch, max(1, chunk)
+        self.stats = OffloadStats()
+        key_of = key_of or (lambda l, e: (l, e))
+        demand_of = demand_of or (lambda r, s, l: (r, s, l))
+        self.placer = LedgerPlacer(ledger, key_of=key_of, demand_of=demand_of, cache_slots=n_cache,
+                                   device=_CopyEngine(self), request=request)
+        self.ledger = ledger
+        base = self.pool.data_ptr()
+        self._weights = dict(gate=base, up=base + self.I * self.H * 2, down=base + 2 * self.I * self.H * 2,
+                             gate_stride=self.per, up_stride=self.per, down_stride=self.per, num_slots=n_slots)
+        i32 = dict(dtype=torch.int32)
+        self.table_host = torch.zeros((self.L, self.E), **i32).pin_memory()
+        self.table_dev = torch.zeros((self.L, self.E), **i32, device=self.dev)
+        self.max_launch = 1 + -(-self.E // self.chunk)
+        self.active_host = torch.zeros((self.max_launch, self.E + 1), **i32).pin_memory()
+        self.active_dev = torch.zeros((self.max_launch, self.E + 1), **i32, device=self.dev)
+        self.counts_host = torch.zeros((2, self.E), **i32).pin_memory()
+        self._bufs = {}
+        self.placer.load_initial([key_of(l, e) for l, hs in enumerate(hot) for e in hs])
+        torch.cuda.synchronize(self.dev)
+
+    def finish(self):
+        """Ledger mode: close the last layer and complete every transfer in
+        flight (the ledger's byte closure holds afterwards)."""
+        if self.placer is not None:
+            self.placer.drain()
 
     # ---- buffers (grow-free per token count) ------------------------------------------
     def _buffers(self, t):
@@ -309,6 +665,8 @@ class OffloadMoEStack:
         needed = np.nonzero(counts[0])[0].tolist()
         self.stats.layers += 1
         self.stats.expert_uses += len(needed)
+        if self.placer is not None:
+            return self._forward_layer_ledger(l, x, out, residual, norm, counts, needed, predict, b, comp)
 
         pinned, ready, waits, demand = set(), [], [], []
         table = self.table_host[l].numpy()
@@ -388,11 +746,56 @@ class OffloadMoEStack:
             self.ring.slots[idx].last_use = done
         return out
 
+    def _forward_layer_ledger(self, l, x, out, residual, norm, counts, needed, predict, b, comp):
+        """forward_layer's placement and launches when a ledger keeps residency."""
+        t = x.shape[0]
+        cur = {e: int(counts[0][e]) for e in needed}
+        predicted = np.nonzero(counts[1])[0].tolist() if predict else []
+        slots, pending, demand, issued = self.placer.place_layer(self._step, l, cur, predicted)
+        self.stats.demand_copies += len(demand)
+        self.stats.prefetch_copies += len(issued)
+        self.stats.h2d_bytes += (len(demand) + len(issued)) * self.per * 2
+        self.stats.cache_hits += len(cur) - len(demand)
+        table = self.table_host[l].numpy()
+        for e, s in slots.items():
+            table[e] = s
+        demand_set = set(demand)
+        ready = [e for e in needed if e not in demand_set]
+        chunks = [demand[c0:c0 + self.chunk] for c0 in range(0, len(demand), self.chunk)]
+        act = self.active_host.numpy()
+        lists = [ready] + chunks
+        for i, lst in enumerate(lists):
+            act[i, 0] = len(lst)
+            act[i, 1:1 + len(lst)] = lst
+        self.table_dev[l].copy_(self.table_host[l], non_blocking=True)
+        self.active_dev[:len(lists)].copy_(self.active_host[:len(lists)], non_blocking=True)
+        rows, ws, cur_r = b["rows"], b["ws"], b["cur"]
+        for e in ready:                      # cached experts whose transfers are still landing
+            if e in pending:
+                comp.wait_event(pending[e])
+        if ready:
+            self._ffn(l, x, cur_r, 0, rows, ws)
+        for c, part in enumerate(chunks):
+            for e in part:
+                comp.wait_event(pending[e])
+            self._ffn(l, x, cur_r, 1 + c, rows, ws)
+        if norm:
+            check(lib.pdx_combine_layernorm(_ptr(rows), _ptr(cur_r["w"]), _ptr(cur_r["inverse"]), t, self.k, self.H,
+                                            _ptr(residual), ctypes.c_float(LN_EPS), _ptr(out), _stream()))
+        else:
+            check(lib.pdx_combine(_ptr(rows), _ptr(cur_r["w"]), _ptr(cur_r["inverse"]), t, self.k, self.H,
+                                  _ptr(residual), _ptr(out), _stream()))
+        done = torch.cuda.Event()
+        done.record(comp)
+        self.placer.begin_compute(l, cur, done)
+        return out
+
     def forward(self, x):
         """Every layer on ``x`` [T, H]; layer l+1's input is
         layer_norm(MoE_l(x_l) + x_l) (the next-layer activation of the resident
         stack).  Returns a buffer owned by the stack (valid until the next call
         with the same token count)."""
+        self._step += 1
         b = self._buffers(x.shape[0])
         h = x
         for l in range(self.L):
@@ -457,8 +860,58 @@ class NativeOffloadMoEStack:
                                             _stream()))
         return out
 
-    def forward(self, x):
-        """Every layer on ``x``; layer l+1's input is layer_norm(MoE_l(x_l) + x_l)."""
+    _PLACES = {_lib.PLACE_HOT: "hot", _lib.PLACE_WARM: "static", _lib.PLACE_CACHE: "cache",
+               _lib.PLACE_LOADING: "cache_loading", _lib.PLACE_DEMAND: "demand"}
+
+    def trace_row(self, step, *, diagnostics=True):
+        """The reference's per-layer row (the dict PDScopeCudaRuntime.forward
+        returns, expertbench/pdscope_runtime.py:492-512) for the last
+        forward_layer call, built from the native engine's own trace
+        (pdx_offload_last_trace): token counts, the decision the engine
+        executed (every routed expert on the GPU: resident, cached or copied
+        on demand), the prefetch ledger and the routing fingerprints."""
+        tr = _lib.OffloadTrace()
+        E = self.E
+        counts = (ctypes.c_int32 * (2 * E))()
+        place = (ctypes.c_int32 * E)()
+        pre = (ctypes.c_int32 * E)()
+        dem = (ctypes.c_int32 * E)()
+        check(lib.pdx_offload_last_trace(self._h, ctypes.byref(tr), counts, place, pre, dem))
+        layer, t = tr.layer, tr.tokens
+        cur = {e: counts[e] for e in range(E) if counts[e] > 0}
+        nxt = {e: counts[E + e] for e in range(E) if counts[E + e] > 0}
+        placements = {e: self._PLACES[place[e]] for e in cur}
+        demand = [dem[i] for i in range(tr.demand)]
+        resident = sorted((e for e in cur if place[e] != _lib.PLACE_DEMAND), key=lambda e: (-cur[e], e))
+        issued = [pre[i] for i in range(tr.prefetch_issued)]
+        phase = "prefill" if step == 0 else "decode"
+        decision = dict(phase=phase, mode="offload_native", cpu_queue=[], gpu_resident_queue=resident,
+                        on_demand_queue=demand, prefetch_queue=issued, unload_queue=[],
+                        placements={e: "gpu" for e in sorted(cur)}, slot_kind=placements)
+        sha, nsha = None, None
+        if diagnostics:
+            from .runtime import tensor_hash
+            sel = torch.empty((t, self.k), dtype=torch.int64, device=self.dev)
+            check(lib.pdx_offload_copy_selected(self._h, 0, t, _ptr(sel), _stream()))
+            sha = tensor_hash(sel)
+            if layer + 1 < self.L and nxt:
+                check(lib.pdx_offload_copy_selected(self._h, 1, t, _ptr(sel), _stream()))
+                nsha = tensor_hash(sel)
+        return dict(phase=phase, step=step, layer=layer, token_counts=cur, dispatch="compact", decision=decision,
+                    prefetch_issued=issued, prefetch_capacity_skipped=tr.prefetch_skipped,
+                    next_prediction_counts=nxt, predictor="next_layer_gate_on_current_activation",
+                    scheduler="native_offload_engine", selected_sha256=sha, next_selected_sha256=nsha,
+                    ready_at_reveal=tr.hot + tr.warm + tr.cache_ready, loading_at_reveal=tr.cache_loading,
+                    counters=dict(h2d_bytes_completed=tr.h2d_bytes, demand_copies=tr.demand,
+                                  prefetch_copies=tr.prefetch_issued, prefetch_used=tr.prefetch_used,
+                                  gpu_completed_experts=tr.routed_experts, cpu_completed_experts=0),
+                    ping_pong_slots=[], merge_mode="fused", demand_chunks=tr.demand_chunks,
+                    pipeline="copy-engine demand chunks, then next-layer prefetch on the same copy stream",
+                    measured_performance=False)
+
+    def forward(self, x, *, step=None, rows=None):
+        """Every layer on ``x``; layer l+1's input is layer_norm(MoE_l(x_l) + x_l).
+        With ``rows`` (a list) and ``step``, appends each layer's trace row."""
         t = x.shape[0]
         acts = self._acts.get(t)
         if acts is None:
@@ -466,6 +919,8 @@ class NativeOffloadMoEStack:
         h = x
         for l in range(self.L):
             self.forward_layer(l, h, acts[l % 2], residual=h, norm=True)
+            if rows is not None:
+                rows.append(self.trace_row(step if step is not None else 0))
             h = acts[l % 2]
         return h
 

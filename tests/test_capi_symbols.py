@@ -55,7 +55,12 @@ def test_workspace_queries_are_monotone():
     a = lib.pdx_layer_workspace_bytes(1, 2048, 128, 8, 768, 0)
     b = lib.pdx_layer_workspace_bytes(512, 2048, 128, 8, 768, 0)
     c = lib.pdx_layer_workspace_bytes(512, 2048, 128, 8, 768, 2)
-    assert 0 < a < b <= c
+    d = lib.pdx_layer_workspace_bytes(4096, 2048, 128, 8, 768, 0)
+    assert 0 < a < b < d and 0 < c < d
+    # auto mode sizes for the path it runs: the weight-streaming path up to 48
+    # rows per expert (T=512 here), the token-tiled GEMM beyond
+    assert b == lib.pdx_layer_workspace_bytes(512, 2048, 128, 8, 768, 1)
+    assert d == lib.pdx_layer_workspace_bytes(4096, 2048, 128, 8, 768, 2)
     assert lib.pdx_pack_workspace_bytes(4096, 8, 128) >= 8 * 128 * 4
     assert lib.pdx_route_workspace_bytes(64, 128) >= 64 * 128 * 2
     # prefill sizes also hold the split-K router partials (up to 4 x T x E FP64)

@@ -122,3 +122,80 @@ def test_native_engine_rejects_bad_calls(stacks):
     with pytest.raises(ValueError):
         nat.forward_layer(L, x[:4], torch.empty_like(x[:4]))        # layer out of range
     nat.close()
+
+
+def test_native_engine_trace_rows(stacks):
+    """The C++ engine reports each layer as the reference's row
+    (pdscope_runtime.py:492-512): routed counts equal the device routing,
+    every routed expert is placed exactly once (hot / static / cache / demand),
+    the row's prefetch ledger and H2D bytes add up to the engine's counters,
+    and selected_sha256 fingerprints the routing the reference would hash."""
+    import hashlib
+    from pdscope_b200.runtime import pack, route
+    from pdscope_b200.stack import activations
+    res, _ = stacks
+    nat = _fresh(res, True)
+    before = nat.stats.as_dict()
+    rows = []
+    for step, t_count in enumerate((12, 1, 1, 1)):
+        x = activations(t_count, H, seed=1500 + step, zipf=True)
+        rows_before = len(rows)
+        nat.forward(x, step=step, rows=rows)
+        torch.cuda.synchronize()
+        r0 = rows[rows_before]
+        assert r0["layer"] == 0 and r0["phase"] == ("prefill" if step == 0 else "decode")
+        sel = route(x, res.gates[0], K, True).selected
+        counts = torch.bincount(sel.flatten(), minlength=E).tolist()
+        assert r0["token_counts"] == {e: c for e, c in enumerate(counts) if c}
+        assert r0["selected_sha256"] == hashlib.sha256(sel.cpu().contiguous().view(torch.uint8).numpy()
+                                                       .tobytes()).hexdigest()
+        nsel = route(x, res.gates[1], K, True).selected
+        ncounts = torch.bincount(nsel.flatten(), minlength=E).tolist()
+        assert r0["next_prediction_counts"] == {e: c for e, c in enumerate(ncounts) if c}
+    assert len(rows) == 4 * L
+    s = nat.stats.as_dict()
+    d = {k: s[k] - before[k] for k in s}
+    for r in rows:
+        dec = r["decision"]
+        routed = set(r["token_counts"])
+        assert set(dec["gpu_resident_queue"]) | set(dec["on_demand_queue"]) == routed
+        assert not set(dec["gpu_resident_queue"]) & set(dec["on_demand_queue"])
+        assert dec["cpu_queue"] == [] and set(dec["slot_kind"]) == routed
+        assert r["counters"]["h2d_bytes_completed"] == (len(dec["on_demand_queue"]) + len(r["prefetch_issued"])) \
+            * 3 * H * I * 2
+    assert sum(r["counters"]["h2d_bytes_completed"] for r in rows) == d["h2d_bytes"]
+    assert sum(len(r["decision"]["on_demand_queue"]) for r in rows) == d["demand_copies"]
+    assert sum(len(r["prefetch_issued"]) for r in rows) == d["prefetch_copies"]
+    assert sum(r["counters"]["prefetch_used"] for r in rows) == d["prefetch_used"]
+    assert rows[-1]["next_prediction_counts"] == {} and rows[-1]["next_selected_sha256"] is None
+    nat.close()
+
+
+def test_offload_through_a_ticket_ledger(stacks):
+    """Residency kept by a ticket ledger with ExpertCache's protocol
+    (expertbench/cache.py:353-647; the reference's own ExpertCache drives the
+    same LedgerPlacer in tests/test_offload_ledger.py): outputs stay equal to
+    the all-resident stack through demand copies, evictions and prefetches,
+    and the ledger's byte closure holds (h2d_bytes_submitted ==
+    h2d_bytes_completed == every copy issued, cache.py:552-574)."""
+    from pdscope_b200.offload import OffloadMoEStack, TicketLedger, zipf_hot_sets
+    from pdscope_b200.stack import activations
+    res, off = stacks
+    hot = zipf_hot_sets(res.gates, 2)
+    nbytes = 3 * H * I * 2
+    ledger = TicketLedger(cache_slots=18, staging_slots=2, nbytes=nbytes,
+                          initial_hotset=[(l, e) for l, hs in enumerate(hot) for e in hs])
+    st = OffloadMoEStack(res.gates, off.host, hot, hidden=H, inter=I, cache_slots=0, top_k=K, chunk=3,
+                         ledger=ledger)
+    for step, t_count in enumerate((12, 1, 1, 40, 1, 1, 7)):
+        x = activations(t_count, H, seed=1700 + step, zipf=True)
+        want = _resident(res, x)
+        got = st.forward(x).clone()
+        torch.cuda.synchronize()
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16)), (step, t_count)
+    st.finish()
+    s = ledger.stats()
+    copies = st.stats.demand_copies + st.stats.prefetch_copies + len(ledger.initial_hotset)
+    assert s["h2d_bytes_submitted"] == s["h2d_bytes_completed"] == copies * nbytes
+    assert s["evictions"] > 0 and st.stats.prefetch_copies > 0
+    assert s["gpu_completed_experts"] == st.stats.expert_uses

@@ -49,7 +49,8 @@ def test_hot_file_round_trip(tmp_path):
     p = tmp_path / "hot.txt"
     write_hot_file(p, hot)
     lines = p.read_text().splitlines()
-    assert lines[0] == "layer,expert" and lines[1] == "0,5"
+    # the reference's hot/qwen.txt format: no header, hottest rank of every layer first
+    assert lines == ["0,5", "1,2", "0,1", "1,0", "0,7", "1,3"]
     assert load_hot_file(p, 2, 2) == [[5, 1], [2, 0]]
     assert load_hot_file(p, 3, 1) == [[5, 1, 7]]
 
