@@ -751,6 +751,11 @@ def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
                                launches_per_step=launches,
                                local_weight_gb_per_step=local_bytes / 1e9,
                                hbm_gbs_step_per_gpu=local_bytes / 1e9 / (ms / K / 1e3))
+        if peer is not None:
+            # where a layer's time goes: eager layers (host launch gaps included) with CUDA events between the
+            # exchange stages (max over ranks of each stage's mean)
+            stages = stack.stage_times_us(t_count, layers=min(8, L), repeats=2)
+            decode[t_count]["stage_us_per_layer_eager"] = {name: max_over_ranks(v) for name, v in sorted(stages.items())}
     t_count = headline_t
     x, y = stack.io(t_count)
     host_in = activations(t_count, H, device=dev, seed=5 + rank).cpu().pin_memory()

@@ -16,8 +16,8 @@
 // the layer (k_ep_wait_back), so the graph of a decode step replays unchanged.
 // Waits are bounded (2 s unless pdx_set_flag_wait_limit_ns sets another
 // limit); on a timeout the error word is raised and the layout is left empty,
-// so nothing downstream reads or writes outside its buffers.  Every TMA-free, plain st/ld over NVLink; no cluster or multicast
-// operation is involved.
+// so nothing downstream reads or writes outside its buffers.  Everything is
+// plain st/ld over NVLink: no TMA, no cluster or multicast operation.
 #include "pdx_common.cuh"
 
 namespace pdx {
@@ -142,52 +142,15 @@ __global__ void __launch_bounds__(1024) k_ep_layout_p2p(int R, int EL, int64_t C
     __shared__ int s_blk[kEpMaxExperts];
     __shared__ int s_grp[kEpMaxExperts];
     __shared__ int s_off[kEpMaxExperts + 1];
+    __shared__ int s_src[32], s_tot[kEpMaxExperts];
     const int n = R * EL;
     const int32_t* cnt = reinterpret_cast<const int32_t*>(lay.cnt[me]);
     for (int i = threadIdx.x; i < n; i += blockDim.x) s_cnt[i] = ok ? __ldcg(cnt + i) : 0;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        // a source's counts must fit its block: clamp (and flag) anything else
-        for (int s = 0; s < R; ++s) {
-            int64_t run = 0;
-            for (int l = 0; l < EL; ++l) {
-                int c = s_cnt[s * EL + l];
-                if (c < 0 || run + c > C) {
-                    raise_error(PDX_DEVERR_BAD_EXPERT);
-                    c = 0;
-                }
-                s_cnt[s * EL + l] = c;
-                run += c;
-            }
-        }
-        for (int s = 0; s < R; ++s) {
-            int64_t run = static_cast<int64_t>(s) * C;
-            for (int l = 0; l < EL; ++l) {
-                s_blk[s * EL + l] = static_cast<int>(run);
-                run += s_cnt[s * EL + l];
-            }
-        }
-        int g = 0, n_active = 0;
-        for (int l = 0; l < EL; ++l) {
-            s_off[l] = g;
-            int tot = 0;
-            for (int s = 0; s < R; ++s) {
-                s_grp[s * EL + l] = g + tot;
-                tot += s_cnt[s * EL + l];
-            }
-            if (tot > 0) active_l[1 + n_active++] = l;
-            g += tot;
-        }
-        s_off[EL] = g;
-        active_l[0] = n_active;
-    }
-    __syncthreads();
+    // a source's counts must fit its block: clamp (and flag) anything else
+    ep_layout_block(s_cnt, R, EL, C, true, s_blk, s_grp, s_off, s_src, s_tot, active_l);
     for (int i = threadIdx.x; i <= EL; i += blockDim.x) offsets_l[i] = s_off[i];
-    for (int i = 0; i < n; ++i) {
-        const int c = s_cnt[i], b = s_blk[i], gs = s_grp[i];
-        for (int j = threadIdx.x; j < c; j += blockDim.x)
-            if (gs + j < rows_cap) perm[gs + j] = b + j;
-    }
+    ep_layout_perm(s_blk, s_grp, s_off, R, EL, rows_cap, perm);
 }
 
 // Return: regrouped FFN row g (receive position perm[g] = s*C + pos) -> back

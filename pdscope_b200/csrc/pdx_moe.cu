@@ -978,7 +978,7 @@ int pdx_ep_dispatch(const void* x, const int32_t* tokens, const int32_t* positio
 int pdx_ep_layout(const int32_t* recv_counts, int32_t ranks, int64_t local_experts, int64_t capacity,
                   int64_t rows_cap, int32_t* offsets_l, int32_t* active_l, int32_t* perm, pdx_stream_t stream) {
     if (!recv_counts || !offsets_l || !active_l || !perm) return fail(PDX_ERR_INVALID, "null EP argument");
-    if (ranks < 1 || local_experts < 1 || capacity < 0) return fail(PDX_ERR_INVALID, "invalid EP layout");
+    if (ranks < 1 || ranks > 32 || local_experts < 1 || capacity < 0) return fail(PDX_ERR_INVALID, "invalid EP layout");
     if (ranks * local_experts > kEpMaxExperts) return fail(PDX_ERR_UNSUPPORTED, "more than %d experts", kEpMaxExperts);
     if (rows_cap < 0 || rows_cap >= (int64_t(1) << 31)) return fail(PDX_ERR_UNSUPPORTED, "receive buffer too large");
     PDX_PDL_TRY(launch_pdl(k_ep_layout, dim3(1), dim3(1024), 0, stream, recv_counts, static_cast<int>(ranks),

@@ -211,10 +211,16 @@ class ExpertParallelMoE:
         return self.ops.combine(back, back.shape[0], d.weights, d.inverse, residual)
 
     # ---- padded exchange over NVLink peer memory ----------------------------------------
-    def forward_p2p(self, x, peer, layer, residual=None, norm=False):
+    def forward_p2p(self, x, peer, layer, residual=None, norm=False, marks=None):
         """The padded layer with the exchange done by peer stores and flags
         (pdx_ep_dispatch_p2p ... pdx_ep_wait_back) instead of all-to-alls.
-        With ``norm`` the output is layer_norm(MoE(x) + residual)."""
+        With ``norm`` the output is layer_norm(MoE(x) + residual).  ``marks``
+        (a list) receives (stage, CUDA event) pairs recorded after each stage."""
+        def mark(name):
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                marks.append((name, ev))
         t_count, hidden = x.shape
         cap = self.capacity(t_count)
         if cap > peer.cap_max:
@@ -223,26 +229,34 @@ class ExpertParallelMoE:
                 not 0 <= layer < peer.L:
             raise ValueError("peer exchange regions were sized for another layer shape, group or layer count")
         R, EL, k, dev = self.world, self.local, self.top_k, x.device
+        mark("start")
         sel, w = self.ops.route(x, self.gate, k, self.normalize)
         p = self.ops.pack(sel, w, self.experts)
+        mark("route_pack")
         lay = ctypes.byref(peer.structs[layer])
         inv = torch.empty(t_count * k, dtype=torch.int32, device=dev)
         s = _stream()
         check(lib.pdx_ep_dispatch_p2p(_ptr(x), _ptr(p.tokens), _ptr(p.positions), _ptr(p.offsets), t_count, k, hidden,
                                       self.experts, R, self.rank, cap, lay, _ptr(inv), s))
+        mark("dispatch")
         rows_cap = R * cap
         ly = Layout(offsets=torch.empty(EL + 1, dtype=torch.int32, device=dev),
                     active=torch.empty(EL + 1, dtype=torch.int32, device=dev),
                     perm=torch.empty(rows_cap, dtype=torch.int32, device=dev), experts=EL)
         check(lib.pdx_ep_layout_p2p(R, self.rank, EL, cap, rows_cap, lay, _ptr(ly.offsets), _ptr(ly.active),
                                     _ptr(ly.perm), s))
+        mark("layout_wait")
         grouped = torch.empty((rows_cap, hidden), dtype=x.dtype, device=dev)
         check(lib.pdx_ep_regroup(ctypes.c_void_p(peer.local(layer, "recv")), _ptr(ly.perm), _ptr(ly.offsets), EL,
                                  rows_cap, hidden, _ptr(grouped), s))
+        mark("regroup")
         y = self.ops.ffn(grouped, ly, self.slab, _lib.FFN_GEMV)
+        mark("ffn")
         check(lib.pdx_ep_return_p2p(_ptr(y), _ptr(ly.perm), _ptr(ly.offsets), EL, rows_cap, hidden, R, self.rank, cap,
                                     lay, s))
+        mark("return")
         check(lib.pdx_ep_wait_back(R, self.rank, lay, s))
+        mark("wait_back")
         out = torch.empty((t_count, hidden), dtype=torch.bfloat16, device=dev)
         back = ctypes.c_void_p(peer.local(layer, "back"))
         if norm:
@@ -251,6 +265,7 @@ class ExpertParallelMoE:
         else:
             check(lib.pdx_ep_combine(back, rows_cap, _ptr(w), _ptr(inv), t_count, k, hidden, _ptr(residual),
                                      _ptr(out), s))
+        mark("combine")
         return out
 
     # ---- the whole layer over the exchange -------------------------------------------
@@ -400,3 +415,25 @@ class ExpertParallelStack:
         """Drop the captured graphs (they hold NCCL work; release before
         destroying the process group)."""
         self._graphs.clear()
+
+    def stage_times_us(self, t_count, layers=8, repeats=3):
+        """Mean device time per layer of each stage of the peer-exchange
+        decode layer (route+pack, dispatch, layout incl. the wait for every
+        source's flag, regroup, FFN, return, wait for the returned blocks,
+        combine), from CUDA events recorded between the stages of eager
+        layers on this rank.  Every rank must call it (the stages wait on one
+        another)."""
+        if self.peer is None:
+            raise ValueError("stage timing covers the peer-memory exchange")
+        x, _ = self.io(t_count)
+        tot, n = {}, 0
+        for _ in range(repeats):
+            h = x
+            for i, layer in enumerate(self.layers[:layers]):
+                marks = []
+                h = layer.forward_p2p(h, self.peer, i, residual=h, norm=True, marks=marks)
+                torch.cuda.synchronize(self.device)
+                for (_, a), (name, b) in zip(marks, marks[1:]):
+                    tot[name] = tot.get(name, 0.0) + a.elapsed_time(b) * 1e3
+                n += 1
+        return {name: v / n for name, v in tot.items()}
