@@ -298,11 +298,13 @@ struct RouteBufs {
     uint16_t* logits;
     int64_t* selected;
     uint16_t* weights;
-    unsigned int* tickets;  // 1 + token blocks
     double* partials;       // split-K router partials (T > kTailMaxTokens)
 };
 
-size_t route_ticket_bytes(int64_t T) { return static_cast<size_t>(1 + (T + kRouteTB - 1) / kRouteTB) * 4; }
+// Dynamic shared memory of k_topk_pack for N = T*k assignments.
+size_t topk_pack_smem_bytes(int64_t E, int64_t N) {
+    return block_pack_smem_ints(E, N, kTopkPackThreads / 32) * sizeof(int);
+}
 
 // Split-K of the tiled router (T > kTailMaxTokens only).  A 64 x 128 tile
 // over all of K is ~2.7 * 10^5 FP64-tensor cycles at H = 2048 (~130 us on one
@@ -342,9 +344,8 @@ int router_splits(int64_t T, int64_t E, int64_t H) {
     return best;
 }
 
-// Routing: exact logits with top-k fused per token block (the k_topk launch is
-// only kept for pdx_topk_from_logits); with fused_pack the last token block
-// also packs (decode-sized batches).
+// Routing: exact logits, then top-k (with fused_pack at decode sizes, top-k
+// and the pack in one CTA).
 int launch_route(const void* x, const void* gate, int64_t T, int64_t H, int64_t E, int32_t k, int32_t normalize,
                  const RouteBufs& b, const PackOut* fused_pack, cudaStream_t stream) {
     if (T > kTailMaxTokens) {
@@ -378,40 +379,35 @@ int launch_route(const void* x, const void* gate, int64_t T, int64_t H, int64_t 
                                     static_cast<long long>(kTailMaxTokens));
         return PDX_OK;
     }
+    // decode sizes: logits on many CTAs, then top-k (with fused_pack: top-k and
+    // the pack, one CTA), chained by programmatic dependent launch
     const int n_tb = static_cast<int>((T + kRouteTB - 1) / kRouteTB);
     const int n_eb = static_cast<int>((E + kRouteEB - 1) / kRouteEB);
-    RouteTail tail{};
-    PDX_CUDA_TRY(cudaMemsetAsync(b.tickets, 0, route_ticket_bytes(T), stream));
-    tail.enabled = 1;
-    tail.k = k;
-    tail.normalize = normalize;
-    tail.tickets = b.tickets;
-    tail.selected = b.selected;
-    tail.weights = b.weights;
-    size_t smem = 0;
+    const uint16_t* xb = static_cast<const uint16_t*>(x);
+    const uint16_t* gb = static_cast<const uint16_t*>(gate);
+    if (T <= kSmallRouteT && H <= static_cast<int64_t>(kSmallRouteMaxChunks) * kSmallRouteThreads * 8)
+        PDX_PDL_TRY(launch_pdl(k_router_small, dim3(static_cast<unsigned>(E)), dim3(kSmallRouteThreads), 0, stream,
+                               xb, gb, static_cast<int>(T), static_cast<int>(H), static_cast<int>(E), b.logits));
+    else
+        PDX_PDL_TRY(launch_pdl(k_router_logits, dim3(static_cast<unsigned>(n_tb * n_eb)), dim3(kRouteWarps * 32), 0,
+                               stream, xb, gb, static_cast<int>(T), static_cast<int>(H), static_cast<int>(E),
+                               b.logits));
+    const int Ti = static_cast<int>(T), Ei = static_cast<int>(E);
     if (fused_pack) {
-        tail.do_pack = 1;
-        tail.pack = *fused_pack;
-        smem = static_cast<size_t>(E + E + 1 + (kRouteWarps * E)) * sizeof(int);
-    }
-    if (T <= kSmallRouteT) {
-        // decode sizes: one CTA per expert
-        with_epl(E, [&](auto epl) {
-            k_router_small<decltype(epl)::value><<<static_cast<unsigned>(E), kSmallRouteThreads, smem, stream>>>(
-                static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gate), static_cast<int>(T),
-                static_cast<int>(H), static_cast<int>(E), b.logits, tail);
-            return 0;
-        });
-        PDX_LAUNCHED();
+        const size_t smem = topk_pack_smem_bytes(E, T * k);
+        PDX_PDL_TRY(with_epl(E, [&](auto epl) {
+            return launch_pdl(k_topk_pack<decltype(epl)::value>, dim3(1), dim3(kTopkPackThreads), smem, stream,
+                              static_cast<const uint16_t*>(b.logits), Ti, Ei, k, normalize, b.selected, b.weights,
+                              *fused_pack);
+        }));
         return PDX_OK;
     }
-    with_epl(E, [&](auto epl) {
-        k_router_logits<decltype(epl)::value><<<n_tb * n_eb, kRouteWarps * 32, smem, stream>>>(
-            static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gate), static_cast<int>(T),
-            static_cast<int>(H), static_cast<int>(E), b.logits, tail);
-        return 0;
-    });
-    PDX_LAUNCHED();
+    const int warps_per_cta = 8;
+    const int grid = static_cast<int>((T + warps_per_cta - 1) / warps_per_cta);
+    PDX_PDL_TRY(with_epl(E, [&](auto epl) {
+        return launch_pdl(k_topk<decltype(epl)::value>, dim3(grid), dim3(warps_per_cta * 32), 0, stream,
+                          static_cast<const uint16_t*>(b.logits), Ti, Ei, k, normalize, b.selected, b.weights);
+    }));
     return PDX_OK;
 }
 
@@ -430,7 +426,7 @@ int launch_pack(const int64_t* selected, const uint16_t* weights, int64_t T, int
                 int* chunk_hist, cudaStream_t stream, int64_t chunk = 0) {
     const int64_t N = T * k;
     if (N <= kPackSingleMax) {
-        const size_t smem = static_cast<size_t>(E + E + 1 + 8 * E) * sizeof(int);
+        const size_t smem = block_pack_smem_ints(E, N, kPackThreads / 32) * sizeof(int);
         k_pack_single<<<1, kPackThreads, smem, stream>>>(selected, weights, static_cast<int>(T), k,
                                                           static_cast<int>(E), o);
         PDX_LAUNCHED();
@@ -706,7 +702,7 @@ uint64_t pdx_launch_count(void) { return g_launches.load(); }
 
 size_t pdx_route_workspace_bytes(int64_t T, int64_t E) {
     T = std::max<int64_t>(T, 1);
-    return align_up(route_ticket_bytes(T)) + align_up(static_cast<size_t>(T) * std::max<int64_t>(E, 0) * 2) +
+    return align_up(static_cast<size_t>(T) * std::max<int64_t>(E, 0) * 2) +
            align_up(route_partial_bytes(T, std::max<int64_t>(E, 0)));
 }
 
@@ -720,7 +716,6 @@ int pdx_route_topk(const void* x, const void* gate, int64_t T, int64_t H, int64_
         return fail(PDX_ERR_WORKSPACE, "workspace must be non-null and 256-byte aligned");
     Carver c{static_cast<char*>(workspace), workspace_bytes};
     RouteBufs b;
-    b.tickets = static_cast<unsigned int*>(c.take(route_ticket_bytes(T)));
     b.logits = logits_out ? static_cast<uint16_t*>(logits_out) : static_cast<uint16_t*>(c.take(T * E * 2));
     b.partials = static_cast<double*>(c.take(route_partial_bytes(T, E)));
     b.selected = selected_out;
@@ -898,7 +893,6 @@ size_t pdx_layer_workspace_bytes(int64_t T, int64_t H, int64_t E, int32_t top_k,
     top_k = std::max<int32_t>(top_k, 1);
     const int64_t N = T * top_k;
     Carver c{nullptr, SIZE_MAX};
-    c.take(route_ticket_bytes(T));  // route tickets
     c.take(T * E * 2);           // logits
     c.take(route_partial_bytes(T, E));
     c.take(N * 8);               // selected
@@ -930,7 +924,6 @@ int pdx_moe_layer(const void* x, const void* gate, int64_t T, int64_t H, int64_t
     const int64_t N = T * top_k;
     Carver c{static_cast<char*>(workspace), workspace_bytes};
     RouteBufs rb;
-    rb.tickets = static_cast<unsigned int*>(c.take(route_ticket_bytes(T)));
     rb.logits = logits_out ? static_cast<uint16_t*>(logits_out) : static_cast<uint16_t*>(c.take(T * E * 2));
     rb.partials = static_cast<double*>(c.take(route_partial_bytes(T, E)));
     rb.selected = selected_out ? selected_out : static_cast<int64_t*>(c.take(N * 8));
@@ -938,7 +931,8 @@ int pdx_moe_layer(const void* x, const void* gate, int64_t T, int64_t H, int64_t
     PackBufs pb = carve_pack(c, T, top_k, E, counts_out);
     uint16_t* y = static_cast<uint16_t*>(c.take(N * H * 2));
     if (c.overflow) return fail(PDX_ERR_WORKSPACE, "layer workspace too small (%zu > %zu bytes)", c.used, c.cap);
-    const bool fused = T <= kTailMaxTokens;
+    // the routing kernel also packs when the pack's shared memory fits the default 48 KiB
+    const bool fused = T <= kTailMaxTokens && topk_pack_smem_bytes(E, N) <= 48 * 1024;
     if ((st = launch_route(x, gate, T, H, E, top_k, normalize, rb, fused ? &pb.o : nullptr, stream))) return st;
     if (!fused && (st = launch_pack(rb.selected, rb.weights, T, top_k, E, pb.o, pb.chunk_hist, stream))) return st;
     if ((st = launch_ffn(x, T, pb.o.tokens, pb.o.offsets, pb.o.active, E, N, weights, H, I, y, m, c, stream)))

@@ -1,4 +1,5 @@
-// Router kernels: exact BF16 logits, softmax/top-k, and the fused decode tail.
+// Router kernels: exact BF16 logits, softmax/top-k, and the decode-size
+// top-k + pack kernel.
 //
 // Reference: route() -- expertbench/adapters/qwen.py:140-152 (logits via
 // F.linear, FP32 softmax, torch.topk, renormalise, cast to BF16).
@@ -9,36 +10,28 @@ namespace pdx {
 constexpr int kRouteTB = 8;       // tokens per CTA block
 constexpr int kRouteEB = 8;       // experts per CTA block
 constexpr int kRouteWarps = 8;    // warps per CTA, each owning a share of K
-static_assert(kRouteWarps == kRouteTB, "the fused tail routes one token per warp");
-
-struct RouteTail {
-    int enabled;           // 1: top-k in this kernel (per token block), 0: k_topk follows
-    int k;
-    int normalize;
-    int do_pack;           // 1: the last token block to finish also packs every token
-    unsigned int* tickets; // [1 + token blocks], zeroed by the host before the launch
-    int64_t* selected;
-    uint16_t* weights;
-    PackOut pack;
-};
 
 __device__ __forceinline__ double bits_to_f64(uint32_t b16) {
     return static_cast<double>(__uint_as_float(b16 << 16));
 }
 
-// logits[t, e] = RNE_bf16( sum_h x[t,h] * gate[e,h] ) with FP64 accumulation.
-// A CTA owns an 8-token x 8-expert block.  Warp w accumulates the 256-wide K
-// chunks j = w, w+8, ...; inside a chunk lane l takes elements 8l..8l+7.  A
-// transpose-reduction leaves block outputs (2l, 2l+1) (row-major t*8+e) in
-// lane l; the 8 warps' partials are then added in warp order.  Products of
-// two BF16 values are exact in FP64 and the FP64 sum of 2048 of them is
-// within a few units of 2^-53 relative, so the BF16 rounding equals that of
-// the exact sum except in cases of probability ~1e-12 per logit.
-template <int EPL>
+// Decode sizes route in two kernels chained by programmatic dependent launch
+// (no host work, no memset, no inter-CTA tickets between them): the logits
+// kernel, whose CTAs load their gate rows before waiting for the kernel that
+// produced x (the gate does not depend on it), and k_topk_pack, one CTA that
+// routes every token and packs them from shared memory.
+
+// logits[t, e] = RNE_bf16( sum_h x[t,h] * gate[e,h] ) with FP64 accumulation,
+// 16 < T <= 64.  A CTA owns an 8-token x 8-expert block.  Warp w accumulates
+// the 256-wide K chunks j = w, w+8, ...; inside a chunk lane l takes elements
+// 8l..8l+7.  A transpose-reduction leaves block outputs (2l, 2l+1) (row-major
+// t*8+e) in lane l; the 8 warps' partials are then added in warp order.
+// Products of two BF16 values are exact in FP64 and the FP64 sum of 2048 of
+// them is within a few units of 2^-53 relative, so the BF16 rounding equals
+// that of the exact sum except in cases of probability ~1e-12 per logit.
 __global__ void __launch_bounds__(kRouteWarps * 32) k_router_logits(const uint16_t* __restrict__ x,
                                                                      const uint16_t* __restrict__ gate, int T,
-                                                                     int H, int E, uint16_t* __restrict__ logits,
-                                                                     RouteTail tail) {
+                                                                     int H, int E, uint16_t* __restrict__ logits) {
     __shared__ double s_part[kRouteWarps][kRouteTB * kRouteEB];
     const int warp = static_cast<int>(threadIdx.x >> 5);
     const int lane = static_cast<int>(lane_id());
@@ -48,15 +41,20 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_router_logits(const uint16
     double acc[kRouteTB * kRouteEB];
 #pragma unroll
     for (int i = 0; i < kRouteTB * kRouteEB; ++i) acc[i] = 0.0;
-    for (int k0 = warp * 256 + lane * 8; k0 < H; k0 += kRouteWarps * 256) {
-        uint4 xv[kRouteTB], gv[kRouteEB];
+    int k0 = warp * 256 + lane * 8;
+    // the first K chunk of the gate rows is loaded before the wait for x
+    uint4 gv[kRouteEB];
+#pragma unroll
+    for (int e = 0; e < kRouteEB; ++e)
+        gv[e] = (k0 < H && e0 + e < E) ? __ldg(reinterpret_cast<const uint4*>(gate + static_cast<size_t>(e0 + e) * H + k0))
+                                       : make_uint4(0, 0, 0, 0);
+    griddep_wait();
+    griddep_launch();
+    for (; k0 < H; k0 += kRouteWarps * 256) {
+        uint4 xv[kRouteTB];
 #pragma unroll
         for (int t = 0; t < kRouteTB; ++t)
             xv[t] = (t0 + t < T) ? __ldg(reinterpret_cast<const uint4*>(x + static_cast<size_t>(t0 + t) * H + k0))
-                                 : make_uint4(0, 0, 0, 0);
-#pragma unroll
-        for (int e = 0; e < kRouteEB; ++e)
-            gv[e] = (e0 + e < E) ? __ldg(reinterpret_cast<const uint4*>(gate + static_cast<size_t>(e0 + e) * H + k0))
                                  : make_uint4(0, 0, 0, 0);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
@@ -76,6 +74,12 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_router_logits(const uint16
 #pragma unroll
                 for (int e = 0; e < kRouteEB; ++e) acc[t * kRouteEB + e] = fma(xd[t], gd[e], acc[t * kRouteEB + e]);
         }
+        const int kn = k0 + kRouteWarps * 256;   // next chunk's gate rows
+#pragma unroll
+        for (int e = 0; e < kRouteEB; ++e)
+            if (kn < H)
+                gv[e] = (e0 + e < E) ? __ldg(reinterpret_cast<const uint4*>(gate + static_cast<size_t>(e0 + e) * H + kn))
+                                     : make_uint4(0, 0, 0, 0);
     }
     // transpose-reduce 64 partial sums over 32 lanes: lane l keeps outputs 2l, 2l+1
 #pragma unroll
@@ -102,72 +106,47 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_router_logits(const uint16
         const int e = e0 + o % kRouteEB;
         if (t < T && e < E) logits[static_cast<size_t>(t) * E + e] = f64_to_bf16_bits(sum);
     }
-    if (!tail.enabled) return;
-    // ---- fused tail -------------------------------------------------------------
-    // The CTA that completes a token block (its n_eb expert blocks all written)
-    // routes those 8 tokens, one warp each; with do_pack, the last token block to
-    // finish then packs every token.  Threadfence-reduction pattern: writers
-    // fence before the ticket, the winner fences after it.
-    __shared__ unsigned int s_ticket;
-    const int tb = static_cast<int>(blockIdx.x) / n_eb;
-    const int n_tb = (T + kRouteTB - 1) / kRouteTB;
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) s_ticket = atomicAdd(&tail.tickets[1 + tb], 1u);
-    __syncthreads();
-    if (s_ticket != static_cast<unsigned int>(n_eb - 1)) return;
-    __threadfence();
-    const int t = tb * kRouteTB + warp;  // kRouteWarps == kRouteTB: one token per warp
-    if (t < T)
-        warp_softmax_topk<EPL>(logits + static_cast<size_t>(t) * E, E, tail.k, tail.normalize != 0,
-                               tail.selected + static_cast<size_t>(t) * tail.k,
-                               tail.weights + static_cast<size_t>(t) * tail.k);
-    if (!tail.do_pack) return;
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) s_ticket = atomicAdd(&tail.tickets[0], 1u);
-    __syncthreads();
-    if (s_ticket != static_cast<unsigned int>(n_tb - 1)) return;
-    __threadfence();
-    extern __shared__ int smem_i[];
-    int* hist = smem_i;
-    int* excl = hist + E;
-    int* warp_hist = excl + E + 1;
-    block_pack_all(tail.selected, tail.weights, T, tail.k, E, hist, excl, warp_hist, tail.pack);
 }
 
 // Decode-size router (T <= kSmallRouteT): one CTA per expert, so the 512 KiB
 // of gate rows is read by E CTAs at once instead of E/8.  Thread i takes the
-// 8-element K chunks i, i+256, ... of the expert's gate row and of every
-// token's row and accumulates the exact products in FP64; each token's sum is
-// reduced over the CTA in a fixed order (xor butterfly inside warps, warps in
-// order) and rounded once to BF16, as k_router_logits.  The fused tail is the
-// same: the CTA that writes the last expert's logits routes every token (one
-// warp per token) and, with do_pack, packs them.
+// 8-element K chunks i, i+256, ... of the expert's gate row (loaded before the
+// wait for x) and of every token's row and accumulates the exact products in
+// FP64; each token's sum is reduced over the CTA in a fixed order (xor
+// butterfly inside warps, warps in order) and rounded once to BF16, as
+// k_router_logits.
 constexpr int kSmallRouteT = 16;
 constexpr int kSmallRouteThreads = 256;
+constexpr int kSmallRouteMaxChunks = 4;   // gate chunks held in registers: H <= 4 * 256 * 8
 
-template <int EPL>
 __global__ void __launch_bounds__(kSmallRouteThreads) k_router_small(const uint16_t* __restrict__ x,
                                                                      const uint16_t* __restrict__ gate, int T,
-                                                                     int H, int E, uint16_t* __restrict__ logits,
-                                                                     RouteTail tail) {
+                                                                     int H, int E, uint16_t* __restrict__ logits) {
     constexpr int kWarps = kSmallRouteThreads / 32;
     __shared__ double s_part[kWarps][kSmallRouteT];
     const int warp = static_cast<int>(threadIdx.x >> 5);
     const int lane = static_cast<int>(lane_id());
     const int e = static_cast<int>(blockIdx.x);
+    const uint16_t* grow = gate + static_cast<size_t>(e) * H;
+    uint4 gv[kSmallRouteMaxChunks];
+#pragma unroll
+    for (int c = 0; c < kSmallRouteMaxChunks; ++c) {
+        const int k0 = (c * kSmallRouteThreads + static_cast<int>(threadIdx.x)) * 8;
+        gv[c] = k0 < H ? __ldg(reinterpret_cast<const uint4*>(grow + k0)) : make_uint4(0, 0, 0, 0);
+    }
     griddep_wait();
+    griddep_launch();
     double acc[kSmallRouteT];
 #pragma unroll
     for (int t = 0; t < kSmallRouteT; ++t) acc[t] = 0.0;
-    const uint16_t* grow = gate + static_cast<size_t>(e) * H;
-    for (int k0 = static_cast<int>(threadIdx.x) * 8; k0 < H; k0 += kSmallRouteThreads * 8) {
-        const uint4 gv = __ldg(reinterpret_cast<const uint4*>(grow + k0));
+#pragma unroll
+    for (int c = 0; c < kSmallRouteMaxChunks; ++c) {
+        const int k0 = (c * kSmallRouteThreads + static_cast<int>(threadIdx.x)) * 8;
+        if (k0 >= H) break;
         double gd[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-            const uint32_t w = (&gv.x)[q >> 1];
+            const uint32_t w = (&gv[c].x)[q >> 1];
             gd[q] = bits_to_f64((q & 1) ? (w >> 16) : (w & 0xFFFFu));
         }
 #pragma unroll
@@ -199,26 +178,29 @@ __global__ void __launch_bounds__(kSmallRouteThreads) k_router_small(const uint1
         for (int w = 1; w < kWarps; ++w) sum += s_part[w][t];
         logits[static_cast<size_t>(t) * E + e] = f64_to_bf16_bits(sum);
     }
-    if (!tail.enabled) return;
-    __shared__ unsigned int s_ticket;
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) s_ticket = atomicAdd(&tail.tickets[1], 1u);
-    __syncthreads();
-    if (s_ticket != static_cast<unsigned int>(E - 1)) return;
-    __threadfence();
-    for (int t = warp; t < T; t += kWarps)
-        warp_softmax_topk<EPL>(logits + static_cast<size_t>(t) * E, E, tail.k, tail.normalize != 0,
-                               tail.selected + static_cast<size_t>(t) * tail.k,
-                               tail.weights + static_cast<size_t>(t) * tail.k);
-    if (!tail.do_pack) return;
-    __threadfence();
-    __syncthreads();
-    extern __shared__ int smem_small[];
-    int* hist = smem_small;
+}
+
+// Decode-size top-k + pack, one CTA: warp w routes tokens w, w+32, ... from
+// the logits, then the CTA packs every token from shared memory
+// (block_pack_all).  dynamic smem: block_pack_smem_ints(E, T*k, 32) ints.
+constexpr int kTopkPackThreads = 1024;
+template <int EPL>
+__global__ void __launch_bounds__(kTopkPackThreads) k_topk_pack(const uint16_t* __restrict__ logits, int T, int E,
+                                                               int k, int normalize, int64_t* __restrict__ selected,
+                                                               uint16_t* __restrict__ weights, PackOut pack) {
+    griddep_wait();
+    griddep_launch();
+    const int warp = static_cast<int>(threadIdx.x >> 5);
+    const int nw = static_cast<int>(blockDim.x >> 5);
+    for (int t = warp; t < T; t += nw)
+        warp_softmax_topk<EPL>(logits + static_cast<size_t>(t) * E, E, k, normalize != 0,
+                               selected + static_cast<size_t>(t) * k, weights + static_cast<size_t>(t) * k);
+    __syncthreads();  // this CTA's selected/weights stores are visible to its threads
+    extern __shared__ int smem_tp[];
+    int* hist = smem_tp;
     int* excl = hist + E;
     int* warp_hist = excl + E + 1;
-    block_pack_all(tail.selected, tail.weights, T, tail.k, E, hist, excl, warp_hist, tail.pack);
+    block_pack_all(selected, weights, T, k, E, hist, excl, warp_hist, pack);
 }
 
 // Prefill-size router on the FP64 tensor path (mma.sync m8n8k4 .f64; tcgen05
@@ -418,6 +400,8 @@ __global__ void __launch_bounds__(256) k_topk_partials(const double* __restrict_
                                                        int k, int normalize, uint16_t* __restrict__ logits,
                                                        int64_t* __restrict__ selected,
                                                        uint16_t* __restrict__ weights) {
+    griddep_wait();
+    griddep_launch();
     const int warps = static_cast<int>(blockDim.x >> 5);
     const bool nrm = normalize != 0;
     for (int t = static_cast<int>(blockIdx.x) * warps + static_cast<int>(threadIdx.x >> 5); t < T;
@@ -430,6 +414,8 @@ template <int EPL>
 __global__ void __launch_bounds__(256) k_topk(const uint16_t* __restrict__ logits, int T, int E, int k,
                                               int normalize, int64_t* __restrict__ selected,
                                               uint16_t* __restrict__ weights) {
+    griddep_wait();
+    griddep_launch();
     const int warps = static_cast<int>(blockDim.x >> 5);
     const int first = static_cast<int>(blockIdx.x) * warps + static_cast<int>(threadIdx.x >> 5);
     block_topk_rows<EPL>(logits, T, E, k, normalize != 0, selected, weights, first, gridDim.x * warps);

@@ -314,14 +314,35 @@ __device__ __forceinline__ void block_stable_scatter(const int64_t* selected, co
     }
 }
 
-// Whole pack by one block (N = T*k small).  smem: hist[E], excl[E+1],
-// warp_hist[NW*E].
+// Whole pack by one block (N = T*k <= kPackSmemMax), from shared memory: the
+// routing is read from global memory once (one coalesced pass) into s_ids /
+// s_w (by position t*k + s), then histogram, scan and the stable scatter run
+// on shared memory, so the only global accesses on the block's critical path
+// are that load and the output stores (a single CTA walking dependent L2
+// reads is what makes a pack slow).  smem: hist[E], excl[E+1], warp_hist[NW*E],
+// s_ids[N] ints, s_w[N] shorts.
+constexpr int kPackSmemMax = 2048;
 __device__ __forceinline__ void block_pack_all(const int64_t* selected, const uint16_t* weights, int T, int k,
                                                int E, int* hist, int* excl, int* warp_hist, const PackOut& o) {
     const int N = T * k;
+    int* s_ids = warp_hist + (static_cast<int>(blockDim.x) >> 5) * E;
+    uint16_t* s_w = reinterpret_cast<uint16_t*>(s_ids + N);
     for (int i = threadIdx.x; i < E; i += blockDim.x) hist[i] = 0;
+    for (int p = threadIdx.x; p < N; p += blockDim.x) {
+        const int64_t e = selected[p];
+        int v = static_cast<int>(e);
+        if (e < 0 || e >= E) {
+            raise_error(PDX_DEVERR_BAD_EXPERT);
+            v = -1;
+        }
+        s_ids[p] = v;
+        s_w[p] = weights[p];
+    }
     __syncthreads();
-    block_histogram(selected, T, k, E, 0, N, hist);
+    for (int f = threadIdx.x; f < N; f += blockDim.x) {
+        const int e = s_ids[(f % T) * k + f / T];
+        if (e >= 0) atomicAdd(&hist[e], 1);
+    }
     __syncthreads();
     if (threadIdx.x < 32) warp_exclusive_scan(hist, E, excl, o.active, nullptr);
     __syncthreads();
@@ -331,7 +352,46 @@ __device__ __forceinline__ void block_pack_all(const int64_t* selected, const ui
     }
     if (threadIdx.x == 0) o.offsets[E] = excl[E];
     __syncthreads();
-    block_stable_scatter(selected, weights, T, k, E, 0, N, excl, warp_hist, o);
+    // stable scatter in flat order f = s*T + t (rounds of blockDim.x entries;
+    // within a round the (warp, lane) order is the flat order)
+    const int tid = static_cast<int>(threadIdx.x);
+    const int warp = tid >> 5;
+    const int nw = static_cast<int>(blockDim.x) >> 5;
+    const uint32_t lane = lane_id();
+    const uint32_t lt_mask = (1u << lane) - 1u;
+    for (int base = 0; base < N; base += blockDim.x) {
+        const int f = base + tid;
+        const int t = f % T, s = f / T;
+        const int pos = t * k + s;
+        const int e = f < N ? s_ids[pos] : -1;
+        for (int i = tid; i < nw * E; i += blockDim.x) warp_hist[i] = 0;
+        __syncthreads();
+        const uint32_t peers = __match_any_sync(0xffffffffu, e);
+        const int rank = __popc(peers & lt_mask);
+        if (e >= 0 && rank == 0) warp_hist[warp * E + e] = __popc(peers);
+        __syncthreads();
+        if (e >= 0) {
+            int before = 0;
+            for (int w = 0; w < warp; ++w) before += warp_hist[w * E + e];
+            const int p = excl[e] + before + rank;
+            o.tokens[p] = t;
+            o.positions[p] = pos;
+            o.packed_w[p] = s_w[pos];
+            o.inverse[pos] = p;
+        }
+        __syncthreads();
+        for (int e2 = tid; e2 < E; e2 += blockDim.x) {
+            int add = 0;
+            for (int w = 0; w < nw; ++w) add += warp_hist[w * E + e2];
+            excl[e2] += add;
+        }
+        __syncthreads();
+    }
+}
+
+// Shared memory of block_pack_all, in ints, for N = T*k entries and `warps` warps.
+__host__ __device__ constexpr size_t block_pack_smem_ints(int64_t E, int64_t N, int warps) {
+    return static_cast<size_t>(E + E + 1 + warps * E + N + (N + 1) / 2);
 }
 
 }  // namespace pdx
