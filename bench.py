@@ -14,9 +14,10 @@ Workload (synthetic seeded data, random-init weights):
     Zipf(1.1) router skew.
   * ``e2e``: the same decode step through the public stack API with the input
     copied host->device from pinned memory and the output copied back every step.
-  * ``roofline``: the grouped expert FFN of the decode path (row gather + two
-    weight-streaming tcgen05 GEMMs) timed on its own stream with CUDA events;
-    algorithmic bytes = active experts x 9,437,184 B + activation rows.
+  * ``roofline``: the grouped expert FFN of the decode path (one launch of
+    k_decode_ffn: gate/up and down projections, weights streamed by TMA into
+    tcgen05 MMAs) timed on its own stream with CUDA events; algorithmic
+    bytes = active experts x 9,437,184 B + activation rows.
   * ``cpu_baseline``: the reference's CPU layer path (oracle/cpu_path.py, torch
     CPU ops) on this host's cores, a bounded sample of layers.
 Multi-GPU (N>1, torchrun): expert parallel, 128/N experts per GPU, each rank
@@ -378,7 +379,7 @@ def main():
             f = line.split()
             if len(f) == 2 and f[0] == "decode_ffn_dram_bytes_per_active_expert":
                 traffic = float(f[1]) * statistics.mean(act)
-    roofline = dict(bound="hbm", kernel="pdx_moe_ffn_grouped decode path (k_gather_rows + 2x k_stream_gemm: TMA weight stream, tcgen05 swap-AB)",
+    roofline = dict(bound="hbm", kernel="pdx_moe_ffn_grouped decode path (k_decode_ffn: gate/up + down in one launch, TMA weight stream, tcgen05 swap-AB)",
                     achieved=achieved, peak=pk["hbm_gbs"], unit="GB/s", frac=achieved / pk["hbm_gbs"],
                     peak_source=pk["source"], frac_of_8000_nominal=achieved / 8000.0, traffic=traffic,
                     bytes_per_launch=bytes_per_launch, us_per_launch=per_launch_s * 1e6)

@@ -150,14 +150,17 @@ int pdx_gather_rows(const void *x, const int32_t *tokens, int64_t rows, int64_t 
  * with the reference's BF16 roundings (after each linear, after silu, after
  * the product).  `x` is the [T,H] token matrix; rows are gathered through
  * `tokens` (tokens == NULL: x already holds the `rows` rows in packed order).
- * mode: 0 = auto (the decode path up to 16 rows per expert on average, else
+ * mode: 0 = auto (the decode path up to 48 rows per expert on average, else
  * the prefill path); 1 = decode path (weights streamed by TMA as the
- * tcgen05 M operand, tokens as N, split-K for few experts); 2 = prefill path
+ * tcgen05 M operand, tokens as N, split-K for few experts; with `tokens`
+ * given and T <= 64 one launch computes both projections straight from x,
+ * otherwise a row gather and one launch per projection); 2 = prefill path
  * (tcgen05 grouped GEMM tiled over tokens, 128 x 256 tiles on single CTAs);
  * 3 = SIMT weight-streaming GEMV (an independent implementation kept for
  * cross-checks and for shapes the tcgen05 paths do not tile); 4 = the prefill
  * path (same as 2); 5 = the prefill path on CTA pairs (tcgen05 cta_group::2,
- * 256 x 256 tiles).
+ * 256 x 256 tiles); 6 = the decode path always as row gather + one launch
+ * per projection (a cross-check of the single-launch form).
  */
 #define PDX_FFN_AUTO 0
 #define PDX_FFN_GEMV 1
@@ -165,6 +168,7 @@ int pdx_gather_rows(const void *x, const int32_t *tokens, int64_t rows, int64_t 
 #define PDX_FFN_SIMT 3
 #define PDX_FFN_GEMM_1CTA 4
 #define PDX_FFN_GEMM_PAIR 5
+#define PDX_FFN_GEMV_STAGED 6
 size_t pdx_ffn_workspace_bytes(int64_t rows, int64_t E, int64_t H, int64_t I, int32_t mode);
 int pdx_moe_ffn_grouped(const void *x, int64_t T, const int32_t *tokens,
                         const int32_t *offsets, const int32_t *active, int64_t E,

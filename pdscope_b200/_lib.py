@@ -24,7 +24,7 @@ PDX_DEVERR_WAIT_TIMEOUT = 1
 PDX_DEVERR_BAD_EXPERT = 2
 PDX_DEVERR_BAD_SLOT = 3
 
-FFN_AUTO, FFN_GEMV, FFN_GEMM, FFN_SIMT, FFN_GEMM_1CTA, FFN_GEMM_PAIR = 0, 1, 2, 3, 4, 5
+FFN_AUTO, FFN_GEMV, FFN_GEMM, FFN_SIMT, FFN_GEMM_1CTA, FFN_GEMM_PAIR, FFN_GEMV_STAGED = 0, 1, 2, 3, 4, 5, 6
 LAYER_OUT_NORM = 0x100   # OR into pdx_moe_layer's mode: out = layer_norm(MoE(x) + residual)
 
 ABI_VERSION = 1

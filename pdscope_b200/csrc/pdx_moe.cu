@@ -16,6 +16,7 @@
 #include <utility>
 
 #include "combine.cu"
+#include "ffn_decode.cu"
 #include "ffn_gemm.cu"
 #include "ffn_gemv.cu"
 #include "ffn_stream.cu"
@@ -176,6 +177,16 @@ int device_setup(int* sms_out) {
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_stream_gemm<32, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ss));
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_stream_gemm<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ss));
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_stream_gemm<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ss));
+        const int ds = static_cast<int>(kDecSmemBytes);
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<16, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<16, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<16, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<32, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<32, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<32, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<64, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<64, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
+        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<64, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
         g_num_sms[dev] = sms;
         g_attrs_set[dev] = true;
     }
@@ -256,7 +267,7 @@ int check_ffn_shape(int64_t H, int64_t I, int32_t mode) {
             return fail(PDX_ERR_UNSUPPORTED, "SIMT path needs I %% 16 == 0 and H %% 32 == 0");
         if (H > 4096 || I > 4096)
             return fail(PDX_ERR_UNSUPPORTED, "SIMT path supports H, I <= 4096");
-    } else if (mode == PDX_FFN_GEMV) {
+    } else if (mode == PDX_FFN_GEMV || mode == PDX_FFN_GEMV_STAGED) {
         if (!stream_shape_ok(H, I))
             return fail(PDX_ERR_UNSUPPORTED, "weight-streaming path needs H %% 128 == 0 and I %% 128 == 0");
     } else if (is_gemm_mode(mode)) {
@@ -347,7 +358,8 @@ int router_splits(int64_t T, int64_t E, int64_t H) {
 // Routing: exact logits, then top-k (with fused_pack at decode sizes, top-k
 // and the pack in one CTA).
 int launch_route(const void* x, const void* gate, int64_t T, int64_t H, int64_t E, int32_t k, int32_t normalize,
-                 const RouteBufs& b, const PackOut* fused_pack, cudaStream_t stream) {
+                 const RouteBufs& b, const PackOut* fused_pack, cudaStream_t stream, unsigned int* zero_ptr = nullptr,
+                 int64_t zero_words = 0) {
     if (T > kTailMaxTokens) {
         // prefill sizes: tiled FP64 logits, then one warp per token for top-k
         int sms = 0;
@@ -398,7 +410,7 @@ int launch_route(const void* x, const void* gate, int64_t T, int64_t H, int64_t 
         PDX_PDL_TRY(with_epl(E, [&](auto epl) {
             return launch_pdl(k_topk_pack<decltype(epl)::value>, dim3(1), dim3(kTopkPackThreads), smem, stream,
                               static_cast<const uint16_t*>(b.logits), Ti, Ei, k, normalize, b.selected, b.weights,
-                              *fused_pack);
+                              *fused_pack, zero_ptr, static_cast<int>(zero_words));
         }));
         return PDX_OK;
     }
@@ -499,7 +511,67 @@ StreamPlan plan_stream(int64_t rows, int64_t E, int64_t H, int64_t I) {
     return p;
 }
 
+// Single-launch decode FFN (ffn_decode.cu): the whole token matrix x [T, H]
+// is the gate/up N operand, so it needs the packed tokens and T <= 64, and
+// its shared-memory tables bound the rows and active experts.
+bool decode_fused_ok(int64_t T, int64_t rows, int64_t E, int64_t H, int64_t I, const int32_t* tokens) {
+    return tokens != nullptr && T >= 1 && T <= kDecMaxT && rows <= kDecMaxRows &&
+           std::min(E, rows) <= kDecMaxActive && stream_shape_ok(H, I);
+}
+
+struct DecodePlan {
+    int nb, nt2;          // gate/up token columns (T rounded up to 16), down token tile
+    int s1, s2;           // K slices per tile of each projection
+    int64_t tiles1, tiles2;
+    size_t p1_bytes, p2_bytes;
+    int64_t zero_words;   // tickets of both projections + per-expert h counters
+};
+
+// Depends only on (rows, E, H, I) and T, so the workspace query (which sizes
+// for any T) and the launch agree; the split counts are plan_stream's.
+DecodePlan plan_decode(int64_t T, int64_t rows, int64_t E, int64_t H, int64_t I) {
+    DecodePlan p{};
+    const int64_t est = std::max<int64_t>(1, std::min(E, rows));
+    const int64_t avg = (rows + est - 1) / est;
+    p.nb = T <= 16 ? 16 : (T <= 32 ? 32 : 64);
+    p.nt2 = avg <= 12 ? 16 : (avg <= 24 ? 32 : 64);
+    const int64_t m1 = I / 128, m2 = H / 128;
+    p.tiles1 = est * m1;
+    p.tiles2 = m2 * (rows / p.nt2 + est);
+    p.s1 = plan_splits(static_cast<int>(H / 64), m1 * est);
+    p.s2 = plan_splits(static_cast<int>(I / 64), m2 * est);
+    p.p1_bytes = p.s1 > 1 ? static_cast<size_t>(m1 * p.s1 * rows) * 256 * 4 : 0;
+    p.p2_bytes = p.s2 > 1 ? static_cast<size_t>(p.tiles2 * p.s2 * p.nt2) * 128 * 4 : 0;
+    p.zero_words = 4 * p.tiles1 + 4 * p.tiles2 + est;
+    return p;
+}
+
+struct DecodeBufs {
+    DecodePlan plan;
+    uint16_t* h;
+    float* p1;
+    float* p2;
+    unsigned int* counters;  // zero_words words, cleared before every launch
+};
+
+DecodeBufs carve_decode(Carver& c, int64_t T, int64_t rows, int64_t E, int64_t H, int64_t I) {
+    DecodeBufs b;
+    b.plan = plan_decode(T, rows, E, H, I);
+    b.h = static_cast<uint16_t*>(c.take(static_cast<size_t>(rows) * I * 2));
+    b.p1 = static_cast<float*>(c.take(std::max<size_t>(b.plan.p1_bytes, 16)));
+    b.p2 = static_cast<float*>(c.take(std::max<size_t>(b.plan.p2_bytes, 16)));
+    b.counters = static_cast<unsigned int*>(c.take(static_cast<size_t>(b.plan.zero_words) * 4));
+    return b;
+}
+
 size_t ffn_ws_bytes(int64_t rows, int64_t E, int64_t H, int64_t I, int mode) {
+    if (mode == PDX_FFN_GEMV) {
+        // either form may run (the single-launch one needs the tokens and T <= 64)
+        Carver c{nullptr, SIZE_MAX};
+        carve_decode(c, 1, rows, E, H, I);
+        return std::max(c.used, ffn_ws_bytes(rows, E, H, I, PDX_FFN_GEMV_STAGED));
+    }
+    if (mode == PDX_FFN_GEMV_STAGED) mode = PDX_FFN_GEMV;
     size_t b = align_up(static_cast<size_t>(rows) * I * 2);                        // h
     if (is_gemm_mode(mode) || mode == PDX_FFN_GEMV) b += align_up(static_cast<size_t>(rows) * H * 2);  // x rows
     if (mode == PDX_FFN_GEMV) {
@@ -522,9 +594,64 @@ int launch_stream_pair(const CUtensorMap& tm_g, const CUtensorMap& tm_u, const C
     return PDX_OK;
 }
 
+template <int NB>
+int launch_decode_nt2(int nt2, dim3 grid, const CUtensorMap& tm_g, const CUtensorMap& tm_u, const CUtensorMap& tm_x,
+                      const CUtensorMap& tm_d, const CUtensorMap& tm_h, const DecodeArgs& a, cudaStream_t stream) {
+    if (nt2 == 16)
+        PDX_PDL_TRY(launch_pdl(k_decode_ffn<NB, 16>, grid, dim3(kDecThreads), kDecSmemBytes, stream, tm_g, tm_u, tm_x,
+                               tm_d, tm_h, a));
+    else if (nt2 == 32)
+        PDX_PDL_TRY(launch_pdl(k_decode_ffn<NB, 32>, grid, dim3(kDecThreads), kDecSmemBytes, stream, tm_g, tm_u, tm_x,
+                               tm_d, tm_h, a));
+    else
+        PDX_PDL_TRY(launch_pdl(k_decode_ffn<NB, 64>, grid, dim3(kDecThreads), kDecSmemBytes, stream, tm_g, tm_u, tm_x,
+                               tm_d, tm_h, a));
+    return PDX_OK;
+}
+
+// The single-launch decode FFN.  `zeroed`: the kernel before it in the stream
+// already cleared b.counters (the fused top-k + pack of pdx_moe_layer does);
+// otherwise a clearing kernel is launched first.
+int launch_decode_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* offsets, const int32_t* active,
+                      int64_t rows, const pdx_expert_weights* w, int64_t H, int64_t I, void* y, const DecodeBufs& b,
+                      bool zeroed, cudaStream_t stream) {
+    int sms = 0;
+    int st = device_setup(&sms);
+    if (st) return st;
+    const DecodePlan& p = b.plan;
+    if (!zeroed)
+        PDX_PDL_TRY(launch_pdl(k_zero_words, dim3(static_cast<unsigned>(std::min<int64_t>(64, (p.zero_words + 255) / 256))),
+                               dim3(256), 0, stream, b.counters, static_cast<int>(p.zero_words)));
+    const int64_t gs = w->num_slots > 1 ? w->gate_stride / H : 0;
+    const int64_t us = w->num_slots > 1 ? w->up_stride / H : 0;
+    const int64_t ds = w->num_slots > 1 ? w->down_stride / I : 0;
+    if ((w->num_slots - 1) * std::max(gs, std::max(us, ds)) + H >= (int64_t(1) << 31))
+        return fail(PDX_ERR_UNSUPPORTED, "expert slab too large for 32-bit TMA row coordinates");
+    CUtensorMap tm_g, tm_u, tm_x, tm_d, tm_h;
+    if ((st = encode_2d(&tm_g, w->gate, (w->num_slots - 1) * gs + I, H, 128))) return st;
+    if ((st = encode_2d(&tm_u, w->up, (w->num_slots - 1) * us + I, H, 128))) return st;
+    if ((st = encode_2d(&tm_d, w->down, (w->num_slots - 1) * ds + H, I, 128))) return st;
+    if ((st = encode_2d(&tm_x, x, T, H, p.nb))) return st;
+    if ((st = encode_2d(&tm_h, b.h, rows, I, p.nt2))) return st;
+    DecodeArgs a{offsets, active, tokens, w->slot_of_expert, w->num_slots, gs, us, ds,
+                 static_cast<int>(H), static_cast<int>(I), static_cast<int>(T), static_cast<int>(rows),
+                 p.s1, p.s2, b.h, static_cast<uint16_t*>(y), b.p1, b.p2,
+                 b.counters, b.counters + 4 * p.tiles1, b.counters + 4 * p.tiles1 + 4 * p.tiles2};
+    const dim3 grid(static_cast<unsigned>(std::min<int64_t>(sms, p.tiles1 * p.s1 + p.tiles2 * p.s2)));
+    if (p.nb == 16) return launch_decode_nt2<16>(p.nt2, grid, tm_g, tm_u, tm_x, tm_d, tm_h, a, stream);
+    if (p.nb == 32) return launch_decode_nt2<32>(p.nt2, grid, tm_g, tm_u, tm_x, tm_d, tm_h, a, stream);
+    return launch_decode_nt2<64>(p.nt2, grid, tm_g, tm_u, tm_x, tm_d, tm_h, a, stream);
+}
+
 int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* offsets, const int32_t* active,
                int64_t E, int64_t rows, const pdx_expert_weights* w, int64_t H, int64_t I, void* y, int mode,
                Carver& ws, cudaStream_t stream) {
+    if (mode == PDX_FFN_GEMV && decode_fused_ok(T, rows, E, H, I, tokens)) {
+        const DecodeBufs b = carve_decode(ws, T, rows, E, H, I);
+        if (ws.overflow) return fail(PDX_ERR_WORKSPACE, "FFN workspace too small (%zu > %zu bytes)", ws.used, ws.cap);
+        return launch_decode_ffn(x, T, tokens, offsets, active, rows, w, H, I, y, b, false, stream);
+    }
+    if (mode == PDX_FFN_GEMV_STAGED) mode = PDX_FFN_GEMV;
     int sms = 0;
     int st = device_setup(&sms);
     if (st) return st;
@@ -930,13 +1057,24 @@ int pdx_moe_layer(const void* x, const void* gate, int64_t T, int64_t H, int64_t
     rb.weights = weights_out ? static_cast<uint16_t*>(weights_out) : static_cast<uint16_t*>(c.take(N * 2));
     PackBufs pb = carve_pack(c, T, top_k, E, counts_out);
     uint16_t* y = static_cast<uint16_t*>(c.take(N * H * 2));
+    // decode batches: both projections in one launch straight from x
+    const bool one_launch = m == PDX_FFN_GEMV && decode_fused_ok(T, N, E, H, I, pb.o.tokens);
+    DecodeBufs db{};
+    if (one_launch) db = carve_decode(c, T, N, E, H, I);
     if (c.overflow) return fail(PDX_ERR_WORKSPACE, "layer workspace too small (%zu > %zu bytes)", c.used, c.cap);
     // the routing kernel also packs when the pack's shared memory fits the default 48 KiB
+    // (and then clears the single-launch FFN's tickets and counters)
     const bool fused = T <= kTailMaxTokens && topk_pack_smem_bytes(E, N) <= 48 * 1024;
-    if ((st = launch_route(x, gate, T, H, E, top_k, normalize, rb, fused ? &pb.o : nullptr, stream))) return st;
-    if (!fused && (st = launch_pack(rb.selected, rb.weights, T, top_k, E, pb.o, pb.chunk_hist, stream))) return st;
-    if ((st = launch_ffn(x, T, pb.o.tokens, pb.o.offsets, pb.o.active, E, N, weights, H, I, y, m, c, stream)))
+    const bool zeroed = fused && one_launch;
+    if ((st = launch_route(x, gate, T, H, E, top_k, normalize, rb, fused ? &pb.o : nullptr, stream,
+                           zeroed ? db.counters : nullptr, zeroed ? db.plan.zero_words : 0)))
         return st;
+    if (!fused && (st = launch_pack(rb.selected, rb.weights, T, top_k, E, pb.o, pb.chunk_hist, stream))) return st;
+    if (one_launch)
+        st = launch_decode_ffn(x, T, pb.o.tokens, pb.o.offsets, pb.o.active, N, weights, H, I, y, db, zeroed, stream);
+    else
+        st = launch_ffn(x, T, pb.o.tokens, pb.o.offsets, pb.o.active, E, N, weights, H, I, y, m, c, stream);
+    if (st) return st;
     if (out_norm)
         PDX_PDL_TRY(launch_pdl(k_combine_norm, dim3(static_cast<unsigned>(T)), dim3(kCombineThreads), 0, stream,
                                static_cast<const uint16_t*>(y), static_cast<const uint16_t*>(rb.weights),

@@ -183,13 +183,17 @@ __global__ void __launch_bounds__(kSmallRouteThreads) k_router_small(const uint1
 // Decode-size top-k + pack, one CTA: warp w routes tokens w, w+32, ... from
 // the logits, then the CTA packs every token from shared memory
 // (block_pack_all).  dynamic smem: block_pack_smem_ints(E, T*k, 32) ints.
+// It also clears `zero_words` words at `zero_ptr` (the tickets and counters of
+// the FFN launch that follows it), so no clearing kernel sits in the chain.
 constexpr int kTopkPackThreads = 1024;
 template <int EPL>
 __global__ void __launch_bounds__(kTopkPackThreads) k_topk_pack(const uint16_t* __restrict__ logits, int T, int E,
                                                                int k, int normalize, int64_t* __restrict__ selected,
-                                                               uint16_t* __restrict__ weights, PackOut pack) {
+                                                               uint16_t* __restrict__ weights, PackOut pack,
+                                                               unsigned int* __restrict__ zero_ptr, int zero_words) {
     griddep_wait();
     griddep_launch();
+    for (int i = static_cast<int>(threadIdx.x); i < zero_words; i += static_cast<int>(blockDim.x)) zero_ptr[i] = 0u;
     const int warp = static_cast<int>(threadIdx.x >> 5);
     const int nw = static_cast<int>(blockDim.x >> 5);
     for (int t = warp; t < T; t += nw)

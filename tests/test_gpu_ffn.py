@@ -115,7 +115,7 @@ def _grouped_case(pdx, tokens, experts, k, hidden, inter, mode, seed, slot_perm=
     return got
 
 
-@pytest.mark.parametrize("mode", (1, 2, 3, 4, 5))
+@pytest.mark.parametrize("mode", (1, 2, 3, 4, 5, 6))
 @pytest.mark.parametrize("tokens", (1, 5, 64, 300))
 def test_grouped_ffn_small_shape(pdx, mode, tokens):
     _grouped_case(pdx, tokens, 16, 4, 256, 128, mode, 100 + tokens)
@@ -133,6 +133,27 @@ def test_grouped_ffn_slot_mapping(pdx, mode):
                                          (5, 512)))
 def test_grouped_ffn_qwen3_shape(pdx, mode, tokens):
     _grouped_case(pdx, tokens, 128, 8, 2048, 768, mode, 200 + tokens)
+
+
+@pytest.mark.parametrize("tokens,experts,k,hidden,inter,zipf", (
+    (1, 128, 8, 2048, 768, False), (2, 128, 8, 2048, 768, False), (8, 128, 8, 2048, 768, False),
+    (16, 64, 8, 1024, 512, False), (17, 128, 8, 2048, 768, False), (33, 32, 8, 512, 256, False),
+    (64, 128, 8, 2048, 768, False), (64, 16, 4, 256, 128, True), (40, 8, 8, 512, 256, True)))
+def test_single_launch_decode_matches_staged(pdx, tokens, experts, k, hidden, inter, zipf):
+    """The decode FFN in one launch (mode 1 with T <= 64: gate/up on the whole
+    token matrix, down in the same launch behind per-expert h counters)
+    against the staged form (mode 6: row gather, then one launch per
+    projection).  Same weight tiles, K slices and slice order, so the rows are
+    bit-identical; the single launch runs twice in a row on one workspace (its
+    tickets and counters are cleared before every launch).  Cases cover split-K
+    in either projection (few active experts), Zipf-skewed experts with more
+    rows than one down tile, every token on every expert, and T not a multiple
+    of 16."""
+    a = _grouped_case(pdx, tokens, experts, k, hidden, inter, 6, 300 + tokens, zipf=zipf)
+    b = _grouped_case(pdx, tokens, experts, k, hidden, inter, 1, 300 + tokens, zipf=zipf)
+    c = _grouped_case(pdx, tokens, experts, k, hidden, inter, 1, 300 + tokens, zipf=zipf)
+    assert np.array_equal(a, b)
+    assert np.array_equal(b, c)
 
 
 def test_ffn_paths_agree(pdx):

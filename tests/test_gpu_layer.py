@@ -50,7 +50,7 @@ def _check_layer(res, x, gate, wg, wu, wd, k):
     return got
 
 
-@pytest.mark.parametrize("mode", (0, 1, 2, 3, 4, 5))
+@pytest.mark.parametrize("mode", (0, 1, 2, 3, 4, 5, 6))
 def test_small_layer_golden(pdx, golden, mode):
     """The golden small layer (E=16, k=4, H=256, I=128, T=32)."""
     x, gate, wg, wu, wd = mo.synthetic_layer(4242, 32, 256, 16, 128)
@@ -73,6 +73,25 @@ def test_layer_ragged_sizes(pdx, tokens):
     x, gate, wg, wu, wd = mo.synthetic_layer(77 + tokens, tokens, 512, 32, 256)
     res, _, _ = _layer(pdx, x, gate, wg, wu, wd, 8)
     _check_layer(res, x, gate, wg, wu, wd, 8)
+
+
+@pytest.mark.parametrize("tokens", (1, 8, 64))
+def test_layer_single_launch_decode_matches_staged(pdx, tokens):
+    """pdx_moe_layer at decode batches: the single-launch FFN, whose tickets and
+    counters the fused top-k + pack kernel clears, equals the staged FFN bit
+    for bit, on repeated calls with one workspace."""
+    from tests.gpu_util import to_dev
+    x, gate, wg, wu, wd = mo.synthetic_layer(500 + tokens, tokens, 2048, 128, 768)
+    res, layer, _ = _layer(pdx, x, gate, wg, wu, wd, 8, mode=6)
+    staged = res.out.clone()
+    _check_layer(res, x, gate, wg, wu, wd, 8)
+    xd = to_dev(x)
+    for _ in range(3):
+        again = layer.forward(xd, mode=1)
+        torch.cuda.synchronize()
+        assert torch.equal(again.out, staged)
+    from pdscope_b200.runtime import raise_device_error
+    raise_device_error()
 
 
 def test_layer_residual(pdx):
