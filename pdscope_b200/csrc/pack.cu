@@ -18,6 +18,8 @@ constexpr int kPackScanSmemInts = 40 * 1024;
 __global__ void __launch_bounds__(kPackThreads) k_pack_single(const int64_t* __restrict__ selected,
                                                               const uint16_t* __restrict__ weights, int T, int k,
                                                               int E, PackOut o) {
+    griddep_wait();
+    griddep_launch();
     extern __shared__ int smem_i[];
     int* hist = smem_i;
     int* excl = hist + E;

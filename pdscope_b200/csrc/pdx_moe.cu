@@ -383,7 +383,7 @@ int launch_route(const void* x, const void* gate, int64_t T, int64_t H, int64_t 
             else
                 k_topk<EPL><<<grid, warps_per_cta * 32, 0, stream>>>(b.logits, static_cast<int>(T),
                                                                      static_cast<int>(E), k, normalize, b.selected,
-                                                                     b.weights);
+                                                                     b.weights, nullptr, 0);
             return 0;
         });
         PDX_LAUNCHED();
@@ -405,6 +405,23 @@ int launch_route(const void* x, const void* gate, int64_t T, int64_t H, int64_t 
                                stream, xb, gb, static_cast<int>(T), static_cast<int>(H), static_cast<int>(E),
                                b.logits));
     const int Ti = static_cast<int>(T), Ei = static_cast<int>(E);
+    if (fused_pack && T > kSmallRouteT) {
+        // Past a few tokens one CTA's issue slots bound the top-k (64 tokens on one
+        // SM took ~14 us); spread it, one warp per token over T/4 CTAs, then pack
+        // in one CTA.
+        const int tk_warps = 4;
+        const int tk_grid = static_cast<int>((T + tk_warps - 1) / tk_warps);
+        PDX_PDL_TRY(with_epl(E, [&](auto epl) {
+            return launch_pdl(k_topk<decltype(epl)::value>, dim3(tk_grid), dim3(tk_warps * 32), 0, stream,
+                              static_cast<const uint16_t*>(b.logits), Ti, Ei, k, normalize, b.selected, b.weights,
+                              zero_ptr, static_cast<int>(zero_words));
+        }));
+        const size_t smem = block_pack_smem_ints(E, T * k, kPackThreads / 32) * sizeof(int);
+        PDX_PDL_TRY(launch_pdl(k_pack_single, dim3(1), dim3(kPackThreads), smem, stream,
+                               static_cast<const int64_t*>(b.selected), static_cast<const uint16_t*>(b.weights), Ti,
+                               k, Ei, *fused_pack));
+        return PDX_OK;
+    }
     if (fused_pack) {
         const size_t smem = topk_pack_smem_bytes(E, T * k);
         PDX_PDL_TRY(with_epl(E, [&](auto epl) {
@@ -418,7 +435,8 @@ int launch_route(const void* x, const void* gate, int64_t T, int64_t H, int64_t 
     const int grid = static_cast<int>((T + warps_per_cta - 1) / warps_per_cta);
     PDX_PDL_TRY(with_epl(E, [&](auto epl) {
         return launch_pdl(k_topk<decltype(epl)::value>, dim3(grid), dim3(warps_per_cta * 32), 0, stream,
-                          static_cast<const uint16_t*>(b.logits), Ti, Ei, k, normalize, b.selected, b.weights);
+                          static_cast<const uint16_t*>(b.logits), Ti, Ei, k, normalize, b.selected, b.weights,
+                          static_cast<unsigned int*>(nullptr), 0);
     }));
     return PDX_OK;
 }
@@ -862,7 +880,7 @@ int pdx_topk_from_logits(const void* logits, int64_t T, int64_t E, int32_t top_k
     with_epl(E, [&](auto epl) {
         k_topk<decltype(epl)::value><<<grid, warps_per_cta * 32, 0, stream>>>(
             static_cast<const uint16_t*>(logits), static_cast<int>(T), static_cast<int>(E), top_k, normalize,
-            selected_out, static_cast<uint16_t*>(weights_out));
+            selected_out, static_cast<uint16_t*>(weights_out), nullptr, 0);
         return 0;
     });
     PDX_LAUNCHED();

@@ -415,11 +415,17 @@ __global__ void __launch_bounds__(256) k_topk_partials(const double* __restrict_
 
 // Softmax + top-k + renormalisation, one warp per token.
 template <int EPL>
+// (Also clears `zero_words` words at `zero_ptr`, spread over the CTAs: the
+// tickets and counters of the decode FFN launch two kernels later.)
 __global__ void __launch_bounds__(256) k_topk(const uint16_t* __restrict__ logits, int T, int E, int k,
                                               int normalize, int64_t* __restrict__ selected,
-                                              uint16_t* __restrict__ weights) {
+                                              uint16_t* __restrict__ weights, unsigned int* __restrict__ zero_ptr,
+                                              int zero_words) {
     griddep_wait();
     griddep_launch();
+    for (int i = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x); i < zero_words;
+         i += static_cast<int>(gridDim.x * blockDim.x))
+        zero_ptr[i] = 0u;
     const int warps = static_cast<int>(blockDim.x >> 5);
     const int first = static_cast<int>(blockIdx.x) * warps + static_cast<int>(threadIdx.x >> 5);
     block_topk_rows<EPL>(logits, T, E, k, normalize != 0, selected, weights, first, gridDim.x * warps);
