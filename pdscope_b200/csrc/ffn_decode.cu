@@ -1,6 +1,6 @@
-// Decode-batch grouped expert FFN in ONE launch: the gate/up and the down
+// Weight-streaming grouped expert FFN in ONE launch: the gate/up and the down
 // projection of every active expert, weights streamed by TMA as the tcgen05 M
-// operand ("swap AB"), with no row gather in front.
+// operand ("swap AB").
 //
 // Reference: expert_forward() -- expertbench/adapters/qwen.py:87-90, run per
 // routed expert by ExpertExecutor.gpu (expertbench/executor.py:454-488).
@@ -16,6 +16,9 @@
 //     column tokens[p].  The tensor core has ~10x more throughput than the
 //     weight stream needs at these sizes, so the extra columns are free and
 //     the gather kernel disappears.
+//     (DIRECT form, T <= 64.  The PACKED form, for larger batches or rows
+//     already in packed order, tiles each expert's packed rows instead, 16,
+//     32 or 64 rows per tile, like phase 2.)
 //   * Phase 2 (down) runs in the same persistent CTAs, on the packed h rows
 //     (N = 16/32/64 rows of one expert per tile).  Its weight tiles need
 //     nothing from phase 1, so the weight producer streams them right behind
@@ -49,13 +52,15 @@ constexpr uint32_t kDecStageBytes = 2 * kDecABytes + kDecMaxT * 64 * 2;  // gate
 constexpr uint32_t kDecTmemCols = 256;  // two accumulators of up to 128 columns
 constexpr int kDecMaxActive = 512;
 constexpr int kDecMaxRows = 1024;
-constexpr size_t kDecSmemBytes = 1024 + kDecStages * kDecStageBytes + 256 + 4 * (kDecMaxActive + 1) * 4 +
+// tables after the stages and barriers: phase-1 and phase-2 tile prefixes,
+// segment start, row count, weight slot (per active expert), tokens (per row)
+constexpr size_t kDecSmemBytes = 1024 + kDecStages * kDecStageBytes + 256 + 5 * (kDecMaxActive + 1) * 4 +
                                  kDecMaxRows * 4;
 
 struct DecodeArgs {
     const int32_t* offsets;        // [E+1] packed segment starts
     const int32_t* active;         // [E+1] active count, then the active expert ids
-    const int32_t* tokens;         // [rows] packed row -> token
+    const int32_t* tokens;         // [rows] packed row -> token (DIRECT form)
     const int32_t* slot_of_expert; // NULL = identity
     int64_t num_slots;
     int64_t gate_rows_per_slot;    // TMA-map rows between consecutive slots
@@ -65,9 +70,10 @@ struct DecodeArgs {
     int splits1, splits2;          // K slices per tile of each phase
     uint16_t* h;                   // [rows, I]
     uint16_t* y;                   // [rows, H]
-    float* partials1;              // [I/128][splits1][rows][2][128] when splits1 > 1
+    float* partials1;              // splits1 > 1: DIRECT [I/128][splits1][rows][2][128],
+                                   //   PACKED [phase-1 units][2*NB][128]
     float* partials2;              // [phase-2 units][NT2][128] when splits2 > 1
-    unsigned int* tickets1;        // [active * I/128 * 4], zero on entry
+    unsigned int* tickets1;        // [phase-1 tiles * 4], zero on entry
     unsigned int* tickets2;        // [phase-2 tiles * 4], zero on entry
     unsigned int* h_ready;         // [active], zero on entry
 };
@@ -103,13 +109,55 @@ struct DecUnit {
     int phase2;  // 0: gate/up, 1: down
     int a;       // index into the active-expert tables
     int ib;      // 128-row weight block
-    int nb;      // NT2-row token block (phase 2)
+    int nb;      // token-row block of the expert's segment (0 in the DIRECT phase 1)
     int tile;    // tile index within its phase
     int slice;
     int kb0, kb1;
 };
 
-template <int NB, int NT2>
+// Exclusive prefix over the active experts of `tiles(a)` (one warp), written
+// to pre[]; returns the total in every lane.
+template <typename F>
+__device__ __forceinline__ int warp_tile_prefix(int n_active, int* pre, F tiles) {
+    const uint32_t lane = lane_id();
+    const int per = (n_active + 31) / 32;
+    const int b = static_cast<int>(lane) * per;
+    int local = 0;
+    for (int i = 0; i < per; ++i)
+        if (b + i < n_active) {
+            const int t = tiles(b + i);
+            pre[b + i] = t;
+            local += t;
+        }
+    int inc = local;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, inc, off);
+        if (static_cast<int>(lane) >= off) inc += v;
+    }
+    int run = inc - local;
+    for (int i = 0; i < per; ++i)
+        if (b + i < n_active) {
+            const int t = pre[b + i];
+            pre[b + i] = run;
+            run += t;
+        }
+    return __shfl_sync(0xffffffffu, inc, 31);
+}
+
+// Largest a < n with pre[a] <= tile.
+__device__ __forceinline__ int find_expert(const int* pre, int n, int tile) {
+    int lo = 0, hi = n - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (pre[mid] <= tile) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+// DIRECT: phase-1 B operand = x [T, H] (tm_x box NB rows), NB >= T.
+// PACKED: phase-1 B operand = the packed rows (tm_x over [rows, H], box NB).
+template <bool DIRECT, int NB, int NT2>
 __global__ void __launch_bounds__(kDecThreads, 1)
     k_decode_ffn(const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_u,
                  const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_d,
@@ -125,9 +173,10 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     uint64_t* drain_bar = tmem_empty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    int* s_misc = reinterpret_cast<int*>(tmem_slot + 2);  // [0] phase-2 tiles
+    int* s_misc = reinterpret_cast<int*>(tmem_slot + 2);  // [0] phase-2 tiles, [1] phase-1 tiles
     int* prefix2 = reinterpret_cast<int*>(smem + kDecStages * kDecStageBytes + 256);
-    int* t_seg0 = prefix2 + (kDecMaxActive + 1);
+    int* prefix1 = prefix2 + (kDecMaxActive + 1);
+    int* t_seg0 = prefix1 + (kDecMaxActive + 1);
     int* t_rows = t_seg0 + (kDecMaxActive + 1);
     int* t_slot = t_rows + (kDecMaxActive + 1);
     int* s_tok = t_slot + (kDecMaxActive + 1);
@@ -173,42 +222,31 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     const int n_active = min(args.active[0], kDecMaxActive);
     const int n_rows = min(args.rows, kDecMaxRows);
     if (warp == 2) {
-        // phase-2 tiles per active expert = m2 * ceil(n_e / NT2) -> exclusive prefix
-        const int per = (n_active + 31) / 32;
-        const int b = static_cast<int>(lane) * per;
-        int local = 0;
-        for (int i = 0; i < per; ++i)
-            if (b + i < n_active) {
-                const int e = args.active[1 + b + i];
-                const int seg0 = args.offsets[e];
-                const int rows = args.offsets[e + 1] - seg0;
-                int64_t slot = args.slot_of_expert ? args.slot_of_expert[e] : e;
-                if (slot < 0 || slot >= args.num_slots) {
-                    raise_error(PDX_DEVERR_BAD_SLOT);
-                    slot = 0;  // keeps the pipeline consistent; the call is flagged invalid
-                }
-                const int tiles = m2 * ((rows + NT2 - 1) / NT2);
-                prefix2[b + i] = tiles;
-                t_seg0[b + i] = seg0;
-                t_rows[b + i] = rows;
-                t_slot[b + i] = static_cast<int>(slot);
-                local += tiles;
+        // per active expert: segment, rows, slot; tiles per expert of phase 1
+        // (DIRECT m1, PACKED m1 * ceil(n_e / NB)) and phase 2 (m2 * ceil(n_e /
+        // NT2)) -> exclusive prefixes
+        for (int i = static_cast<int>(lane); i < n_active; i += 32) {
+            const int e = args.active[1 + i];
+            const int seg0 = args.offsets[e];
+            int64_t slot = args.slot_of_expert ? args.slot_of_expert[e] : e;
+            if (slot < 0 || slot >= args.num_slots) {
+                raise_error(PDX_DEVERR_BAD_SLOT);
+                slot = 0;  // keeps the pipeline consistent; the call is flagged invalid
             }
-        int inc = local;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const int v = __shfl_up_sync(0xffffffffu, inc, off);
-            if (static_cast<int>(lane) >= off) inc += v;
+            t_seg0[i] = seg0;
+            t_rows[i] = args.offsets[e + 1] - seg0;
+            t_slot[i] = static_cast<int>(slot);
         }
-        int run = inc - local;
-        for (int i = 0; i < per; ++i)
-            if (b + i < n_active) {
-                const int t = prefix2[b + i];
-                prefix2[b + i] = run;
-                run += t;
-            }
-        if (lane == 31) s_misc[0] = inc;
-    } else if (warp >= 3) {
+        __syncwarp();
+        const int tot2 = warp_tile_prefix(n_active, prefix2, [&](int a) { return m2 * ((t_rows[a] + NT2 - 1) / NT2); });
+        const int tot1 = DIRECT ? n_active * m1
+                                : warp_tile_prefix(n_active, prefix1,
+                                                   [&](int a) { return m1 * ((t_rows[a] + NB - 1) / NB); });
+        if (lane == 0) {
+            s_misc[0] = tot2;
+            s_misc[1] = tot1;
+        }
+    } else if (DIRECT && warp >= 3) {
         for (int i = static_cast<int>(threadIdx.x) - 96; i < n_rows; i += kDecThreads - 96) {
             int t = args.tokens[i];
             if (t < 0 || t >= args.T) {
@@ -222,7 +260,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const int units1 = n_active * m1 * s1;
+    const int units1 = s_misc[1] * s1;
     const int total_units = units1 + s_misc[0] * s2;
 
     auto decode = [&](int u) {
@@ -231,9 +269,17 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             d.phase2 = 0;
             d.tile = u / s1;
             d.slice = u % s1;
-            d.a = d.tile / m1;
-            d.ib = d.tile % m1;
-            d.nb = 0;
+            if (DIRECT) {
+                d.a = d.tile / m1;
+                d.ib = d.tile % m1;
+                d.nb = 0;
+            } else {
+                d.a = find_expert(prefix1, n_active, d.tile);
+                const int nbc = (t_rows[d.a] + NB - 1) / NB;
+                const int local = d.tile - prefix1[d.a];
+                d.ib = local / nbc;
+                d.nb = local % nbc;
+            }
             d.kb0 = (d.slice * nkb1) / s1;
             d.kb1 = ((d.slice + 1) * nkb1) / s1;
         } else {
@@ -241,11 +287,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             d.phase2 = 1;
             d.tile = v / s2;
             d.slice = v % s2;
-            int lo = 0, hi = n_active - 1;
-            while (lo < hi) {
-                const int mid = (lo + hi + 1) >> 1;
-                if (prefix2[mid] <= d.tile) lo = mid; else hi = mid - 1;
-            }
+            const int lo = find_expert(prefix2, n_active, d.tile);
             d.a = lo;
             const int nbc = (t_rows[lo] + NT2 - 1) / NT2;
             const int local = d.tile - prefix2[lo];
@@ -291,12 +333,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            const unsigned int h_target = 4u * static_cast<unsigned int>(m1);
             for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
                 const DecUnit d = decode(u);
-                int row_b = 0;
+                int row_b = DIRECT ? 0 : t_seg0[d.a] + d.nb * NB;
                 if (d.phase2) {
-                    // this expert's h rows: wait until every phase-1 tile of it is stored
+                    // this expert's h rows: wait until every phase-1 tile of it is
+                    // stored (four quadrant warps per tile)
+                    const unsigned int h_target =
+                        4u * static_cast<unsigned int>(DIRECT ? m1 : m1 * ((t_rows[d.a] + NB - 1) / NB));
                     const unsigned int* flag = args.h_ready + d.a;
                     if (ld_acquire_gpu(flag) < h_target) {
                         const unsigned long long t0 = global_timer_ns();
@@ -324,7 +368,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                     if (d.phase2)
                         tma_load_2d(sb, &tm_h, &full_bar[stage], kb * 64, row_b);
                     else
-                        tma_load_2d(sb, &tm_x, &full_bar[stage], kb * 64, 0);
+                        tma_load_2d(sb, &tm_x, &full_bar[stage], kb * 64, row_b);
                     if (++stage == kDecStages) { stage = 0; phase ^= 1u; }
                 }
             }
@@ -386,7 +430,56 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * 128);
             const int seg0 = t_seg0[d.a];
             const int ne = t_rows[d.a];
-            if (!d.phase2) {
+            if (!d.phase2 && !DIRECT) {
+                // gate columns [0, NB), up columns [NB, 2 NB): rows seg0 + nb*NB + t
+                float acc[2 * NB];
+#pragma unroll
+                for (int c = 0; c < 2 * NB; c += 16) {
+                    uint32_t r[16];
+                    tmem_ld16(taddr + c, r);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) acc[c + j] = __uint_as_float(r[j]);
+                }
+                tc_fence_before();
+                mbar_arrive(&tmem_empty[b]);
+                bool publish = true;
+                if (s1 > 1) {
+                    float* mine = args.partials1 + static_cast<size_t>(u) * 2 * NB * 128;
+#pragma unroll
+                    for (int c = 0; c < 2 * NB; ++c) mine[c * 128 + i_row] = acc[c];
+                    __threadfence();
+                    __syncwarp();
+                    unsigned int prev = 0;
+                    if (lane == 0) prev = atomicAdd(&args.tickets1[d.tile * 4 + q], 1u);
+                    prev = __shfl_sync(0xffffffffu, prev, 0);
+                    publish = prev == static_cast<unsigned int>(s1 - 1);
+                    if (publish) {
+                        __threadfence();
+                        const float* base = args.partials1 + static_cast<size_t>(d.tile) * s1 * 2 * NB * 128;
+#pragma unroll
+                        for (int c = 0; c < 2 * NB; ++c) acc[c] = __ldcg(base + c * 128 + i_row);
+                        for (int s = 1; s < s1; ++s) {
+                            const float* p = base + static_cast<size_t>(s) * 2 * NB * 128;
+#pragma unroll
+                            for (int c = 0; c < 2 * NB; ++c) acc[c] += __ldcg(p + c * 128 + i_row);
+                        }
+                    }
+                }
+                if (!publish) continue;
+                const int col = d.ib * 128 + i_row;
+#pragma unroll
+                for (int t = 0; t < NB; ++t) {
+                    const int r = d.nb * NB + t;
+                    if (r < ne)
+                        args.h[static_cast<int64_t>(seg0 + r) * args.I + col] =
+                            f2bits(swiglu_bf16(__float_as_uint(acc[t]), __float_as_uint(acc[NB + t])));
+                }
+                fence_proxy_async_global();
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) red_release_gpu_add(args.h_ready + d.a, 1u);
+            } else if (!d.phase2) {
                 // gate column tokens[p] and up column NB + tokens[p] of every routed row p
                 const int col = d.ib * 128 + i_row;
                 float* part = nullptr;

@@ -178,15 +178,13 @@ int device_setup(int* sms_out) {
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_stream_gemm<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ss));
         PDX_CUDA_TRY(cudaFuncSetAttribute(k_stream_gemm<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ss));
         const int ds = static_cast<int>(kDecSmemBytes);
-        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<16, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
-        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<16, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
-        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<16, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
-        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<32, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
-        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<32, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
-        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<32, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
-        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<64, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
-        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<64, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
-        PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<64, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds));
+#define PDX_DEC_ATTR(D, NB, NT2) \
+    PDX_CUDA_TRY(cudaFuncSetAttribute(k_decode_ffn<D, NB, NT2>, cudaFuncAttributeMaxDynamicSharedMemorySize, ds))
+        PDX_DEC_ATTR(true, 16, 16); PDX_DEC_ATTR(true, 16, 32); PDX_DEC_ATTR(true, 16, 64);
+        PDX_DEC_ATTR(true, 32, 16); PDX_DEC_ATTR(true, 32, 32); PDX_DEC_ATTR(true, 32, 64);
+        PDX_DEC_ATTR(true, 64, 16); PDX_DEC_ATTR(true, 64, 32); PDX_DEC_ATTR(true, 64, 64);
+        PDX_DEC_ATTR(false, 16, 16); PDX_DEC_ATTR(false, 32, 32); PDX_DEC_ATTR(false, 64, 64);
+#undef PDX_DEC_ATTR
         g_num_sms[dev] = sms;
         g_attrs_set[dev] = true;
     }
@@ -529,36 +527,47 @@ StreamPlan plan_stream(int64_t rows, int64_t E, int64_t H, int64_t I) {
     return p;
 }
 
-// Single-launch decode FFN (ffn_decode.cu): the whole token matrix x [T, H]
-// is the gate/up N operand, so it needs the packed tokens and T <= 64, and
-// its shared-memory tables bound the rows and active experts.
-bool decode_fused_ok(int64_t T, int64_t rows, int64_t E, int64_t H, int64_t I, const int32_t* tokens) {
+// Single-launch weight-streaming FFN (ffn_decode.cu).  DIRECT form: the whole
+// token matrix x [T, H] is the gate/up N operand, so it needs the packed
+// tokens and T <= 64, and its shared-memory tables bound the rows.  PACKED
+// form: gate/up tiles over packed rows (gathered first when tokens are
+// given).  Both bound the active experts by the shared-memory tables.
+bool decode_direct_ok(int64_t T, int64_t rows, int64_t E, int64_t H, int64_t I, const int32_t* tokens) {
     return tokens != nullptr && T >= 1 && T <= kDecMaxT && rows <= kDecMaxRows &&
            std::min(E, rows) <= kDecMaxActive && stream_shape_ok(H, I);
 }
+bool decode_packed_ok(int64_t rows, int64_t E, int64_t H, int64_t I) {
+    return std::min(E, rows) <= kDecMaxActive && stream_shape_ok(H, I);
+}
 
 struct DecodePlan {
-    int nb, nt2;          // gate/up token columns (T rounded up to 16), down token tile
+    bool direct;
+    int nb, nt2;          // gate/up token tile (DIRECT: T rounded up to 16), down token tile
     int s1, s2;           // K slices per tile of each projection
     int64_t tiles1, tiles2;
     size_t p1_bytes, p2_bytes;
     int64_t zero_words;   // tickets of both projections + per-expert h counters
 };
 
-// Depends only on (rows, E, H, I) and T, so the workspace query (which sizes
-// for any T) and the launch agree; the split counts are plan_stream's.
-DecodePlan plan_decode(int64_t T, int64_t rows, int64_t E, int64_t H, int64_t I) {
+// Depends only on (rows, E, H, I), the form and T, so the workspace query
+// (which sizes for any T) and the launch agree; token tiles and split counts
+// are plan_stream's.
+DecodePlan plan_decode(int64_t T, int64_t rows, int64_t E, int64_t H, int64_t I, bool direct) {
     DecodePlan p{};
+    p.direct = direct;
     const int64_t est = std::max<int64_t>(1, std::min(E, rows));
     const int64_t avg = (rows + est - 1) / est;
-    p.nb = T <= 16 ? 16 : (T <= 32 ? 32 : 64);
-    p.nt2 = avg <= 12 ? 16 : (avg <= 24 ? 32 : 64);
+    const int nt = avg <= 12 ? 16 : (avg <= 24 ? 32 : 64);
+    p.nb = direct ? (T <= 16 ? 16 : (T <= 32 ? 32 : 64)) : nt;
+    p.nt2 = nt;
     const int64_t m1 = I / 128, m2 = H / 128;
-    p.tiles1 = est * m1;
+    p.tiles1 = direct ? est * m1 : m1 * (rows / p.nb + est);
     p.tiles2 = m2 * (rows / p.nt2 + est);
     p.s1 = plan_splits(static_cast<int>(H / 64), m1 * est);
     p.s2 = plan_splits(static_cast<int>(I / 64), m2 * est);
-    p.p1_bytes = p.s1 > 1 ? static_cast<size_t>(m1 * p.s1 * rows) * 256 * 4 : 0;
+    if (p.s1 > 1)
+        p.p1_bytes = direct ? static_cast<size_t>(m1 * p.s1 * rows) * 256 * 4
+                            : static_cast<size_t>(p.tiles1 * p.s1 * 2 * p.nb) * 128 * 4;
     p.p2_bytes = p.s2 > 1 ? static_cast<size_t>(p.tiles2 * p.s2 * p.nt2) * 128 * 4 : 0;
     p.zero_words = 4 * p.tiles1 + 4 * p.tiles2 + est;
     return p;
@@ -567,15 +576,17 @@ DecodePlan plan_decode(int64_t T, int64_t rows, int64_t E, int64_t H, int64_t I)
 struct DecodeBufs {
     DecodePlan plan;
     uint16_t* h;
+    uint16_t* xp;            // PACKED form: gathered token rows
     float* p1;
     float* p2;
     unsigned int* counters;  // zero_words words, cleared before every launch
 };
 
-DecodeBufs carve_decode(Carver& c, int64_t T, int64_t rows, int64_t E, int64_t H, int64_t I) {
-    DecodeBufs b;
-    b.plan = plan_decode(T, rows, E, H, I);
+DecodeBufs carve_decode(Carver& c, int64_t T, int64_t rows, int64_t E, int64_t H, int64_t I, bool direct) {
+    DecodeBufs b{};
+    b.plan = plan_decode(T, rows, E, H, I, direct);
     b.h = static_cast<uint16_t*>(c.take(static_cast<size_t>(rows) * I * 2));
+    if (!direct) b.xp = static_cast<uint16_t*>(c.take(static_cast<size_t>(rows) * H * 2));
     b.p1 = static_cast<float*>(c.take(std::max<size_t>(b.plan.p1_bytes, 16)));
     b.p2 = static_cast<float*>(c.take(std::max<size_t>(b.plan.p2_bytes, 16)));
     b.counters = static_cast<unsigned int*>(c.take(static_cast<size_t>(b.plan.zero_words) * 4));
@@ -584,10 +595,11 @@ DecodeBufs carve_decode(Carver& c, int64_t T, int64_t rows, int64_t E, int64_t H
 
 size_t ffn_ws_bytes(int64_t rows, int64_t E, int64_t H, int64_t I, int mode) {
     if (mode == PDX_FFN_GEMV) {
-        // either form may run (the single-launch one needs the tokens and T <= 64)
-        Carver c{nullptr, SIZE_MAX};
-        carve_decode(c, 1, rows, E, H, I);
-        return std::max(c.used, ffn_ws_bytes(rows, E, H, I, PDX_FFN_GEMV_STAGED));
+        // any of the single-launch forms or the staged one may run
+        Carver c1{nullptr, SIZE_MAX}, c2{nullptr, SIZE_MAX};
+        carve_decode(c1, 1, rows, E, H, I, true);
+        carve_decode(c2, 1, rows, E, H, I, false);
+        return std::max(std::max(c1.used, c2.used), ffn_ws_bytes(rows, E, H, I, PDX_FFN_GEMV_STAGED));
     }
     if (mode == PDX_FFN_GEMV_STAGED) mode = PDX_FFN_GEMV;
     size_t b = align_up(static_cast<size_t>(rows) * I * 2);                        // h
@@ -612,24 +624,26 @@ int launch_stream_pair(const CUtensorMap& tm_g, const CUtensorMap& tm_u, const C
     return PDX_OK;
 }
 
-template <int NB>
-int launch_decode_nt2(int nt2, dim3 grid, const CUtensorMap& tm_g, const CUtensorMap& tm_u, const CUtensorMap& tm_x,
-                      const CUtensorMap& tm_d, const CUtensorMap& tm_h, const DecodeArgs& a, cudaStream_t stream) {
-    if (nt2 == 16)
-        PDX_PDL_TRY(launch_pdl(k_decode_ffn<NB, 16>, grid, dim3(kDecThreads), kDecSmemBytes, stream, tm_g, tm_u, tm_x,
-                               tm_d, tm_h, a));
-    else if (nt2 == 32)
-        PDX_PDL_TRY(launch_pdl(k_decode_ffn<NB, 32>, grid, dim3(kDecThreads), kDecSmemBytes, stream, tm_g, tm_u, tm_x,
-                               tm_d, tm_h, a));
-    else
-        PDX_PDL_TRY(launch_pdl(k_decode_ffn<NB, 64>, grid, dim3(kDecThreads), kDecSmemBytes, stream, tm_g, tm_u, tm_x,
-                               tm_d, tm_h, a));
+template <bool DIRECT, int NB, int NT2>
+int launch_decode_kernel(dim3 grid, const CUtensorMap& tm_g, const CUtensorMap& tm_u, const CUtensorMap& tm_x,
+                         const CUtensorMap& tm_d, const CUtensorMap& tm_h, const DecodeArgs& a, cudaStream_t stream) {
+    PDX_PDL_TRY(launch_pdl(k_decode_ffn<DIRECT, NB, NT2>, grid, dim3(kDecThreads), kDecSmemBytes, stream, tm_g, tm_u,
+                           tm_x, tm_d, tm_h, a));
     return PDX_OK;
 }
 
-// The single-launch decode FFN.  `zeroed`: the kernel before it in the stream
-// already cleared b.counters (the fused top-k + pack of pdx_moe_layer does);
-// otherwise a clearing kernel is launched first.
+template <int NB>
+int launch_decode_direct(int nt2, dim3 grid, const CUtensorMap& tm_g, const CUtensorMap& tm_u,
+                         const CUtensorMap& tm_x, const CUtensorMap& tm_d, const CUtensorMap& tm_h,
+                         const DecodeArgs& a, cudaStream_t stream) {
+    if (nt2 == 16) return launch_decode_kernel<true, NB, 16>(grid, tm_g, tm_u, tm_x, tm_d, tm_h, a, stream);
+    if (nt2 == 32) return launch_decode_kernel<true, NB, 32>(grid, tm_g, tm_u, tm_x, tm_d, tm_h, a, stream);
+    return launch_decode_kernel<true, NB, 64>(grid, tm_g, tm_u, tm_x, tm_d, tm_h, a, stream);
+}
+
+// The single-launch FFN.  `zeroed`: the kernel before it in the stream already
+// cleared b.counters (the routing kernels of pdx_moe_layer do); otherwise the
+// row gather (PACKED form with tokens) or a clearing kernel does it first.
 int launch_decode_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* offsets, const int32_t* active,
                       int64_t rows, const pdx_expert_weights* w, int64_t H, int64_t I, void* y, const DecodeBufs& b,
                       bool zeroed, cudaStream_t stream) {
@@ -637,9 +651,17 @@ int launch_decode_ffn(const void* x, int64_t T, const int32_t* tokens, const int
     int st = device_setup(&sms);
     if (st) return st;
     const DecodePlan& p = b.plan;
-    if (!zeroed)
-        PDX_PDL_TRY(launch_pdl(k_zero_words, dim3(static_cast<unsigned>(std::min<int64_t>(64, (p.zero_words + 255) / 256))),
-                               dim3(256), 0, stream, b.counters, static_cast<int>(p.zero_words)));
+    const int zero_words = zeroed ? 0 : static_cast<int>(p.zero_words);
+    const void* xb = x;   // phase-1 B operand
+    if (!p.direct && tokens) {
+        PDX_PDL_TRY(launch_pdl(k_gather_rows, dim3(static_cast<unsigned>(rows)), dim3(kCombineThreads), 0, stream,
+                               static_cast<const uint16_t*>(x), tokens, static_cast<int>(rows), static_cast<int>(H),
+                               b.xp, b.counters, zero_words));
+        xb = b.xp;
+    } else if (zero_words > 0) {
+        PDX_PDL_TRY(launch_pdl(k_zero_words, dim3(static_cast<unsigned>(std::min(64, (zero_words + 255) / 256))),
+                               dim3(256), 0, stream, b.counters, zero_words));
+    }
     const int64_t gs = w->num_slots > 1 ? w->gate_stride / H : 0;
     const int64_t us = w->num_slots > 1 ? w->up_stride / H : 0;
     const int64_t ds = w->num_slots > 1 ? w->down_stride / I : 0;
@@ -649,25 +671,34 @@ int launch_decode_ffn(const void* x, int64_t T, const int32_t* tokens, const int
     if ((st = encode_2d(&tm_g, w->gate, (w->num_slots - 1) * gs + I, H, 128))) return st;
     if ((st = encode_2d(&tm_u, w->up, (w->num_slots - 1) * us + I, H, 128))) return st;
     if ((st = encode_2d(&tm_d, w->down, (w->num_slots - 1) * ds + H, I, 128))) return st;
-    if ((st = encode_2d(&tm_x, x, T, H, p.nb))) return st;
+    if ((st = encode_2d(&tm_x, xb, p.direct ? T : rows, H, p.nb))) return st;
     if ((st = encode_2d(&tm_h, b.h, rows, I, p.nt2))) return st;
     DecodeArgs a{offsets, active, tokens, w->slot_of_expert, w->num_slots, gs, us, ds,
                  static_cast<int>(H), static_cast<int>(I), static_cast<int>(T), static_cast<int>(rows),
                  p.s1, p.s2, b.h, static_cast<uint16_t*>(y), b.p1, b.p2,
                  b.counters, b.counters + 4 * p.tiles1, b.counters + 4 * p.tiles1 + 4 * p.tiles2};
     const dim3 grid(static_cast<unsigned>(std::min<int64_t>(sms, p.tiles1 * p.s1 + p.tiles2 * p.s2)));
-    if (p.nb == 16) return launch_decode_nt2<16>(p.nt2, grid, tm_g, tm_u, tm_x, tm_d, tm_h, a, stream);
-    if (p.nb == 32) return launch_decode_nt2<32>(p.nt2, grid, tm_g, tm_u, tm_x, tm_d, tm_h, a, stream);
-    return launch_decode_nt2<64>(p.nt2, grid, tm_g, tm_u, tm_x, tm_d, tm_h, a, stream);
+    if (!p.direct) {
+        if (p.nb == 16) return launch_decode_kernel<false, 16, 16>(grid, tm_g, tm_u, tm_x, tm_d, tm_h, a, stream);
+        if (p.nb == 32) return launch_decode_kernel<false, 32, 32>(grid, tm_g, tm_u, tm_x, tm_d, tm_h, a, stream);
+        return launch_decode_kernel<false, 64, 64>(grid, tm_g, tm_u, tm_x, tm_d, tm_h, a, stream);
+    }
+    if (p.nb == 16) return launch_decode_direct<16>(p.nt2, grid, tm_g, tm_u, tm_x, tm_d, tm_h, a, stream);
+    if (p.nb == 32) return launch_decode_direct<32>(p.nt2, grid, tm_g, tm_u, tm_x, tm_d, tm_h, a, stream);
+    return launch_decode_direct<64>(p.nt2, grid, tm_g, tm_u, tm_x, tm_d, tm_h, a, stream);
 }
 
 int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* offsets, const int32_t* active,
                int64_t E, int64_t rows, const pdx_expert_weights* w, int64_t H, int64_t I, void* y, int mode,
                Carver& ws, cudaStream_t stream) {
-    if (mode == PDX_FFN_GEMV && decode_fused_ok(T, rows, E, H, I, tokens)) {
-        const DecodeBufs b = carve_decode(ws, T, rows, E, H, I);
-        if (ws.overflow) return fail(PDX_ERR_WORKSPACE, "FFN workspace too small (%zu > %zu bytes)", ws.used, ws.cap);
-        return launch_decode_ffn(x, T, tokens, offsets, active, rows, w, H, I, y, b, false, stream);
+    if (mode == PDX_FFN_GEMV) {
+        const bool direct = decode_direct_ok(T, rows, E, H, I, tokens);
+        if (direct || decode_packed_ok(rows, E, H, I)) {
+            const DecodeBufs b = carve_decode(ws, T, rows, E, H, I, direct);
+            if (ws.overflow)
+                return fail(PDX_ERR_WORKSPACE, "FFN workspace too small (%zu > %zu bytes)", ws.used, ws.cap);
+            return launch_decode_ffn(x, T, tokens, offsets, active, rows, w, H, I, y, b, false, stream);
+        }
     }
     if (mode == PDX_FFN_GEMV_STAGED) mode = PDX_FFN_GEMV;
     int sms = 0;
@@ -1076,9 +1107,9 @@ int pdx_moe_layer(const void* x, const void* gate, int64_t T, int64_t H, int64_t
     PackBufs pb = carve_pack(c, T, top_k, E, counts_out);
     uint16_t* y = static_cast<uint16_t*>(c.take(N * H * 2));
     // decode batches: both projections in one launch straight from x
-    const bool one_launch = m == PDX_FFN_GEMV && decode_fused_ok(T, N, E, H, I, pb.o.tokens);
+    const bool one_launch = m == PDX_FFN_GEMV && decode_direct_ok(T, N, E, H, I, pb.o.tokens);
     DecodeBufs db{};
-    if (one_launch) db = carve_decode(c, T, N, E, H, I);
+    if (one_launch) db = carve_decode(c, T, N, E, H, I, true);
     if (c.overflow) return fail(PDX_ERR_WORKSPACE, "layer workspace too small (%zu > %zu bytes)", c.used, c.cap);
     // the routing kernel also packs when the pack's shared memory fits the default 48 KiB
     // (and then clears the single-launch FFN's tickets and counters)

@@ -65,7 +65,8 @@ def test_expert_forward_vs_torch_on_device(pdx):
         np.testing.assert_allclose(f32(ours), f32(ref), rtol=RTOL, atol=ATOL)
 
 
-def _grouped_case(pdx, tokens, experts, k, hidden, inter, mode, seed, slot_perm=False, zipf=False, check=True):
+def _grouped_case(pdx, tokens, experts, k, hidden, inter, mode, seed, slot_perm=False, zipf=False, check=True,
+                  prepacked=False):
     from tests.gpu_util import to_bits, to_dev
     from pdscope_b200 import _lib
     from pdscope_b200.runtime import ExpertSlab
@@ -95,8 +96,13 @@ def _grouped_case(pdx, tokens, experts, k, hidden, inter, mode, seed, slot_perm=
     ws_bytes = _lib.lib.pdx_ffn_workspace_bytes(rows, experts, hidden, inter, mode)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
     xd = to_dev(x)
+    tok_ptr = ctypes.c_void_p(dev["tokens"].data_ptr())
+    x_rows = tokens
+    if prepacked:  # rows already in packed order (tokens == NULL), as the expert-parallel exchange hands them over
+        xd = xd[dev["tokens"].long()].contiguous()
+        tok_ptr, x_rows = None, rows
     _lib.check(_lib.lib.pdx_moe_ffn_grouped(
-        ctypes.c_void_p(xd.data_ptr()), tokens, ctypes.c_void_p(dev["tokens"].data_ptr()),
+        ctypes.c_void_p(xd.data_ptr()), x_rows, tok_ptr,
         ctypes.c_void_p(dev["offsets"].data_ptr()), ctypes.c_void_p(active.data_ptr()), experts, rows,
         ctypes.byref(slab.struct), hidden, inter, ctypes.c_void_p(y.data_ptr()), mode,
         ctypes.c_void_p(ws.data_ptr()), ws.numel(), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
@@ -138,7 +144,9 @@ def test_grouped_ffn_qwen3_shape(pdx, mode, tokens):
 @pytest.mark.parametrize("tokens,experts,k,hidden,inter,zipf", (
     (1, 128, 8, 2048, 768, False), (2, 128, 8, 2048, 768, False), (8, 128, 8, 2048, 768, False),
     (16, 64, 8, 1024, 512, False), (17, 128, 8, 2048, 768, False), (33, 32, 8, 512, 256, False),
-    (64, 128, 8, 2048, 768, False), (64, 16, 4, 256, 128, True), (40, 8, 8, 512, 256, True)))
+    (64, 128, 8, 2048, 768, False), (64, 16, 4, 256, 128, True), (40, 8, 8, 512, 256, True),
+    (65, 128, 8, 2048, 768, False), (130, 128, 8, 2048, 768, True), (512, 128, 8, 2048, 768, False),
+    (300, 16, 4, 256, 128, True)))
 def test_single_launch_decode_matches_staged(pdx, tokens, experts, k, hidden, inter, zipf):
     """The decode FFN in one launch (mode 1 with T <= 64: gate/up on the whole
     token matrix, down in the same launch behind per-expert h counters)
@@ -148,12 +156,23 @@ def test_single_launch_decode_matches_staged(pdx, tokens, experts, k, hidden, in
     tickets and counters are cleared before every launch).  Cases cover split-K
     in either projection (few active experts), Zipf-skewed experts with more
     rows than one down tile, every token on every expert, and T not a multiple
-    of 16."""
+    of 16; past 64 tokens the single launch tiles the gate/up GEMM over the
+    gathered rows (config 1 at T = 512 among them)."""
     a = _grouped_case(pdx, tokens, experts, k, hidden, inter, 6, 300 + tokens, zipf=zipf)
     b = _grouped_case(pdx, tokens, experts, k, hidden, inter, 1, 300 + tokens, zipf=zipf)
     c = _grouped_case(pdx, tokens, experts, k, hidden, inter, 1, 300 + tokens, zipf=zipf)
     assert np.array_equal(a, b)
     assert np.array_equal(b, c)
+
+
+@pytest.mark.parametrize("tokens,experts", ((8, 128), (64, 16), (200, 128)))
+def test_single_launch_prepacked_rows(pdx, tokens, experts):
+    """Rows handed over already in packed order (tokens == NULL, the
+    expert-parallel exchange's form): the single launch tiles them directly
+    and matches the staged form bit for bit."""
+    a = _grouped_case(pdx, tokens, experts, 8, 2048, 768, 6, 700 + tokens, prepacked=True)
+    b = _grouped_case(pdx, tokens, experts, 8, 2048, 768, 1, 700 + tokens, prepacked=True)
+    assert np.array_equal(a, b)
 
 
 def test_ffn_paths_agree(pdx):
