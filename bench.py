@@ -747,9 +747,11 @@ def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
             clocks = sampler.summary()
         else:
             ms = timed(lambda: stack.step(t_count), K, W)
-        local_bytes = L * el * expert_bytes  # every local expert receives rows at these batch sizes x ranks
+        act = stack.local_active_experts()   # this rank's experts that received rows, per layer
+        local_bytes = sum(act) * expert_bytes
         decode[t_count] = dict(ms_per_step=ms / K, tok_s=world * t_count * K / (ms / 1e3),
                                launches_per_step=launches,
+                               local_active_experts_per_layer=statistics.mean(act),
                                local_weight_gb_per_step=local_bytes / 1e9,
                                hbm_gbs_step_per_gpu=local_bytes / 1e9 / (ms / K / 1e3))
         if peer is not None:
@@ -797,8 +799,8 @@ def run_expert_parallel(args, rank, local_rank, world, dev, dist, K, W, pk, L):
                     dtype="bf16", data="synthetic", config=config,
                     execution=(f"expert parallel, {el} experts per GPU, dispatch/combine exchange over NVLink, "
                                f"one CUDA graph per step"),
-                    roofline=dict(bound="hbm", kernel="whole expert-parallel decode step (local expert weights "
-                                                      "per step / step time, per GPU)",
+                    roofline=dict(bound="hbm", kernel="whole expert-parallel decode step (weights of the local "
+                                                      "experts that received rows / step time, per GPU)",
                                   achieved=d["hbm_gbs_step_per_gpu"], peak=pk["hbm_gbs"], unit="GB/s",
                                   frac=d["hbm_gbs_step_per_gpu"] / pk["hbm_gbs"], peak_source=pk["source"],
                                   traffic=None),

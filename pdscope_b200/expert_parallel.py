@@ -201,6 +201,7 @@ class ExpertParallelMoE:
         if recv.shape[0] == 0:
             return recv
         lay = self.ops.layout(recv_counts, self.world, self.local, capacity, recv.shape[0])
+        self.last_active = lay.active
         grouped = self.ops.regroup(recv, lay)
         mode = _lib.FFN_GEMV if capacity > 0 else _lib.FFN_AUTO   # decode: weight-streaming path
         y = self.ops.ffn(grouped, lay, self.slab, mode)
@@ -245,6 +246,7 @@ class ExpertParallelMoE:
                     perm=torch.empty(rows_cap, dtype=torch.int32, device=dev), experts=EL)
         check(lib.pdx_ep_layout_p2p(R, self.rank, EL, cap, rows_cap, lay, _ptr(ly.offsets), _ptr(ly.active),
                                     _ptr(ly.perm), s))
+        self.last_active = ly.active   # this rank's active local experts (a graph replay refreshes it)
         mark("layout_wait")
         grouped = torch.empty((rows_cap, hidden), dtype=x.dtype, device=dev)
         check(lib.pdx_ep_regroup(ctypes.c_void_p(peer.local(layer, "recv")), _ptr(ly.perm), _ptr(ly.offsets), EL,
@@ -410,6 +412,11 @@ class ExpertParallelStack:
                 self._run(t_count, mode)
             self._graphs[t_count] = g
         g.replay()
+
+    def local_active_experts(self):
+        """Per layer, how many of this rank's experts received rows in the
+        last step (synchronises the device)."""
+        return [int(layer.last_active[0].item()) for layer in self.layers]
 
     def release_graphs(self):
         """Drop the captured graphs (they hold NCCL work; release before
