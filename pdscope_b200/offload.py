@@ -38,6 +38,7 @@ live-consumer assertion, pdscope_runtime.py:376-377).
 from __future__ import annotations
 
 import ctypes
+import math
 from collections import OrderedDict
 from dataclasses import dataclass
 
@@ -217,16 +218,22 @@ class LedgerPlacer:
             self._complete(ticket, wait=False)
         self._retire()
 
-    def place_layer(self, step, layer, counts, predicted=()):
+    def place_layer(self, step, layer, counts, predicted=(), probabilities=None):
         """Slots for this layer's routed experts ``counts`` {expert: tokens} and
         prefetch copies of ``predicted`` (next-layer experts).  Returns
         (slot of each routed expert, {expert: copy event} of the routed experts
         whose transfers are still in flight, demand experts, prefetched
-        experts)."""
+        experts).  ``probabilities``: at a decode step (one token), the
+        token's full softmax over the layer's experts, handed to a
+        score-keeping ledger right after the demand is declared and before
+        any load -- the order the reference's DecodeScoreLayerCache requires
+        (update_decode_scores, expertbench/cache.py:903-929)."""
         self.close_layer()
         identity = self.identity = self.demand_of(self.request, step, layer)
         keys = {e: self.key_of(layer, e) for e in counts}
         self.ledger.on_demand(identity, {keys[e]: int(n) for e, n in counts.items()})
+        if probabilities is not None and step > 0 and hasattr(self.ledger, "update_decode_scores"):
+            self.ledger.update_decode_scores(identity, [float(v) for v in probabilities])
         slots, pending, demand = {}, {}, []
         for e in sorted(counts):
             key = keys[e]
@@ -305,11 +312,21 @@ class _CopyEngine:
 
 class TicketLedger:
     """A small ticket ledger with ExpertCache's call protocol, for hosts
-    without the reference package: LRU over cache slots of equal size,
-    demand-staging fallback when the cache has no evictable entry, byte
-    counters with the same names.  Keys are (layer, expert) tuples and demand
-    ids (request, step, layer) tuples; ``CapacityBlocked`` is raised as the
-    reference does when speculation finds no evictable room."""
+    without the reference package: cache slots of equal size, demand-staging
+    fallback when the cache has no evictable entry, byte counters with the
+    same names.  Keys are (layer, expert) tuples and demand ids (request,
+    step, layer) tuples; ``CapacityBlocked`` is raised as the reference does
+    when speculation finds no evictable room.
+
+    ``policy``: "lru" evicts the least recently demanded entry.  "score"
+    keeps the decode score of the reference's DecodeScoreLayerCache
+    (expertbench/cache.py:852-966): scores start at zero, and each decode
+    layer step's ``update_decode_scores`` sets, for every expert of the
+    layer, s = 0.5 s + 0.5 p if the expert is among the 2*top_k most probable
+    (ties to the lower id) and s = 0.5 s otherwise, in binary64; during decode
+    steps (step > 0) the victim is the evictable entry of least (score, key),
+    during prefill the least recently demanded one.  Unlike the reference's
+    class, the cache is one pool for all layers, not fixed per-layer quotas."""
 
     class CapacityBlocked(RuntimeError):
         pass
@@ -326,8 +343,15 @@ class TicketLedger:
         ticket: object
         state: str
 
-    def __init__(self, cache_slots, staging_slots, nbytes, initial_hotset=()):
+    def __init__(self, cache_slots, staging_slots, nbytes, initial_hotset=(), *, policy="lru", top_k=None):
+        if policy not in ("lru", "score"):
+            raise ValueError(f"unknown ledger policy {policy!r}")
+        if policy == "score" and not (isinstance(top_k, int) and top_k >= 1):
+            raise ValueError("the score policy needs the router's top_k")
         self.cache_slots, self.staging_slots, self.nbytes = cache_slots, staging_slots, nbytes
+        self.policy, self.top_k = policy, top_k
+        self._scores = {}            # layer -> [float] per expert
+        self._scored = None          # demand id whose scores are current
         self.initial_hotset = frozenset(initial_hotset)
         self._entries = {}           # key -> dict(ticket, ready, submitted, users)
         self._lru = OrderedDict()    # cache keys, least recent first
@@ -336,7 +360,8 @@ class TicketLedger:
         self._gen = 0
         self._active = None          # (identity, remaining keys)
         self._stats = dict(h2d_bytes_submitted=0, h2d_bytes_completed=0, gpu_completed_experts=0, evictions=0,
-                           demand_loads_submitted=0, prefetch_loads_submitted=0, initial_loads_submitted=0)
+                           demand_loads_submitted=0, prefetch_loads_submitted=0, initial_loads_submitted=0,
+                           score_updates=0)
 
     def stats(self):
         return dict(self._stats)
@@ -359,13 +384,48 @@ class TicketLedger:
         ent = self._entries[key]
         return ent["ready"] and not ent["users"] and not (self._active and key in self._active[1])
 
+    def update_decode_scores(self, identity, probabilities):
+        """The decode step's full softmax over the layer's experts (one token).
+        With the LRU policy the scores are kept too when ``top_k`` is given
+        (observed, not used: the reference's observe_only mode)."""
+        if self.top_k is None:
+            return
+        if self._active is None or self._active[0] != identity or identity[1] == 0:
+            raise RuntimeError("score update requires the current decode demand")
+        if self._scored == identity:
+            raise RuntimeError("the scores of this demand were updated already")
+        values = [float(v) for v in probabilities]
+        if any(not (0.0 <= v <= 1.0) for v in values) or abs(math.fsum(values) - 1.0) > 1e-5:
+            raise RuntimeError("score update requires the full softmax probabilities")
+        layer = identity[2]
+        prev = self._scores.get(layer) or [0.0] * len(values)
+        if len(prev) != len(values):
+            raise RuntimeError("probability vector length differs from the layer's expert count")
+        order = sorted(range(len(values)), key=lambda i: (-values[i], i))
+        chosen = set(order[:min(2 * self.top_k, len(values))])
+        self._scores[layer] = [0.5 * prev[i] + (0.5 * values[i] if i in chosen else 0.0)
+                               for i in range(len(values))]
+        self._scored = identity
+        self._stats["score_updates"] += 1
+
+    def score_values(self, layer):
+        return tuple(self._scores.get(layer, ()))
+
+    def _victim(self):
+        candidates = (k for k in self._lru if self._evictable(k))
+        if self.policy == "score" and self._active is not None and self._active[0][1] > 0:
+            scores = self._scores
+            return min(candidates, default=None,
+                       key=lambda k: (scores.get(k[0], ())[k[1]] if k[1] < len(scores.get(k[0], ())) else 0.0, k))
+        return next(candidates, None)
+
     def begin_load(self, key, *, origin="demand", admit=True):
         if key in self._entries:
             return self._entries[key]["ticket"]
         cached = sum(1 for k in self._entries if self._entries[k]["ticket"].pool == "cache")
         victim = None
         if cached >= self.cache_slots:
-            victim = next((k for k in self._lru if self._evictable(k)), None)
+            victim = self._victim()
         if cached < self.cache_slots or victim is not None:
             if victim is not None:
                 self._retired.append(self._entries.pop(victim)["ticket"])
@@ -567,6 +627,9 @@ class OffloadMoEStack:
         self.active_host = torch.zeros((self.max_launch, self.E + 1), **i32).pin_memory()
         self.active_dev = torch.zeros((self.max_launch, self.E + 1), **i32, device=self.dev)
         self.counts_host = torch.zeros((2, self.E), **i32).pin_memory()
+        # one decode token's logits, for a ledger that keeps decode scores
+        self.scores_wanted = hasattr(ledger, "update_decode_scores")
+        self.logits_host = torch.zeros((1, self.E), dtype=torch.bfloat16).pin_memory()
         self._bufs = {}
         self.placer.load_initial([key_of(l, e) for l, hs in enumerate(hot) for e in hs])
         torch.cuda.synchronize(self.dev)
@@ -660,13 +723,18 @@ class OffloadMoEStack:
         if predict:
             self._route_pack(x, self.gates[l + 1], nxt, b["counts"][1], ws)
         self.counts_host.copy_(b["counts"], non_blocking=True)
+        scores = self.placer is not None and self.scores_wanted and t == 1
+        if scores:
+            self.logits_host.copy_(cur["logits"], non_blocking=True)
         comp.synchronize()   # the per-layer grouping sync
         counts = self.counts_host.numpy()
         needed = np.nonzero(counts[0])[0].tolist()
         self.stats.layers += 1
         self.stats.expert_uses += len(needed)
         if self.placer is not None:
-            return self._forward_layer_ledger(l, x, out, residual, norm, counts, needed, predict, b, comp)
+            # the decode token's full softmax (the native probabilities a score ledger keeps)
+            probs = torch.softmax(self.logits_host[0].double(), 0).tolist() if scores else None
+            return self._forward_layer_ledger(l, x, out, residual, norm, counts, needed, predict, b, comp, probs)
 
         pinned, ready, waits, demand = set(), [], [], []
         table = self.table_host[l].numpy()
@@ -746,12 +814,12 @@ class OffloadMoEStack:
             self.ring.slots[idx].last_use = done
         return out
 
-    def _forward_layer_ledger(self, l, x, out, residual, norm, counts, needed, predict, b, comp):
+    def _forward_layer_ledger(self, l, x, out, residual, norm, counts, needed, predict, b, comp, probs=None):
         """forward_layer's placement and launches when a ledger keeps residency."""
         t = x.shape[0]
         cur = {e: int(counts[0][e]) for e in needed}
         predicted = np.nonzero(counts[1])[0].tolist() if predict else []
-        slots, pending, demand, issued = self.placer.place_layer(self._step, l, cur, predicted)
+        slots, pending, demand, issued = self.placer.place_layer(self._step, l, cur, predicted, probs)
         self.stats.demand_copies += len(demand)
         self.stats.prefetch_copies += len(issued)
         self.stats.h2d_bytes += (len(demand) + len(issued)) * self.per * 2

@@ -199,3 +199,37 @@ def test_offload_through_a_ticket_ledger(stacks):
     assert s["h2d_bytes_submitted"] == s["h2d_bytes_completed"] == copies * nbytes
     assert s["evictions"] > 0 and st.stats.prefetch_copies > 0
     assert s["gpu_completed_experts"] == st.stats.expert_uses
+
+
+def test_offload_through_a_decode_score_ledger(stacks):
+    """The score-keeping ledger (the reference DecodeScoreLayerCache's decode
+    rule: EMA of the token's top-2k softmax probabilities, least score
+    evicted at decode steps): each one-token step hands the full softmax of
+    every layer to the ledger before any load; outputs stay equal to the
+    all-resident stack, the byte closure holds, and every decode layer step
+    updated the scores once."""
+    from pdscope_b200.offload import OffloadMoEStack, TicketLedger, zipf_hot_sets
+    from pdscope_b200.stack import activations
+    res, off = stacks
+    hot = zipf_hot_sets(res.gates, 2)
+    nbytes = 3 * H * I * 2
+    ledger = TicketLedger(cache_slots=12, staging_slots=4, nbytes=nbytes, policy="score", top_k=K,
+                          initial_hotset=[(l, e) for l, hs in enumerate(hot) for e in hs])
+    st = OffloadMoEStack(res.gates, off.host, hot, hidden=H, inter=I, cache_slots=0, top_k=K, chunk=3,
+                         ledger=ledger)
+    steps = (10, 1, 1, 1, 1, 1, 1)
+    for step, t_count in enumerate(steps):
+        x = activations(t_count, H, seed=1900 + step, zipf=True)
+        want = _resident(res, x)
+        got = st.forward(x).clone()
+        torch.cuda.synchronize()
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16)), (step, t_count)
+    st.finish()
+    s = ledger.stats()
+    copies = st.stats.demand_copies + st.stats.prefetch_copies + len(ledger.initial_hotset)
+    assert s["h2d_bytes_submitted"] == s["h2d_bytes_completed"] == copies * nbytes
+    assert s["score_updates"] == L * (len(steps) - 1)
+    assert s["evictions"] > 0
+    for l in range(L):
+        sc = ledger.score_values(l)
+        assert len(sc) == E and all(0.0 <= v <= 1.0 for v in sc) and sum(sc) > 0.0

@@ -121,3 +121,101 @@ def test_reference_expert_cache_drives_the_placement():
     assert st.get("evictions", 0) > 0
     assert st.get("prefetch_loads_submitted", 0) + placer.prefetch_skipped > 0
     assert ledger.active_demand is None
+
+
+def _run_scored(ledger, key_of, demand_of, cache_slots, staging_slots, hot, steps=8):
+    """Prefill (6 tokens) then one-token decode steps whose routing comes from
+    a seeded softmax; every decode layer step hands the full softmax to the
+    ledger through LedgerPlacer.place_layer(..., probabilities)."""
+    from pdscope_b200.offload import LedgerPlacer
+    dev = FakeDevice(cache_slots + staging_slots)
+    placer = LedgerPlacer(ledger, key_of=key_of, demand_of=demand_of, cache_slots=cache_slots, device=dev)
+    placer.load_initial([key_of(l, e) for l in range(L) for e in hot[l]])
+    rng = np.random.default_rng(7)
+    history = {l: [] for l in range(L)}
+    for step in range(steps):
+        tokens = 1 if step else 6
+        for l in range(L):
+            logits = rng.standard_normal((tokens, E))
+            p = np.exp(logits - logits.max(1, keepdims=True))
+            p /= p.sum(1, keepdims=True)
+            sel = np.argsort(-p, axis=1, kind="stable")[:, :K]
+            ids, n = np.unique(sel, return_counts=True)
+            counts = {int(e): int(c) for e, c in zip(ids, n)}
+            probs = p[0].tolist() if step else None
+            if probs is not None:
+                history[l].append(p[0])
+            slots, _, _, _ = placer.place_layer(step, l, counts, (), probs)
+            for e, s in slots.items():
+                assert dev.memory[s] == key_of(l, e), (step, l, e)
+            done = Event()
+            dev.protected = set(slots.values())
+            placer.begin_compute(l, counts, done)
+            done.finished = True
+            dev.protected = set()
+    placer.drain()
+    return dev, history
+
+
+def _expected_scores(history):
+    """Decode score after each update: s = 0.5 s + 0.5 p on the 2k most
+    probable experts (ties to the lower id), s = 0.5 s elsewhere."""
+    s = np.zeros(E)
+    for p in history:
+        chosen = np.zeros(E, bool)
+        chosen[sorted(range(E), key=lambda i: (-p[i], i))[:2 * K]] = True
+        s = np.array([0.5 * s[i] + (0.5 * p[i] if chosen[i] else 0.0) for i in range(E)])
+    return s
+
+
+def test_score_ledger_keeps_the_decode_score():
+    from pdscope_b200.offload import TicketLedger
+    hot = [[0, 1, 2] for _ in range(L)]
+    ledger = TicketLedger(cache_slots=18, staging_slots=2, nbytes=NB, policy="score", top_k=K)
+    dev, history = _run_scored(ledger, lambda l, e: (l, e), lambda r, s, l: (r, s, l), 18, 2, hot)
+    st = ledger.stats()
+    assert st["h2d_bytes_submitted"] == st["h2d_bytes_completed"] == dev.copies * NB
+    assert st["score_updates"] == 7 * L and st["evictions"] > 0
+    for l in range(L):
+        assert ledger.score_values(l) == tuple(_expected_scores(history[l]))
+
+
+def test_score_ledger_evicts_the_least_scored_entry():
+    """At a decode step the victim is the evictable entry of least score."""
+    from pdscope_b200.offload import TicketLedger
+    led = TicketLedger(cache_slots=2, staging_slots=1, nbytes=NB, policy="score", top_k=1)
+    for key in ((0, 0), (0, 1)):
+        t = led.begin_load(key, origin="initial")
+        led.submit(t)
+        led.complete_load(t)
+    ident = ("r", 1, 0)
+    led.on_demand(ident, {(0, 2): 1})
+    led.update_decode_scores(ident, [0.1, 0.6, 0.3])   # expert 0 stays out of the top 2k = 2
+    t = led.begin_load((0, 2))
+    assert t.pool == "cache" and led.take_retired()[0].key == (0, 0)
+    assert led.score_values(0) == (0.0, 0.3, 0.15)
+
+
+def test_reference_decode_score_cache_drives_the_placement():
+    """The reference's own DecodeScoreLayerCache (cache.py:852-966) through
+    the placer: same scores as the package's score ledger on the same
+    routing, byte closure, every routed expert in its own slot."""
+    if not (REF / "expertbench" / "cache.py").exists():
+        pytest.skip("reference source tree not present")
+    sys.path.insert(0, str(REF))
+    try:
+        from expertbench.cache import DecodeScoreLayerCache, DemandID, ExpertKey
+    finally:
+        sys.path.remove(str(REF))
+    hot = [[0, 1, 2] for _ in range(L)]
+    keys = {ExpertKey(l, e, "bf16"): NB for l in range(L) for e in range(E)}
+    initial = [ExpertKey(l, e, "bf16") for l in range(L) for e in hot[l]]
+    # per-layer quotas fixed by the initial set; one grouped launch reads a
+    # layer's routed experts together, so staging holds a whole prefill miss set
+    ledger = DecodeScoreLayerCache(keys, len(initial) * NB, [NB] * E, top_k=K, initial_hotset=initial)
+    dev, history = _run_scored(ledger, lambda l, e: ExpertKey(l, e, "bf16"), DemandID, len(initial), E, hot)
+    st = ledger.stats()
+    assert st["h2d_bytes_submitted"] == st["h2d_bytes_completed"] == dev.copies * NB
+    assert st["score_updates"] == 7 * L
+    for l in range(L):
+        assert ledger.score_values(l) == tuple(_expected_scores(history[l]))
