@@ -150,12 +150,13 @@ __device__ __forceinline__ float block_sum_ln(float v, float* red) {
 
 // Normalise the row held in v (this thread's chunks c = (tid + 256 j) * 8)
 // and store it: population variance, FP32 statistics in a fixed order.
-__device__ __forceinline__ void layernorm_store(float (&v)[kLnMaxPerThread], float sum, int H, float eps,
-                                                uint16_t* out_row, float* red) {
+template <int VPT>
+__device__ __forceinline__ void layernorm_store(float (&v)[VPT], float sum, int H, float eps, uint16_t* out_row,
+                                                float* red) {
     const float mean = block_sum_ln(sum, red) / static_cast<float>(H);
     float q = 0.f;
 #pragma unroll
-    for (int j = 0; j < kLnMaxPerThread / 8; ++j) {
+    for (int j = 0; j < VPT / 8; ++j) {
         const int c = (static_cast<int>(threadIdx.x) + j * kLnThreads) * 8;
         if (c < H) {
 #pragma unroll
@@ -168,7 +169,7 @@ __device__ __forceinline__ void layernorm_store(float (&v)[kLnMaxPerThread], flo
     const float var = block_sum_ln(q, red) / static_cast<float>(H);
     const float inv = 1.0f / sqrtf(var + eps);
 #pragma unroll
-    for (int j = 0; j < kLnMaxPerThread / 8; ++j) {
+    for (int j = 0; j < VPT / 8; ++j) {
         const int c = (static_cast<int>(threadIdx.x) + j * kLnThreads) * 8;
         if (c < H) {
             float o[8];
@@ -203,13 +204,18 @@ __global__ void __launch_bounds__(kLnThreads) k_residual_layernorm(const uint16_
             }
         }
     }
-    layernorm_store(v, s, H, eps, out + static_cast<size_t>(t) * H, red);
+    layernorm_store<kLnMaxPerThread>(v, s, H, eps, out + static_cast<size_t>(t) * H, red);
 }
 
 // Combine and next-layer norm in one pass, bit-identical to k_combine (no
 // residual) followed by k_residual_layernorm:
 //   out[t] = bf16( layer_norm( bf16(sum_s bf16(y_s * w_s)) + residual[t] ) )
 // residual must not alias y (the expert rows of other tokens); it may alias out.
+// VPT = values per thread (8 per 2048 of H): only the registers the row needs,
+// so more tokens are in flight per SM (each token's chain is load -> two block
+// reductions -> store; at prefill sizes the kernel is bound by how many of
+// those chains overlap).
+template <int VPT>
 __global__ void __launch_bounds__(kCombineThreads) k_combine_norm(const uint16_t* __restrict__ y,
                                                                   const uint16_t* __restrict__ weights,
                                                                   const int32_t* __restrict__ inverse, int T, int k,
@@ -223,10 +229,10 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine_norm(const uint16_t
     __shared__ float s_w[32];
     __shared__ float red[32];
     combine_slots(weights, inverse, t, k, y_rows, s_row, s_w);
-    float v[kLnMaxPerThread];
+    float v[VPT];
     float sum = 0.f;
 #pragma unroll
-    for (int j = 0; j < kLnMaxPerThread / 8; ++j) {
+    for (int j = 0; j < VPT / 8; ++j) {
         const int c = (static_cast<int>(threadIdx.x) + j * kLnThreads) * 8;
         if (c < H) {
             float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -240,7 +246,7 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine_norm(const uint16_t
             }
         }
     }
-    layernorm_store(v, sum, H, eps, out + static_cast<size_t>(t) * H, red);
+    layernorm_store<VPT>(v, sum, H, eps, out + static_cast<size_t>(t) * H, red);
 }
 
 }  // namespace pdx

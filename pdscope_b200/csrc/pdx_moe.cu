@@ -101,6 +101,16 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
         if (_e != cudaSuccess) return fail(PDX_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(_e)); \
     } while (0)
 
+// k_combine_norm with the values-per-thread instance the row length needs.
+template <typename... Args>
+cudaError_t launch_combine_norm(int64_t H, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
+    if (H <= 8 * kCombineThreads)
+        return launch_pdl(k_combine_norm<8>, grid, block, smem, stream, std::forward<Args>(args)...);
+    if (H <= 16 * kCombineThreads)
+        return launch_pdl(k_combine_norm<16>, grid, block, smem, stream, std::forward<Args>(args)...);
+    return launch_pdl(k_combine_norm<kLnMaxPerThread>, grid, block, smem, stream, std::forward<Args>(args)...);
+}
+
 constexpr size_t kAlign = 256;
 // SM count the launch plans assume (B200), so that a workspace query and the
 // launch it sizes always agree; the plans only shape the work, not results.
@@ -1010,7 +1020,7 @@ int pdx_combine_layernorm(const void* y, const void* weights, const int32_t* inv
     int st = check_norm_shape(H);
     if (st) return st;
     if (!(eps > 0.f)) return fail(PDX_ERR_INVALID, "eps must be positive");
-    PDX_PDL_TRY(launch_pdl(k_combine_norm, dim3(static_cast<unsigned>(T)), dim3(kCombineThreads), 0, stream,
+    PDX_PDL_TRY(launch_combine_norm(H, dim3(static_cast<unsigned>(T)), dim3(kCombineThreads), 0, stream,
                            static_cast<const uint16_t*>(y), static_cast<const uint16_t*>(weights), inverse,
                            static_cast<int>(T), static_cast<int>(top_k), static_cast<int>(H),
                            static_cast<int>(T * top_k), static_cast<const uint16_t*>(residual), eps,
@@ -1027,7 +1037,7 @@ int pdx_ep_combine_layernorm(const void* y, int64_t y_rows, const void* weights,
     int st = check_norm_shape(H);
     if (st) return st;
     if (!(eps > 0.f)) return fail(PDX_ERR_INVALID, "eps must be positive");
-    PDX_PDL_TRY(launch_pdl(k_combine_norm, dim3(static_cast<unsigned>(T)), dim3(kCombineThreads), 0, stream,
+    PDX_PDL_TRY(launch_combine_norm(H, dim3(static_cast<unsigned>(T)), dim3(kCombineThreads), 0, stream,
                            static_cast<const uint16_t*>(y), static_cast<const uint16_t*>(weights), inv_ep,
                            static_cast<int>(T), static_cast<int>(top_k), static_cast<int>(H),
                            static_cast<int>(y_rows), static_cast<const uint16_t*>(residual), eps,
@@ -1125,7 +1135,7 @@ int pdx_moe_layer(const void* x, const void* gate, int64_t T, int64_t H, int64_t
         st = launch_ffn(x, T, pb.o.tokens, pb.o.offsets, pb.o.active, E, N, weights, H, I, y, m, c, stream);
     if (st) return st;
     if (out_norm)
-        PDX_PDL_TRY(launch_pdl(k_combine_norm, dim3(static_cast<unsigned>(T)), dim3(kCombineThreads), 0, stream,
+        PDX_PDL_TRY(launch_combine_norm(H, dim3(static_cast<unsigned>(T)), dim3(kCombineThreads), 0, stream,
                                static_cast<const uint16_t*>(y), static_cast<const uint16_t*>(rb.weights),
                                static_cast<const int32_t*>(pb.o.inverse), static_cast<int>(T),
                                static_cast<int>(top_k), static_cast<int>(H), static_cast<int>(N),
