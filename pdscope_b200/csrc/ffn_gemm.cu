@@ -10,7 +10,8 @@
 //   warp 0      TMA producer: A tile [128 x 64] + B tile [256 x 64] per stage
 //   warp 1      MMA issuer: tcgen05.mma.cta_group::1.kind::f16, M=128 N=256
 //               K=16, FP32 accumulators in TMEM (two 256-column buffers)
-//   warps 2..9  epilogue: tcgen05.ld 32x32b, BF16 rounding, global stores;
+//   warps 2..9  epilogue: tcgen05.ld 32x32b, BF16 rounding, row segments
+//               staged through shared memory into 64-byte global stores;
 //               two warps per TMEM lane quadrant, each on half of the columns
 // GEMM1 (SwiGLU): B = [128 gate rows ; 128 up rows] of the expert, epilogue
 //   h = bf16(bf16(silu(bf16(g))) * bf16(u)) -> h[rows, I].
@@ -38,8 +39,10 @@ constexpr uint32_t kTileBBytes = kGemmBN * kGemmBK * 2;  // 32 KiB
 constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
 constexpr uint32_t kTmemCols = 512;  // two 256-column FP32 accumulators
 constexpr int kMaxActive = 1024;
+constexpr uint32_t kEpiStageBytes = 32 * 64;  // one epilogue warp's 32 rows x 32 BF16 columns
 constexpr size_t kGemmSmemBytes = 1024 /*alignment slack*/ + kGemmStages * kStageBytes + 256 /*barriers*/ +
-                                  4 * (kMaxActive + 1) * 4 /*tile prefix, segment start, rows, slot*/;
+                                  4 * (kMaxActive + 1) * 4 /*tile prefix, segment start, rows, slot*/ +
+                                  kGemmEpiWarps * kEpiStageBytes /*epilogue staging*/;
 
 struct GemmArgs {
     const int32_t* offsets;
@@ -187,6 +190,89 @@ __device__ __forceinline__ void epilogue_cols(int swiglu, uint32_t taddr, uint16
     }
 }
 
+// One 32 x 32 BF16 slab of output through this warp's shared-memory staging
+// buffer: lane r holds row r's 32 columns (packed, 16 words) and writes them
+// as four 16-byte chunks (chunk q of row r at r*64 + (q ^ ((r >> 1) & 3))*16,
+// conflict-free); after the warp sync, lane l stores chunk l & 3 of rows
+// (l >> 2) + 8i, i = 0..3, so every four lanes write one 64-byte row segment.
+// Rows >= n_valid (past the expert's segment) are not stored.
+__device__ __forceinline__ void store_slab(const uint32_t (&packed)[16], unsigned char* sbuf, uint16_t* out0,
+                                           int64_t ld, int col, int n_valid) {
+    const uint32_t lane = lane_id();
+    const uint32_t base = smem_u32(sbuf);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint32_t a = base + lane * 64u + ((static_cast<uint32_t>(q) ^ ((lane >> 1) & 3u)) * 16u);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(packed[4 * q]), "r"(packed[4 * q + 1]),
+                     "r"(packed[4 * q + 2]), "r"(packed[4 * q + 3])
+                     : "memory");
+    }
+    __syncwarp();
+    const uint32_t cc = lane & 3u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t r = (lane >> 2) + 8u * i;
+        const uint32_t a = base + r * 64u + ((cc ^ ((r >> 1) & 3u)) * 16u);
+        uint4 v;
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+        if (static_cast<int>(r) < n_valid)
+            *reinterpret_cast<uint4*>(out0 + static_cast<int64_t>(r) * ld + col + cc * 8) = v;
+    }
+    __syncwarp();
+}
+
+// Columns [c0, c0 + nc) of this warp's 32 accumulator rows (TMEM lanes of its
+// quadrant) -> BF16 output rows out0 + r*ld, through the staging buffer so
+// the global stores are whole 64-byte row segments (the row-per-lane form
+// writes 16 bytes to 32 different rows per store instruction).
+// swiglu: accumulator columns [0,128) hold gate, [128,256) up.
+__device__ __forceinline__ void epilogue_cols_staged(int swiglu, uint32_t taddr, uint16_t* out0, int64_t ld,
+                                                     int n_valid, int c0, int nc, unsigned char* sbuf) {
+    if (swiglu) {
+#pragma unroll 1
+        for (int c = c0; c < c0 + nc; c += 32) {
+            uint32_t g[32], u[32];
+            tmem_ld16(taddr + c, g);
+            tmem_ld16(taddr + c + 16, g + 16);
+            tmem_ld16(taddr + kGemmBN / 2 + c, u);
+            tmem_ld16(taddr + kGemmBN / 2 + c + 16, u + 16);
+            tmem_wait_pin(g);
+            tmem_wait_pin(u);
+            uint32_t packed[16];
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+                float hv[2];
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const float gb = round_bf16(__uint_as_float(g[i + j]));
+                    const float ub = round_bf16(__uint_as_float(u[i + j]));
+                    const float sv = round_bf16(__fdiv_rn(gb, 1.0f + expf(-gb)));
+                    hv[j] = sv * ub;
+                }
+                packed[i / 2] = static_cast<uint32_t>(f2bits(hv[0])) | (static_cast<uint32_t>(f2bits(hv[1])) << 16);
+            }
+            store_slab(packed, sbuf, out0, ld, c, n_valid);
+        }
+    } else {
+#pragma unroll 1
+        for (int c = c0; c < c0 + nc; c += 64) {
+            uint32_t v[64];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) tmem_ld16(taddr + c + 16 * i, v + 16 * i);
+            tmem_wait_pin(v);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint32_t packed[16];
+#pragma unroll
+                for (int i = 0; i < 32; i += 2)
+                    packed[i / 2] = static_cast<uint32_t>(f2bits(__uint_as_float(v[32 * h + i]))) |
+                                    (static_cast<uint32_t>(f2bits(__uint_as_float(v[32 * h + i + 1]))) << 16);
+                store_slab(packed, sbuf, out0, ld, c + 32 * h, n_valid);
+            }
+        }
+    }
+}
+
 // Whole accumulator row: 128 SwiGLU output columns or 256 down columns.
 __device__ __forceinline__ void epilogue_row(int swiglu, uint32_t taddr, uint16_t* orow, bool valid) {
     epilogue_cols(swiglu, taddr, orow, valid, 0, swiglu ? kGemmBN / 2 : kGemmBN);
@@ -211,6 +297,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int* t_seg0 = prefix + (kMaxActive + 1);
     int* t_rows = t_seg0 + (kMaxActive + 1);
     int* t_slot = t_rows + (kMaxActive + 1);
+    unsigned char* epi_stage = reinterpret_cast<unsigned char*>(t_slot + (kMaxActive + 1));  // [8][32 x 64 B]
 
     const int warp = static_cast<int>(threadIdx.x >> 5);
     const uint32_t lane = lane_id();
@@ -320,7 +407,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     } else {
         // ---------------- epilogue (warps 2..9) ----------------
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
-        const int row_in_tile = q * 32 + static_cast<int>(lane);
         const int half = (warp - 2) >> 2;  // which half of the tile's columns
         const int half_cols = (args.swiglu ? kGemmBN / 2 : kGemmBN) / 2;
         int lt = 0;
@@ -332,11 +418,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const TileInfo ti = decode_tile(tile, prefix, n_active, n_tiles);
             const int seg0 = t_seg0[ti.a];
             const int n_e = t_rows[ti.a];
-            const int r = ti.m * kGemmBM + row_in_tile;
-            const bool valid = r < n_e;
-            uint16_t* orow = args.out + static_cast<int64_t>(seg0 + r) * args.out_ld + ti.n * out_cols_per_tile;
+            const int r0 = ti.m * kGemmBM + q * 32;   // first row of this warp's lane quadrant
+            uint16_t* out0 = args.out + static_cast<int64_t>(seg0 + r0) * args.out_ld + ti.n * out_cols_per_tile;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * kGemmBN);
-            epilogue_cols(args.swiglu, taddr, orow, valid, half * half_cols, half_cols);
+            epilogue_cols_staged(args.swiglu, taddr, out0, args.out_ld, min(32, n_e - r0), half * half_cols, half_cols,
+                                 epi_stage + (warp - 2) * kEpiStageBytes);
             tc_fence_before();
             mbar_arrive(&tmem_empty[b]);
         }
