@@ -100,23 +100,41 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(const uint16_t* __r
 }
 
 // out[p] = x[tokens[p]]  (inputs[flat_tokens], pdscope_runtime.py:333-336).
-// CTA 0 also clears `zero_words` words (the split-K tickets of the FFN kernels
-// that follow), so no memset node separates the kernels of the chain.
-__global__ void __launch_bounds__(kCombineThreads) k_gather_rows(const uint16_t* __restrict__ x,
-                                                                 const int32_t* __restrict__ tokens, int rows,
-                                                                 int H, uint16_t* __restrict__ out,
-                                                                 unsigned int* __restrict__ zero_ptr,
-                                                                 int zero_words) {
+// One warp per packed row over a grid sized to the SMs (a CTA per row made
+// the block scheduler the limit at prefill sizes: 99,600 rows took 127 us);
+// each lane keeps up to 8 16-byte chunks of its row in flight.  CTA 0 also
+// clears `zero_words` words (the split-K tickets of the FFN kernels that
+// follow), so no memset node separates the kernels of the chain.
+constexpr int kGatherWarps = 8;
+__global__ void __launch_bounds__(kGatherWarps * 32) k_gather_rows(const uint16_t* __restrict__ x,
+                                                                   const int32_t* __restrict__ tokens, int rows,
+                                                                   int H, uint16_t* __restrict__ out,
+                                                                   unsigned int* __restrict__ zero_ptr,
+                                                                   int zero_words) {
     griddep_wait();
     griddep_launch();
     if (blockIdx.x == 0)
         for (int i = threadIdx.x; i < zero_words; i += blockDim.x) zero_ptr[i] = 0u;
-    const int p = static_cast<int>(blockIdx.x);
-    if (p >= rows) return;
-    const size_t src = static_cast<size_t>(tokens[p]) * H;
-    for (int c = static_cast<int>(threadIdx.x) * 8; c < H; c += blockDim.x * 8)
-        *reinterpret_cast<uint4*>(out + static_cast<size_t>(p) * H + c) =
-            __ldg(reinterpret_cast<const uint4*>(x + src + c));
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    const int chunks = H / 8;   // 16-byte chunks per row
+    for (int p = static_cast<int>(blockIdx.x) * kGatherWarps + static_cast<int>(threadIdx.x >> 5); p < rows;
+         p += static_cast<int>(gridDim.x) * kGatherWarps) {
+        const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(__ldg(tokens + p)) * H);
+        uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(p) * H);
+        for (int c0 = 0; c0 < chunks; c0 += 8 * 32) {
+            uint4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int c = c0 + j * 32 + lane;
+                if (c < chunks) v[j] = __ldg(src + c);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int c = c0 + j * 32 + lane;
+                if (c < chunks) dst[c] = v[j];
+            }
+        }
+    }
 }
 
 // Clears n words (the split-K tickets) when the FFN reads rows already in

@@ -118,6 +118,12 @@ constexpr int kPlanSMs = 148;
 constexpr int kMaxExperts = 1024;
 inline size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
+// Row gather grid: one warp per row, at most 8 CTAs per SM resident at once.
+inline dim3 gather_grid(int64_t rows) {
+    return dim3(static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((rows + kGatherWarps - 1) / kGatherWarps,
+                                                                             8 * kPlanSMs))));
+}
+
 // Bump allocator over the caller's workspace.
 struct Carver {
     char* base;
@@ -664,7 +670,7 @@ int launch_decode_ffn(const void* x, int64_t T, const int32_t* tokens, const int
     const int zero_words = zeroed ? 0 : static_cast<int>(p.zero_words);
     const void* xb = x;   // phase-1 B operand
     if (!p.direct && tokens) {
-        PDX_PDL_TRY(launch_pdl(k_gather_rows, dim3(static_cast<unsigned>(rows)), dim3(kCombineThreads), 0, stream,
+        PDX_PDL_TRY(launch_pdl(k_gather_rows, gather_grid(rows), dim3(kGatherWarps * 32), 0, stream,
                                static_cast<const uint16_t*>(x), tokens, static_cast<int>(rows), static_cast<int>(H),
                                b.xp, b.counters, zero_words));
         xb = b.xp;
@@ -764,7 +770,7 @@ int launch_ffn(const void* x, int64_t T, const int32_t* tokens, const int32_t* o
     // with tokens == NULL the rows of x are already in packed order.
     const int zero_words = mode == PDX_FFN_GEMV ? static_cast<int>(2 * plan.ticket_bytes / 4) : 0;
     if (tokens) {
-        PDX_PDL_TRY(launch_pdl(k_gather_rows, dim3(static_cast<unsigned>(rows)), dim3(kCombineThreads), 0, stream,
+        PDX_PDL_TRY(launch_pdl(k_gather_rows, gather_grid(rows), dim3(kGatherWarps * 32), 0, stream,
                                static_cast<const uint16_t*>(x), tokens, static_cast<int>(rows), static_cast<int>(H),
                                xp, tickets, zero_words));
     } else {
@@ -952,7 +958,7 @@ int pdx_gather_rows(const void* x, const int32_t* tokens, int64_t rows, int64_t 
     if (!x || !tokens || !out || rows < 0) return fail(PDX_ERR_INVALID, "null gather argument");
     if (H < 8 || H % 8) return fail(PDX_ERR_UNSUPPORTED, "H must be a positive multiple of 8");
     if (rows == 0) return ok();
-    k_gather_rows<<<static_cast<unsigned>(rows), kCombineThreads, 0, stream>>>(
+    k_gather_rows<<<gather_grid(rows), kGatherWarps * 32, 0, stream>>>(
         static_cast<const uint16_t*>(x), tokens, static_cast<int>(rows), static_cast<int>(H),
         static_cast<uint16_t*>(out), nullptr, 0);
     PDX_LAUNCHED();
