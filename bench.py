@@ -384,6 +384,40 @@ def main():
                     peak_source=pk["source"], frac_of_8000_nominal=achieved / 8000.0, traffic=traffic,
                     bytes_per_launch=bytes_per_launch, us_per_launch=per_launch_s * 1e6)
 
+    # ---- config 1: one layer (pdx_moe_layer, one C-ABI call) at T = 1 and 512 ----------
+    # (timed before the prefill section: the HBM-bound layer then runs at the clocks
+    # the decode sections see, not in the power-capped aftermath of the prefill GEMMs)
+    from pdscope_b200.runtime import LayerOutputs, ResidentMoELayer
+    layer0 = ResidentMoELayer(stack.gates[0], stack.slabs[0])
+    config1 = {}
+    for t_count, reps in ((1, 200), (512, 50)):
+        x1 = activations(t_count, CFG["hidden"], device=dev, seed=300 + t_count)
+        outs = layer0.forward(x1)
+        # ten pdx_moe_layer calls per CUDA graph, as a serving loop replays them
+        # (the layer's 1.2 GB of expert weights exceed L2, so no call hits in it)
+        torch.cuda.synchronize(dev)
+        g1 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g1):
+            for _ in range(10):
+                layer0.forward(x1, outputs=outs)
+        ms1 = timed(g1.replay, reps // 10, W) / (reps // 10 * 10)
+        del g1
+        u = int((outs.counts > 0).sum().item())
+        layer_bytes = u * EXPERT_BYTES + CFG["experts"] * CFG["hidden"] * 2 + 2 * t_count * CFG["hidden"] * 2
+        config1[str(t_count)] = dict(us_per_layer=ms1 * 1e3, active_experts=u,
+                                     hbm_gbs=layer_bytes / (ms1 / 1e3) / 1e9,
+                                     hbm_frac=layer_bytes / (ms1 / 1e3) / 1e9 / pk["hbm_gbs"],
+                                     tflops=t_count * CFG["top_k"] * FLOPS_PER_ROW / (ms1 / 1e3) / 1e12)
+    if world == 1 and not args.no_cpu:
+        from oracle import cpu_path
+        cores = args.cpu_threads or usable_cores()
+        sample = [cpu_path.make_layer(CFG["hidden"], CFG["experts"], CFG["inter"], seed=100)]
+        for t_count in (1, 512):
+            per_layer, _ = cpu_path.time_layers(sample, t_count, CFG["hidden"], cores, repeats=1)
+            config1[str(t_count)]["cpu_reference_us_per_layer"] = per_layer * 1e6
+            config1[str(t_count)]["cpu_cores"] = cores
+    del layer0
+
     # ---- prefill (config 3): ragged 8-sequence batch, Zipf router skew -----------------
     prefill = None
     if not args.no_prefill:
@@ -427,38 +461,6 @@ def main():
                                      flops_per_launch=flops_launch, us_per_launch=per_launch_p * 1e6))
         pstack.release_graphs()
         del pstack
-
-    # ---- config 1: one layer (pdx_moe_layer, one C-ABI call) at T = 1 and 512 ----------
-    from pdscope_b200.runtime import LayerOutputs, ResidentMoELayer
-    layer0 = ResidentMoELayer(stack.gates[0], stack.slabs[0])
-    config1 = {}
-    for t_count, reps in ((1, 200), (512, 50)):
-        x1 = activations(t_count, CFG["hidden"], device=dev, seed=300 + t_count)
-        outs = layer0.forward(x1)
-        # ten pdx_moe_layer calls per CUDA graph, as a serving loop replays them
-        # (the layer's 1.2 GB of expert weights exceed L2, so no call hits in it)
-        torch.cuda.synchronize(dev)
-        g1 = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g1):
-            for _ in range(10):
-                layer0.forward(x1, outputs=outs)
-        ms1 = timed(g1.replay, reps // 10, W) / (reps // 10 * 10)
-        del g1
-        u = int((outs.counts > 0).sum().item())
-        layer_bytes = u * EXPERT_BYTES + CFG["experts"] * CFG["hidden"] * 2 + 2 * t_count * CFG["hidden"] * 2
-        config1[str(t_count)] = dict(us_per_layer=ms1 * 1e3, active_experts=u,
-                                     hbm_gbs=layer_bytes / (ms1 / 1e3) / 1e9,
-                                     hbm_frac=layer_bytes / (ms1 / 1e3) / 1e9 / pk["hbm_gbs"],
-                                     tflops=t_count * CFG["top_k"] * FLOPS_PER_ROW / (ms1 / 1e3) / 1e12)
-    if world == 1 and not args.no_cpu:
-        from oracle import cpu_path
-        cores = args.cpu_threads or usable_cores()
-        sample = [cpu_path.make_layer(CFG["hidden"], CFG["experts"], CFG["inter"], seed=100)]
-        for t_count in (1, 512):
-            per_layer, _ = cpu_path.time_layers(sample, t_count, CFG["hidden"], cores, repeats=1)
-            config1[str(t_count)]["cpu_reference_us_per_layer"] = per_layer * 1e6
-            config1[str(t_count)]["cpu_cores"] = cores
-    del layer0
 
     # ---- e2e: public API with host buffers (pinned H2D in, D2H out) --------------------
     t_count = headline_t
