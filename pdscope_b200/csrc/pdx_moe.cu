@@ -437,9 +437,12 @@ int launch_route(const void* x, const void* gate, int64_t T, int64_t H, int64_t 
         return PDX_OK;
     }
     if (fused_pack) {
-        const size_t smem = topk_pack_smem_bytes(E, T * k);
+        // up to 32 assignments one warp packs, so the CTA needs only a warp per token
+        const bool small = T * k <= 32;
+        const size_t smem = small ? (2 * E + 1) * sizeof(int) : topk_pack_smem_bytes(E, T * k);
+        const unsigned threads = small ? static_cast<unsigned>(32 * T) : static_cast<unsigned>(kTopkPackThreads);
         PDX_PDL_TRY(with_epl(E, [&](auto epl) {
-            return launch_pdl(k_topk_pack<decltype(epl)::value>, dim3(1), dim3(kTopkPackThreads), smem, stream,
+            return launch_pdl(k_topk_pack<decltype(epl)::value>, dim3(1), dim3(threads), smem, stream,
                               static_cast<const uint16_t*>(b.logits), Ti, Ei, k, normalize, b.selected, b.weights,
                               *fused_pack, zero_ptr, static_cast<int>(zero_words));
         }));

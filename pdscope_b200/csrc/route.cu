@@ -203,6 +203,10 @@ __global__ void __launch_bounds__(kTopkPackThreads) k_topk_pack(const uint16_t* 
     extern __shared__ int smem_tp[];
     int* hist = smem_tp;
     int* excl = hist + E;
+    if (T * k <= 32) {   // a handful of assignments: one warp packs them
+        if (warp == 0) warp_pack_small(selected, weights, T, k, E, hist, excl, pack);
+        return;
+    }
     int* warp_hist = excl + E + 1;
     block_pack_all(selected, weights, T, k, E, hist, excl, warp_hist, pack);
 }

@@ -389,6 +389,46 @@ __device__ __forceinline__ void block_pack_all(const int64_t* selected, const ui
     }
 }
 
+// Whole pack by one warp for N = T*k <= 32 entries (lane = flat index f, so
+// lane order is the stable order): match_any groups the lanes of one expert,
+// the group's first lane writes its count, one warp scan gives the segment
+// starts, and lane f's packed row is start + its rank in the group -- the
+// same outputs as block_pack_all without its block-wide barriers.  smem:
+// hist[E], excl[E+1] ints.
+__device__ __forceinline__ void warp_pack_small(const int64_t* selected, const uint16_t* weights, int T, int k,
+                                                int E, int* hist, int* excl, const PackOut& o) {
+    const int lane = static_cast<int>(lane_id());
+    const int N = T * k;
+    for (int i = lane; i < E; i += 32) hist[i] = 0;
+    int e = -1, t = 0, pos = 0;
+    if (lane < N) {
+        t = lane % T;
+        pos = t * k + lane / T;
+        const int64_t v = selected[pos];
+        if (v < 0 || v >= E) raise_error(PDX_DEVERR_BAD_EXPERT);
+        else e = static_cast<int>(v);
+    }
+    __syncwarp();
+    const uint32_t peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    if (e >= 0 && rank == 0) hist[e] = __popc(peers);
+    __syncwarp();
+    warp_exclusive_scan(hist, E, excl, o.active, nullptr);
+    __syncwarp();
+    for (int i = lane; i < E; i += 32) {
+        o.counts[i] = hist[i];
+        o.offsets[i] = excl[i];
+    }
+    if (lane == 0) o.offsets[E] = excl[E];
+    if (e >= 0) {
+        const int p = excl[e] + rank;
+        o.tokens[p] = t;
+        o.positions[p] = pos;
+        o.packed_w[p] = weights[pos];
+        o.inverse[pos] = p;
+    }
+}
+
 // Shared memory of block_pack_all, in ints, for N = T*k entries and `warps` warps.
 __host__ __device__ constexpr size_t block_pack_smem_ints(int64_t E, int64_t N, int warps) {
     return static_cast<size_t>(E + E + 1 + warps * E + N + (N + 1) / 2);
