@@ -131,65 +131,6 @@ __device__ __forceinline__ void tmem_wait_pin(uint32_t (&r)[N]) {
     for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
 }
 
-// Columns [c0, c0 + nc) of one accumulator row (this thread's TMEM lane) ->
-// BF16 output row.  Several TMEM loads are in flight per wait.
-// swiglu: accumulator columns [0,128) hold gate, [128,256) up; output column c
-//   h = bf16(bf16(silu(bf16(g[c]))) * bf16(u[c])).
-// otherwise: y = bf16(acc) over the 256 columns.
-__device__ __forceinline__ void epilogue_cols(int swiglu, uint32_t taddr, uint16_t* orow, bool valid, int c0,
-                                              int nc) {
-    if (swiglu) {
-#pragma unroll 1
-        for (int c = c0; c < c0 + nc; c += 32) {
-            uint32_t g[32], u[32];
-            tmem_ld16(taddr + c, g);
-            tmem_ld16(taddr + c + 16, g + 16);
-            tmem_ld16(taddr + kGemmBN / 2 + c, u);
-            tmem_ld16(taddr + kGemmBN / 2 + c + 16, u + 16);
-            tmem_wait_pin(g);
-            tmem_wait_pin(u);
-            uint32_t packed[16];
-#pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-                float hv[2];
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const float gb = round_bf16(__uint_as_float(g[i + j]));
-                    const float ub = round_bf16(__uint_as_float(u[i + j]));
-                    const float sv = round_bf16(__fdiv_rn(gb, 1.0f + expf(-gb)));
-                    hv[j] = sv * ub;
-                }
-                packed[i / 2] = static_cast<uint32_t>(f2bits(hv[0])) | (static_cast<uint32_t>(f2bits(hv[1])) << 16);
-            }
-            if (valid) {
-                uint4* dst = reinterpret_cast<uint4*>(orow + c);
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
-            }
-        }
-    } else {
-#pragma unroll 1
-        for (int c = c0; c < c0 + nc; c += 64) {
-            uint32_t v[64];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) tmem_ld16(taddr + c + 16 * i, v + 16 * i);
-            tmem_wait_pin(v);
-            uint32_t packed[32];
-#pragma unroll
-            for (int i = 0; i < 64; i += 2)
-                packed[i / 2] = static_cast<uint32_t>(f2bits(__uint_as_float(v[i]))) |
-                                (static_cast<uint32_t>(f2bits(__uint_as_float(v[i + 1]))) << 16);
-            if (valid) {
-                uint4* dst = reinterpret_cast<uint4*>(orow + c);
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
-            }
-        }
-    }
-}
-
 // One 32 x 32 BF16 slab of output through this warp's shared-memory staging
 // buffer: lane r holds row r's 32 columns (packed, 16 words) and writes them
 // as four 16-byte chunks (chunk q of row r at r*64 + (q ^ ((r >> 1) & 3))*16,
@@ -273,10 +214,6 @@ __device__ __forceinline__ void epilogue_cols_staged(int swiglu, uint32_t taddr,
     }
 }
 
-// Whole accumulator row: 128 SwiGLU output columns or 256 down columns.
-__device__ __forceinline__ void epilogue_row(int swiglu, uint32_t taddr, uint16_t* orow, bool valid) {
-    epilogue_cols(swiglu, taddr, orow, valid, 0, swiglu ? kGemmBN / 2 : kGemmBN);
-}
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_grouped_gemm(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b0,
@@ -470,7 +407,8 @@ constexpr uint32_t kPairTileA = 128 * kGemmBK * 2;  // 16 KiB: this CTA's 128 ro
 constexpr uint32_t kPairTileB = 128 * kGemmBK * 2;  // 16 KiB: this CTA's half of B
 constexpr uint32_t kPairStageBytes = kPairTileA + kPairTileB;
 constexpr int kPairBM = 256;
-constexpr size_t kGemmPairSmemBytes = 1024 + kPairStages * kPairStageBytes + 256 + 4 * (kMaxActive + 1) * 4;
+constexpr size_t kGemmPairSmemBytes = 1024 + kPairStages * kPairStageBytes + 256 + 4 * (kMaxActive + 1) * 4 +
+                                      4 * kEpiStageBytes /*epilogue staging, one buffer per epilogue warp*/;
 
 __device__ __forceinline__ void pair_abort(volatile int* abort_flag, uint32_t peer_abort_addr) {
     *abort_flag = 1;
@@ -496,6 +434,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     int* t_seg0 = prefix + (kMaxActive + 1);
     int* t_rows = t_seg0 + (kMaxActive + 1);
     int* t_slot = t_rows + (kMaxActive + 1);
+    unsigned char* epi_stage = reinterpret_cast<unsigned char*>(t_slot + (kMaxActive + 1));  // [4][32 x 64 B]
 
     const int warp = static_cast<int>(threadIdx.x >> 5);
     const uint32_t lane = lane_id();
@@ -644,7 +583,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     } else {
         // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
         const int q = warp & 3;
-        const int row_in_tile = static_cast<int>(crank) * 128 + q * 32 + static_cast<int>(lane);
+        const int row0_in_tile = static_cast<int>(crank) * 128 + q * 32;   // this warp's first row
         int lt = 0;
         for (int tile = pair; tile < total_tiles; tile += n_pairs, ++lt) {
             const int b = lt & 1;
@@ -657,11 +596,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             const TileInfo ti = decode_tile(tile, prefix, n_active, n_tiles);
             const int seg0 = t_seg0[ti.a];
             const int n_e = t_rows[ti.a];
-            const int r = ti.m * kPairBM + row_in_tile;
-            const bool valid = r < n_e;
-            uint16_t* orow = args.out + static_cast<int64_t>(seg0 + r) * args.out_ld + ti.n * out_cols_per_tile;
+            const int r0 = ti.m * kPairBM + row0_in_tile;
+            uint16_t* out0 = args.out + static_cast<int64_t>(seg0 + r0) * args.out_ld + ti.n * out_cols_per_tile;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * kGemmBN);
-            epilogue_row(args.swiglu, taddr, orow, valid);
+            epilogue_cols_staged(args.swiglu, taddr, out0, args.out_ld, min(32, n_e - r0), 0,
+                                 args.swiglu ? kGemmBN / 2 : kGemmBN, epi_stage + (warp - 2) * kEpiStageBytes);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(tmem_empty0 + static_cast<uint32_t>(b) * 8u);
