@@ -69,6 +69,12 @@ def test_workspace_queries_are_monotone():
     for rows in (128, 512):
         assert lib.pdx_ffn_workspace_bytes(rows, 128, 2048, 768, 0) >= lib.pdx_ffn_workspace_bytes(rows, 128, 2048,
                                                                                                       768, 1)
+    # the decode path's query covers the single launch (both forms) and the
+    # staged form (mode 6) it may fall back to, at every rows / experts mix
+    for rows, experts in ((8, 128), (64, 128), (512, 128), (4096, 128), (300, 16), (2048, 1024)):
+        one = lib.pdx_ffn_workspace_bytes(rows, experts, 2048, 768, _lib.FFN_GEMV)
+        staged = lib.pdx_ffn_workspace_bytes(rows, experts, 2048, 768, _lib.FFN_GEMV_STAGED)
+        assert one >= staged >= rows * 768 * 2
 
 
 def test_validation_errors_without_device():
