@@ -51,6 +51,7 @@ def test_python_constants_match_header():
 
 
 def test_workspace_queries_are_monotone():
+    from pdscope_b200 import _lib
     from pdscope_b200._lib import lib
     a = lib.pdx_layer_workspace_bytes(1, 2048, 128, 8, 768, 0)
     b = lib.pdx_layer_workspace_bytes(512, 2048, 128, 8, 768, 0)
